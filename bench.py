@@ -1,0 +1,522 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Qwen3 attention hot path.
+
+Headline (one JSON line on rank 0): GQA decode-attention HBM throughput at 32k
+context -- the decode sweep workload: 28 layers with independent seeded BF16
+N(0,1) caches, 16 q heads / 8 KV heads / head_dim 128, one new token attending
+to 32769 keys per layer.  A step decodes all 28 layers in one layer-batched
+launch of the split-KV kernel (the layers are independent, so one launch does
+the same work as 28 and does not pay 28 launch latencies).  With N GPUs the
+8 KV heads are sharded (8/N per rank, no cross-rank softmax) and the head
+outputs are all-gathered over NCCL inside the step.  Metric: algorithmic KV
+bytes (4096 B per key per layer) / step time, whole job.
+
+Also reported: the same sweep as 28 per-layer launches (engine-style), the
+causal prefill attention TFLOP/s at L = 32768 (tcgen05 kernel), the end-to-end
+figure through the public Python API with host buffers, the roofline of the
+dominant kernel, the clocks seen during the timed region and the CPU oracle
+timed on the host cores.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GQA decode-attn HBM GB/s (% of peak) at 32k ctx; causal prefill attn TFLOPS"
+CTX = 32768
+N_LAYERS = 28
+NKV_TOTAL = 8
+PREFILL_L = 32768
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return float("nan")
+
+        sm = [num(r[1]) for r in rows]
+        smax = max(num(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        loaded = [s for s in sm if s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": smax, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- helpers
+def load_rib():
+    return importlib.import_module("roofline-inference_b200")
+
+
+def head_range(rank: int, world: int) -> tuple[int, int]:
+    if NKV_TOTAL % world:
+        raise SystemExit(f"--gpus must divide {NKV_TOTAL} KV heads")
+    per = NKV_TOTAL // world
+    return rank * per, (rank + 1) * per
+
+
+def make_decode_workload(rank: int, world: int, device, ctx: int = CTX, layers: int = N_LAYERS):
+    """Caches for this rank's KV heads of every layer, seeded per (layer, head)
+    so that the union over ranks is the 1-GPU workload."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    h0, h1 = head_range(rank, world)
+    nkv = h1 - h0
+    n = ctx + 1
+    cap = wl.round_cap(n)
+    caches = torch.empty((layers, 2, nkv, cap, 128), dtype=torch.bfloat16, device=device)
+    for layer in range(layers):
+        for j, h in enumerate(range(h0, h1)):
+            for kv in range(2):
+                caches[layer, kv, j, :n] = wl.randn_bf16((n, 128), seed=(layer * 64 + h) * 2 + kv,
+                                                         device=device)
+            caches[layer, :, j, n:] = 0
+    q = torch.empty((layers, 2 * nkv, 128), dtype=torch.bfloat16, device=device)
+    for layer in range(layers):
+        for j, h in enumerate(range(h0, h1)):
+            q[layer, 2 * j:2 * j + 2] = wl.randn_bf16((2, 128), seed=900000 + layer * 64 + h,
+                                                      device=device)
+    return {"caches": caches, "q": q, "n": n, "cap": cap, "nkv": nkv, "h0": h0}
+
+
+class DecodePlan:
+    """Preallocated arguments of the layer-batched decode launch (C ABI)."""
+
+    def __init__(self, rib, w, device):
+        self.L = rib.load_library()
+        self.w = w
+        layers = w["caches"].shape[0]
+        stride = w["caches"][0].numel() * 2
+        self.ptrs = torch.tensor([w["caches"].data_ptr() + i * stride for i in range(layers)],
+                                 dtype=torch.int64, device=device)
+        self.lens = torch.full((layers,), w["n"], dtype=torch.int32, device=device)
+        self.out = torch.empty_like(w["q"])
+        self.layers = layers
+        nbytes = self.L.rib_decode_workspace_bytes(layers, w["n"], w["nkv"])
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.per_layer_ws = torch.zeros(self.L.rib_decode_workspace_bytes(1, w["n"], w["nkv"]),
+                                        dtype=torch.uint8, device=device)
+        self.device = device
+        self.scale = 128 ** -0.5
+
+    def launch(self):
+        st = self.L.rib_decode_attention_batched(
+            self.w["q"].data_ptr(), self.ptrs.data_ptr(), self.lens.data_ptr(), self.layers,
+            self.w["n"], self.w["cap"], 2 * self.w["nkv"], self.w["nkv"], self.scale,
+            self.out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+            torch.cuda.current_stream(self.device).cuda_stream)
+        if st != 0:
+            raise RuntimeError(f"decode launch failed: status {st}")
+
+    def launch_layer(self, i: int):
+        w = self.w
+        st = self.L.rib_decode_attention(
+            w["q"][i].data_ptr(), w["caches"][i].data_ptr(), w["cap"], w["n"], 2 * w["nkv"],
+            w["nkv"], self.scale, self.out[i].data_ptr(), self.per_layer_ws.data_ptr(),
+            self.per_layer_ws.numel(), torch.cuda.current_stream(self.device).cuda_stream)
+        if st != 0:
+            raise RuntimeError(f"decode launch failed: status {st}")
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- CPU leg
+def cpu_decode_sample(layers_sample: int = 4, ctx: int = CTX, budget_s: float = 20.0) -> dict:
+    """Times the C oracle (all host threads) on `layers_sample` layers of the
+    decode sweep at `ctx`; value in GB/s of KV read."""
+    from oracle import oracle as coracle
+    import numpy as np
+    threads = coracle.set_threads(os.cpu_count())
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    n = ctx + 1
+    cap = wl.round_cap(n)
+    caches, qs = [], []
+    for layer in range(layers_sample):
+        c = np.zeros((2, NKV_TOTAL, cap, 128), np.uint16)
+        for h in range(NKV_TOTAL):
+            for kv in range(2):
+                t = wl.randn_bf16((n, 128), seed=(layer * 64 + h) * 2 + kv)
+                c[kv, h, :n] = t.view(torch.int16).numpy().view(np.uint16)
+        caches.append(c)
+        qq = np.concatenate([wl.randn_bf16((2, 128), seed=900000 + layer * 64 + h)
+                             .view(torch.int16).numpy().view(np.uint16) for h in range(NKV_TOTAL)])
+        qs.append(qq)
+    q = np.stack(qs)
+    coracle.decode_attention_batched(q, caches, [n] * layers_sample, 128 ** -0.5)  # warm
+    reps, t_total = 0, 0.0
+    while t_total < budget_s / 2 and reps < 50:
+        t0 = time.perf_counter()
+        coracle.decode_attention_batched(q, caches, [n] * layers_sample, 128 ** -0.5)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    bytes_per = layers_sample * 4096 * n
+    return {"value": bytes_per * reps / t_total / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{layers_sample} of {N_LAYERS} layers at ctx {ctx} (all 8 KV heads), "
+                      f"{reps} repetitions, C oracle (OpenMP FP32)",
+            "seconds": t_total}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path for this workload.  MLX (the
+    reference's attention backend) is not installable here, so the CPU oracle
+    port of its semantics is timed on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    samples = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_decode_sample(layers_sample=1, budget_s=1.0)
+    for _ in range(args.steps):
+        samples.append(cpu_decode_sample(layers_sample=2, budget_s=4.0))
+    v = statistics.median(s["value"] for s in samples)
+    n = CTX + 1
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 2 * 4096 * n / (v * 1e9) * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16/f32", "data": "synthetic",
+            "config": {"workload": f"decode sweep, ctx {CTX}, {N_LAYERS} layers, 16q/8kv/128",
+                       "sample": "2 layers per step"},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": samples[0]["cores"],
+                             "kind": "port", "sample": samples[0]["sample"]},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "MLX (the reference's attention backend) is not installable offline; "
+                    "the oracle port of its semantics runs on the host cores"}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU leg
+def run_ours(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        torch.distributed.init_process_group(
+            "nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    rib = load_rib()
+    pk = peaks()
+
+    w = make_decode_workload(rank, world, device)
+    plan = DecodePlan(rib, w, device)
+    gathered = torch.empty((world,) + tuple(plan.out.shape), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(ev_pair=None):
+        if ev_pair is not None:
+            ev_pair[0].record(stream)
+        plan.launch()
+        if ev_pair is not None:
+            ev_pair[1].record(stream)
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(gathered, plan.out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        barrier(world)
+        start.record(stream)
+        for k in range(args.steps):
+            step(ev[k])
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world, device)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    bytes_step_total = N_LAYERS * 4096 * w["n"]          # all ranks
+    bytes_launch_local = N_LAYERS * 2 * w["nkv"] * 128 * 2 * w["n"]
+    value = bytes_step_total / (ms * 1e-3) / 1e9
+    achieved = bytes_launch_local / (launch_ms * 1e-3) / 1e9
+    clk = clocks.summary()
+
+    # ---- engine-style: 28 per-layer launches of the same sweep
+    for i in range(N_LAYERS):
+        plan.launch_layer(i)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        for i in range(N_LAYERS):
+            plan.launch_layer(i)
+    b.record(stream)
+    torch.cuda.synchronize()
+    per_layer_ms = a.elapsed_time(b) / args.steps
+    per_layer_gbs = bytes_launch_local / (per_layer_ms * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers
+    e2e = run_e2e(rib, w, rank, world, device, args, gathered)
+
+    # ---- prefill (tcgen05 kernel), one GPU's view
+    prefill = run_prefill(rib, device, args, pk) if not args.no_prefill else None
+
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"decode sweep: {N_LAYERS} layers x ctx {CTX} (+1 new token), "
+                               f"16q/8kv heads, head_dim 128, independent seeded BF16 N(0,1) "
+                               f"caches",
+                   "launch": "layer-batched (one decode launch per step for all 28 layers)",
+                   "parallelism": f"kv-head shard x{world}" + (", NCCL all-gather" if world > 1
+                                                               else ""),
+                   "l2": f"inputs {bytes_step_total / 1e9:.2f} GB per step > 126 MB L2, no flush",
+                   "kv_bytes_per_step": bytes_step_total},
+        "pct_of_hbm_peak": value / pk["hbm_gbs"] / world * 100.0,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "kernel": "rib::decode::decode_kernel",
+                     "peak_source": pk["source"] + " hbm_gbs (copy, burst)",
+                     "bytes_per_launch": bytes_launch_local, "launch_ms": launch_ms},
+        "per_layer_launches": {"value": per_layer_gbs, "unit": "GB/s", "ms_per_step": per_layer_ms,
+                               "frac": per_layer_gbs / pk["hbm_gbs"]},
+        "prefill": prefill,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_decode_sample()
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(rib, w, rank, world, device, args, gathered):
+    """Same sweep through the public API: per step, copy the 28 layers' qkv
+    rows of the new token from pinned host memory, run the fused
+    norm + RoPE + append (28 launches, new token at position 32768) and one
+    layer-batched decode, and read the outputs back to pinned host memory."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    nkv, pos = w["nkv"], w["n"] - 1
+    nq = 2 * nkv
+    width = (nq + 2 * nkv) * 128
+    qkv_host = torch.empty((N_LAYERS, width), dtype=torch.bfloat16).pin_memory()
+    for layer in range(N_LAYERS):
+        qkv_host[layer] = wl.randn_bf16((width,), seed=500000 + layer * 8 + rank)
+    out_host = torch.empty((N_LAYERS, NKV_TOTAL * 2, 128), dtype=torch.bfloat16).pin_memory()
+    qw = wl.norm_weights(1, device)
+    kw = wl.norm_weights(2, device)
+    qkv_dev = torch.empty((N_LAYERS, width), dtype=torch.bfloat16, device=device)
+    lens = torch.full((N_LAYERS,), w["n"], dtype=torch.int32, device=device)
+    caches = w["caches"]
+    stream = torch.cuda.current_stream(device)
+    launches = N_LAYERS + 1
+
+    def step():
+        qkv_dev.copy_(qkv_host, non_blocking=True)
+        qs = [rib.qk_norm_rope_append(qkv_dev[i], qw, kw, pos, nq, nkv, 1e6, caches[i])
+              for i in range(N_LAYERS)]
+        q = torch.stack([x.reshape(nq, 128) for x in qs])
+        out = rib.decode_attention_batched(q, caches, lens, 128 ** -0.5, max_n=w["n"])
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(gathered, out)
+            full = gathered.permute(1, 0, 2, 3).reshape(N_LAYERS, NKV_TOTAL * 2, 128)
+        else:
+            full = out
+        out_host.copy_(full, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world, device)
+    total = N_LAYERS * 4096 * w["n"]
+    return {"value": total / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": qkv_host.numel() * 2,
+            "d2h_bytes_per_step": out_host.numel() * 2,
+            "gpu_launches_per_step": launches,
+            "path": "qk_norm_rope_append x28 + decode_attention_batched (public API)"}
+
+
+def run_prefill(rib, device, args, pk):
+    """Causal prefill attention at L = 32768 on one GPU (Q/K/V BF16 N(0,1),
+    positions 0..L-1): FLOPs 4096 * L * (L + 1) per call."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    L = PREFILL_L
+    cap = wl.round_cap(L)
+    try:
+        Q = wl.randn_bf16((16, L, 128), seed=71, device=device)
+        K = torch.zeros((1, 8, cap, 128), dtype=torch.bfloat16, device=device)
+        V = torch.zeros((1, 8, cap, 128), dtype=torch.bfloat16, device=device)
+        K[0, :, :L] = wl.randn_bf16((8, L, 128), seed=72, device=device)
+        V[0, :, :L] = wl.randn_bf16((8, L, 128), seed=73, device=device)
+        rib.attention(Q, K, V, L, L, wl.SCALE)
+    except ValueError as e:  # kernel not available in this build
+        return {"unavailable": str(e)}
+    torch.cuda.synchronize()
+    reps = max(args.steps, 3)
+    for _ in range(args.warmup):
+        rib.attention(Q, K, V, L, L, wl.SCALE)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps)]
+    stream = torch.cuda.current_stream(device)
+    for a, b in evs:
+        a.record(stream)
+        rib.attention(Q, K, V, L, L, wl.SCALE)
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    flops = wl.prefill_flops(L)
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"value": tf, "unit": "TFLOP/s", "L": L, "ms": ms, "flops": flops,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": tf / pk["bf16_tflops"],
+                         "peak_source": pk["source"] + " bf16_tflops (burst)",
+                         "kernel": "rib::prefill::prefill_kernel"}}
+
+
+def run_case(case: str):
+    """Bounded workloads for ncu captures: decode-small is the layer-batched
+    decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
+    prefill-small is causal prefill at L = 4096 (3 launches)."""
+    rib = load_rib()
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    if case == "decode-small":
+        w = make_decode_workload(0, 1, device, layers=4)
+        plan = DecodePlan(rib, w, device)
+        for _ in range(3):
+            plan.launch()
+    else:
+        L = 4096
+        Q = wl.randn_bf16((16, L, 128), seed=71, device=device)
+        K = wl.randn_bf16((1, 8, L, 128), seed=72, device=device)
+        V = wl.randn_bf16((1, 8, L, 128), seed=73, device=device)
+        for _ in range(3):
+            rib.attention(Q, K, V, L, L, wl.SCALE)
+    torch.cuda.synchronize()
+    print(f"case {case} done")
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--case", choices=["decode-small", "prefill-small"], default=None,
+                    help="run a bounded case for profiling (ncu) and exit")
+    args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
+    if args.warmup < 3 and args.impl == "ours":
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+/*
+ * rib_attention.h -- C ABI of the B200 (sm_100a) Qwen3 attention hot path.
+ *
+ * The reference (aeilot/roofline-inference, agent-test/v2) runs this path as
+ * Metal kernels compiled by MLX plus one MLX library call.  Each entry point
+ * below replaces one of those interfaces; the citation names the reference
+ * function whose arguments and results it keeps.
+ *
+ * Conventions (all entry points):
+ *   - Pointers are DEVICE pointers unless the name ends in `_host`.  Tensors
+ *     are BF16 stored as uint16 bit patterns, row-major and contiguous in the
+ *     layout stated per argument.  The caller owns every buffer; the library
+ *     never allocates or frees on these paths and keeps no per-call state.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
+ *     only enqueues work and returns; none synchronises.
+ *   - Return value: RIB_OK (0) or one of the RIB_E* codes below.  Argument
+ *     checks run on the host before anything is launched, so an error return
+ *     means nothing was enqueued.
+ *   - head_dim is 128 and the GQA group is 2 (n_q_heads == 2 * n_kv_heads),
+ *     the same preconditions as the reference engine
+ *     (agent-test/v2/engine.py:69-70, agent-test/v2/attention.py:181).
+ */
+#ifndef RIB_ATTENTION_H
+#define RIB_ATTENTION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The Python layer maps 1-3 to ValueError and 4-5 to
+ * RuntimeError, matching the reference's ValueError on shape/capacity errors
+ * (agent-test/v2/engine.py:45-46, 69-70). */
+#define RIB_OK 0
+#define RIB_EINVAL 1    /* bad shape / argument                         */
+#define RIB_ECAPACITY 2 /* "KV capacity exceeded" (engine.py:45-46)     */
+#define RIB_EALIGN 3    /* pointer not 16-byte aligned                  */
+#define RIB_ECUDA 4     /* a CUDA runtime call failed                   */
+#define RIB_ETIMEOUT 5  /* a device-side wait gave up (bounded spin)    */
+
+/* Library version, (major << 16) | minor. */
+int rib_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char *rib_status_string(int status);
+
+/* Reads and clears the device-side status word of the current device: 0 if
+ * no kernel recorded a timeout since the last call, RIB_ETIMEOUT otherwise.
+ * Synchronises the current device. */
+int rib_take_device_status(int *status_host);
+
+/* ------------------------------------------------------------------------ *
+ * Fused per-head RMSNorm + RoPE, one token (decode).
+ * Replaces qk_norm_rope(qkv, qw, kw, pos, nq, nkv, base)
+ *   (agent-test/v2/kernels.py:157-164, Metal source kernels.py:116-146).
+ *   qkv    [(nq + 2*nkv) * 128]   q heads, then k heads, then v heads
+ *   qw, kw [128]                  RMSNorm weights for q and k
+ *   pos                           RoPE position (the reference passes it as a
+ *                                 1-element int32 array; here by value)
+ *   q_out  [nq, 128]              == the reference's q [1, nq, 1, 128]
+ *   kv_out [2, nkv, 128]          == the reference's kv [2, nkv, 1, 128]
+ * RMSNorm eps is 1e-6; rounding points n = bf16(w * bf16(x * inv)); RoPE is
+ * the non-traditional form pairing (d, d+64) with theta = pos * base^(-d/64).
+ * V is copied bit for bit.
+ * ------------------------------------------------------------------------ */
+int rib_qk_norm_rope(const void *qkv, const void *qw, const void *kw, int pos,
+                     int nq, int nkv, double base, void *q_out, void *kv_out,
+                     void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * Fused RMSNorm + RoPE for L tokens at positions offset .. offset+L-1.
+ * Replaces qk_norm_rope_prefill(qkv, qw, kw, offset, nq, nkv, base, Lp)
+ *   (agent-test/v2/kernels.py:215-224, Metal source kernels.py:169-204).
+ *   qkv    [L, (nq + 2*nkv) * 128]
+ *   q_out  [nq, Lp, 128]   rows L..Lp-1 are written as zeros (the reference
+ *                          launches with init_value=0, kernels.py:223)
+ *   kv_out [2, nkv, L, 128]
+ * Requires Lp >= L.
+ * ------------------------------------------------------------------------ */
+int rib_qk_norm_rope_prefill(const void *qkv, int L, const void *qw,
+                             const void *kw, int offset, int nq, int nkv,
+                             double base, int Lp, void *q_out, void *kv_out,
+                             void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * The same kernel with the KV-cache write fused in: K (normed + roped) and V
+ * go straight to rows offset .. offset+L-1 of one layer's cache.
+ * Replaces the pair qk_norm_rope[_prefill] (kernels.py:157/215) followed by
+ * Cache.update (agent-test/v2/engine.py:42-48), called at engine.py:111-113
+ * and engine.py:152-153.
+ *   cache  [2, nkv, cap, 128]   one layer of Cache.kv (engine.py:38)
+ *   q_out  [nq, Lp, 128]        (Lp == 1 for a decode token)
+ * Returns RIB_ECAPACITY if offset + L > cap, as Cache.update raises
+ * ValueError("KV capacity exceeded") (engine.py:45-46).
+ * ------------------------------------------------------------------------ */
+int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw,
+                            const void *kw, int offset, int nq, int nkv,
+                            double base, int Lp, void *q_out, void *cache,
+                            int cap, void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * GQA decode attention: one query token per sequence against n cached keys.
+ * Replaces mx.fast.scaled_dot_product_attention(q, K, V, scale) as called by
+ * Engine.decode (agent-test/v2/engine.py:154-155), where K, V are the views
+ * cache.views(i, n) == buf[0:1, :, :n], buf[1:2, :, :n] (engine.py:50-52).
+ *   q      [nq, 128]             post-RoPE query (the reference's [1,nq,1,128])
+ *   cache  [2, nkv, cap, 128]    one layer of the KV cache
+ *   n      number of valid keys (offset + 1 in Engine.decode, engine.py:149)
+ *   out    [nq, 128]             == [1, nq, 1, 128], o_proj input layout
+ *   workspace / workspace_bytes  device scratch of at least
+ *          rib_decode_workspace_bytes(1, n, nkv) bytes.  Its first
+ *          4 * nkv bytes are counters that must be zero before the first
+ *          call; every call leaves them zero again.  Calls that share a
+ *          workspace must not overlap on the device.
+ * Softmax and accumulation in FP32; output rounded to BF16 once.
+ * ------------------------------------------------------------------------ */
+size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv);
+
+int rib_decode_attention(const void *q, const void *cache, int cap, int n,
+                         int nq, int nkv, float scale, void *out,
+                         void *workspace, size_t workspace_bytes,
+                         void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * Batched ragged decode: B independent sequences, each with its own
+ * contiguous per-sequence cache and its own length.  Generalises the
+ * single-sequence call above (the reference is batch 1 only, README.md
+ * "Single stream"; engine.py:33-40 is the per-sequence cache it generalises).
+ *   q          [B, nq, 128]
+ *   cache_ptrs device array of B pointers, each to a [2, nkv, cap, 128] cache
+ *   lens       device array of B int32 key counts (1 <= lens[b] <= cap)
+ *   max_n      host upper bound on lens[] (sizes the launch)
+ *   out        [B, nq, 128]
+ *   workspace  at least rib_decode_workspace_bytes(B, max_n, nkv) bytes,
+ *              same zero-counter contract as above.
+ * ------------------------------------------------------------------------ */
+int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs,
+                                 const int32_t *lens, int batch, int max_n,
+                                 int cap, int nq, int nkv, float scale,
+                                 void *out, void *workspace,
+                                 size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * Causal GQA prefill attention (tcgen05 / TMEM flash attention).
+ * Replaces attention(Q, K, V, qL, kL, scale, ...) (agent-test/v2/attention.py
+ * :177-185, Metal source attention.py:18-166).
+ *   Q      [H, qLp, 128]         post-RoPE queries; rows >= qL are ignored
+ *   K, V   [nkv, cap, 128]       the K and V halves of one cache layer
+ *                                (the reference passes buf[0:1], buf[1:2])
+ *   O      [qL, H * 128]         o_proj input layout (attention.py:10)
+ * Causal mask is bottom-right aligned: query i sees keys <= kL - qL + i
+ * (attention.py:24, 111).  Requires H == 2 * nkv, qL <= qLp, qL <= kL <= cap.
+ * ------------------------------------------------------------------------ */
+int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL,
+                          int kL, int qLp, int cap, int H, int nkv,
+                          float scale, void *O, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RIB_ATTENTION_H */

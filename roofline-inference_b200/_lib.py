@@ -1,0 +1,138 @@
+"""Loader of the C-ABI library librib_attention.so (CUDA kernels for sm_100a).
+
+The library is built in-tree from csrc/ with nvcc.  `load()` rebuilds it when
+the sources changed (content hash, not mtimes, so a copied tree is judged
+correctly) and then binds the entry points declared in
+include/rib_attention.h with ctypes.  There is no fallback: if the library
+cannot be built or loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import fcntl
+import hashlib
+import os
+import shutil
+import subprocess
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+REPO_DIR = PKG_DIR.parent
+CSRC = PKG_DIR / "csrc"
+HEADER = REPO_DIR / "include" / "rib_attention.h"
+LIB_PATH = PKG_DIR / "librib_attention.so"
+STAMP = PKG_DIR / "librib_attention.so.srchash"
+MAIN_SOURCE = CSRC / "rib_attention.cu"
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-shared",
+]
+
+# status codes (include/rib_attention.h)
+RIB_OK, RIB_EINVAL, RIB_ECAPACITY, RIB_EALIGN, RIB_ECUDA, RIB_ETIMEOUT = range(6)
+
+_lib: ctypes.CDLL | None = None
+
+
+def _sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HEADER]
+
+
+def source_hash() -> str:
+    h = hashlib.sha256()
+    for p in _sources():
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(" ".join(NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
+def is_current() -> bool:
+    return LIB_PATH.exists() and STAMP.exists() and STAMP.read_text().strip() == source_hash()
+
+
+def _nvcc() -> str:
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: cannot build librib_attention.so")
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles csrc/rib_attention.cu for sm_100a into librib_attention.so.
+
+    Serialised with a file lock so that several ranks importing the package at
+    once build it only once."""
+    if not force and is_current():
+        return LIB_PATH
+    lock_path = PKG_DIR / ".librib_attention.lock"
+    with open(lock_path, "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and is_current():
+                return LIB_PATH
+            tmp = LIB_PATH.with_name(f"{LIB_PATH.name}.{os.getpid()}.tmp")
+            cmd = [_nvcc(), *NVCC_FLAGS, "-o", str(tmp), str(MAIN_SOURCE)]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            res = subprocess.run(cmd, capture_output=True, text=True)
+            if res.returncode != 0:
+                raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+            if verbose:
+                print(res.stdout + res.stderr)
+            tmp.replace(LIB_PATH)
+            STAMP.write_text(source_hash() + "\n")
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+    return LIB_PATH
+
+
+def _bind(L: ctypes.CDLL) -> None:
+    vp, i, d, f, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_double, ctypes.c_float, ctypes.c_size_t
+    sig = {
+        "rib_version": ([], i),
+        "rib_status_string": ([i], ctypes.c_char_p),
+        "rib_take_device_status": ([ctypes.POINTER(ctypes.c_int)], i),
+        "rib_qk_norm_rope": ([vp, vp, vp, i, i, i, d, vp, vp, vp], i),
+        "rib_qk_norm_rope_prefill": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, vp], i),
+        "rib_qk_norm_rope_append": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, i, vp], i),
+        "rib_decode_workspace_bytes": ([i, i, i], sz),
+        "rib_decode_attention": ([vp, vp, i, i, i, i, f, vp, vp, sz, vp], i),
+        "rib_decode_attention_batched": ([vp, vp, vp, i, i, i, i, i, f, vp, vp, sz, vp], i),
+        "rib_prefill_attention": ([vp, vp, vp, i, i, i, i, i, i, f, vp, vp], i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+
+
+def load() -> ctypes.CDLL:
+    """Builds if needed, loads and binds the library (once per process)."""
+    global _lib
+    if _lib is None:
+        path = build()
+        L = ctypes.CDLL(str(path))
+        _bind(L)
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    """Raises like the reference: ValueError for shape/capacity/alignment
+    problems (agent-test/v2/engine.py:45-46, 69-70), RuntimeError otherwise."""
+    if status == RIB_OK:
+        return
+    msg = load().rib_status_string(status).decode()
+    if status in (RIB_EINVAL, RIB_ECAPACITY, RIB_EALIGN):
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg} (status {status})")
+
+
+def take_device_status() -> int:
+    """Reads and clears the device status word (synchronises the device)."""
+    v = ctypes.c_int(0)
+    check(load().rib_take_device_status(ctypes.byref(v)), "rib_take_device_status")
+    return v.value

@@ -1,0 +1,353 @@
+// GQA split-KV decode attention (flash-decoding) for sm_100a.
+//
+// Replaces the MLX library call mx.fast.scaled_dot_product_attention(q, K, V,
+// scale) made by Engine.decode (agent-test/v2/engine.py:154-155): one query
+// token per sequence, q heads 2h and 2h+1 read KV head h (GQA group 2), no
+// mask, n = offset + 1 keys (engine.py:149).
+//
+// Work split: CTA (split, kv_head, seq) streams keys [split*chunk,
+// min(n, (split+1)*chunk)) of one KV head for both of its query heads.
+//   - warp NCW (producer): one lane issues 1-D bulk copies (cp.async.bulk) of
+//     K and V tiles of TK keys into a STAGES-deep shared-memory ring; each
+//     tile of one head is a contiguous TK*256-byte run of the cache, so no
+//     tensor map is needed.  L2 policy evict_first: the cache is read once.
+//   - warps 0-2 (consumers) take tiles round-robin (tile t -> warp t % NCW)
+//     and each warp owns SPW ring slots of its own, so a warp waits on the
+//     next phase of a slot only after it consumed the previous one itself
+//     (a slot shared between warps could be waited on one phase early, and
+//     an mbarrier parity wait cannot tell phase k from phase k + 2).
+//     Scores: an 8-lane group
+//     owns 8 keys, lane j of the group holds dims [8j,8j+8) and [64+8j,64+8j+8)
+//     (two 16-byte conflict-free shared loads per key), a 3-step butterfly
+//     reduce-scatter leaves lane l with the full score of key l for both
+//     heads.  Online softmax in the exp2 domain (q pre-scaled by
+//     scale*log2 e), warp-uniform running max.  P.V: lane l owns dims
+//     [4l, 4l+4) and accumulates all keys of the tile for both heads in FP32.
+//   - The CTA merges its consumer warps in shared memory.  With one split the CTA
+//     writes the BF16 output; otherwise it writes an FP32 partial (m, l, o),
+//     and the last CTA of its (seq, kv_head) to arrive (threadfence +
+//     atomic counter) merges all splits and resets the counter to zero.
+#pragma once
+
+#include "common.cuh"
+
+namespace rib {
+namespace decode {
+
+constexpr int D = 128;
+constexpr int TK = 32;                 // keys per pipeline tile
+constexpr int NCW = 3;                 // consumer warps
+constexpr int SPW = 2;                 // ring slots owned by each consumer warp
+constexpr int STAGES = NCW * SPW;      // ring depth
+constexpr int NTHREADS = (NCW + 1) * 32;
+constexpr int ROW_BYTES = D * 2;       // one key row, BF16
+constexpr int TILE_BYTES = TK * ROW_BYTES;
+
+struct Smem {
+  alignas(128) uint8_t k[STAGES][TILE_BYTES];
+  alignas(128) uint8_t v[STAGES][TILE_BYTES];
+  alignas(16) float p[NCW][2][TK];
+  alignas(16) float red_o[NCW][2][D];
+  float red_m[NCW][2];
+  float red_l[NCW][2];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  int is_last;
+};
+
+struct Params {
+  const uint16_t *q;           // [B][nq][128]
+  const uint64_t *cache_ptrs;  // [B] device pointers, or null (single cache)
+  const uint16_t *cache;       // single [2][nkv][cap][128] cache
+  const int32_t *lens;         // [B] device key counts, or null
+  int n_single;                // key count when lens == null
+  int max_n;                   // host bound on key counts (sizes the grid)
+  int cap, nq, nkv;
+  int chunk;                   // keys per split, multiple of TK
+  int max_splits;
+  float qscale;                // scale * log2(e)
+  uint16_t *out;               // [B][nq][128]
+  float *part_ml;              // [B][nkv][max_splits][2][2]  (m, l)
+  float *part_o;               // [B][nkv][max_splits][2][128]
+  int *counters;               // [B][nkv]
+};
+
+__device__ __forceinline__ void unpack8(const uint4 &r, float *f) {
+  f[0] = bf16lo(r.x); f[1] = bf16hi(r.x);
+  f[2] = bf16lo(r.y); f[3] = bf16hi(r.y);
+  f[4] = bf16lo(r.z); f[5] = bf16hi(r.z);
+  f[6] = bf16lo(r.w); f[7] = bf16hi(r.w);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int n = p.lens ? p.lens[b] : p.n_single;
+  if (n < 1 || n > p.cap || n > p.max_n) {  // bad device-side length: record, write nothing
+    if (threadIdx.x == 0 && split == 0) atomicExch(&g_device_status, RIB_EINVAL);
+    return;
+  }
+  const int nsplit = (n + p.chunk - 1) / p.chunk;
+  if (split >= nsplit) return;  // whole CTA: this sequence needs fewer splits
+  const int k_begin = split * p.chunk;
+  const int k_end = min(n, k_begin + p.chunk);
+  const int ntiles = (k_end - k_begin + TK - 1) / TK;
+  const uint16_t *cache = p.cache_ptrs ? reinterpret_cast<const uint16_t *>(p.cache_ptrs[b]) : p.cache;
+  if (reinterpret_cast<uintptr_t>(cache) & 15u) {  // bulk copies need 16-byte alignment
+    if (threadIdx.x == 0 && split == 0) atomicExch(&g_device_status, RIB_EALIGN);
+    return;
+  }
+  const uint16_t *Kh = cache + static_cast<size_t>(h) * p.cap * D;
+  const uint16_t *Vh = cache + static_cast<size_t>(p.nkv + h) * p.cap * D;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+
+  if (warp == NCW) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int t = 0; t < ntiles; ++t) {
+        const int k = t / NCW;  // k-th tile of consumer warp t % NCW
+        const int slot = (t % NCW) * SPW + k % SPW;
+        if (k >= SPW && !mbar_wait(&s.empty[slot], ((k / SPW) - 1) & 1)) break;
+        const int k0 = k_begin + t * TK;
+        const uint32_t bytes = static_cast<uint32_t>(min(TK, k_end - k0)) * ROW_BYTES;
+        mbar_arrive_expect_tx(&s.full[slot], 2 * bytes);
+        bulk_g2s(s.k[slot], Kh + static_cast<size_t>(k0) * D, bytes, &s.full[slot], pol);
+        bulk_g2s(s.v[slot], Vh + static_cast<size_t>(k0) * D, bytes, &s.full[slot], pol);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int g = lane >> 3, j = lane & 7;
+    // q for both heads, dims [8j, 8j+8) and [64+8j, 64+8j+8), pre-scaled.
+    float qa[2][16];
+    {
+      const uint16_t *qb = p.q + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint4 r0 = *reinterpret_cast<const uint4 *>(qb + hh * D + 8 * j);
+        const uint4 r1 = *reinterpret_cast<const uint4 *>(qb + hh * D + 64 + 8 * j);
+        unpack8(r0, &qa[hh][0]);
+        unpack8(r1, &qa[hh][8]);
+#pragma unroll
+        for (int d = 0; d < 16; ++d) qa[hh][d] *= p.qscale;
+      }
+    }
+    for (int t = warp, k = 0; t < ntiles; t += NCW, ++k) {
+      const int slot = warp * SPW + k % SPW;
+      if (!mbar_wait(&s.full[slot], (k / SPW) & 1)) break;
+      const int k0 = k_begin + t * TK;
+      const int rows = min(TK, k_end - k0);
+      const uint8_t *Kt = s.k[slot];
+      const uint8_t *Vt = s.v[slot];
+
+      // ---- scores: group g handles keys g*8 .. g*8+7 of the tile
+      float s0[8], s1[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint8_t *row = Kt + (g * 8 + i) * ROW_BYTES;
+        float kf[16];
+        unpack8(*reinterpret_cast<const uint4 *>(row + 16 * j), &kf[0]);
+        unpack8(*reinterpret_cast<const uint4 *>(row + 128 + 16 * j), &kf[8]);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int d = 0; d < 16; ++d) {
+          a0 = fmaf(qa[0][d], kf[d], a0);
+          a1 = fmaf(qa[1][d], kf[d], a1);
+        }
+        s0[i] = a0;
+        s1[i] = a1;
+      }
+      // ---- butterfly reduce-scatter over the 8 lanes of the group
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const bool up = j & 4;
+        const float snd0 = up ? s0[r] : s0[r + 4], kp0 = up ? s0[r + 4] : s0[r];
+        const float snd1 = up ? s1[r] : s1[r + 4], kp1 = up ? s1[r + 4] : s1[r];
+        s0[r] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 4);
+        s1[r] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 4);
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const bool up = j & 2;
+        const float snd0 = up ? s0[r] : s0[r + 2], kp0 = up ? s0[r + 2] : s0[r];
+        const float snd1 = up ? s1[r] : s1[r + 2], kp1 = up ? s1[r + 2] : s1[r];
+        s0[r] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 2);
+        s1[r] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 2);
+      }
+      {
+        const bool up = j & 1;
+        const float snd0 = up ? s0[0] : s0[1], kp0 = up ? s0[1] : s0[0];
+        const float snd1 = up ? s1[0] : s1[1], kp1 = up ? s1[1] : s1[0];
+        s0[0] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 1);
+        s1[0] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 1);
+      }
+      // lane l now holds the scores of key l of the tile
+      float sc0 = lane < rows ? s0[0] : -INFINITY;
+      float sc1 = lane < rows ? s1[0] : -INFINITY;
+      float mt0 = sc0, mt1 = sc1;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+        mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+      }
+      const float mn0 = fmaxf(m_run[0], mt0), mn1 = fmaxf(m_run[1], mt1);
+      const float al0 = fast_exp2(m_run[0] - mn0), al1 = fast_exp2(m_run[1] - mn1);
+      m_run[0] = mn0;
+      m_run[1] = mn1;
+      const float p0 = fast_exp2(sc0 - mn0), p1 = fast_exp2(sc1 - mn1);
+      l_run[0] = l_run[0] * al0 + p0;
+      l_run[1] = l_run[1] * al1 + p1;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        o[0][e] *= al0;
+        o[1][e] *= al1;
+      }
+      s.p[warp][0][lane] = p0;
+      s.p[warp][1][lane] = p1;
+      __syncwarp();
+
+      // ---- P.V: lane owns dims [4*lane, 4*lane+4)
+      int kk = 0;
+      for (; kk + 4 <= rows; kk += 4) {
+        const float4 pa = *reinterpret_cast<const float4 *>(&s.p[warp][0][kk]);
+        const float4 pb = *reinterpret_cast<const float4 *>(&s.p[warp][1][kk]);
+        const float pa_[4] = {pa.x, pa.y, pa.z, pa.w};
+        const float pb_[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint2 vr = *reinterpret_cast<const uint2 *>(Vt + (kk + u) * ROW_BYTES + 8 * lane);
+          const float v0 = bf16lo(vr.x), v1 = bf16hi(vr.x), v2 = bf16lo(vr.y), v3 = bf16hi(vr.y);
+          o[0][0] = fmaf(pa_[u], v0, o[0][0]);
+          o[0][1] = fmaf(pa_[u], v1, o[0][1]);
+          o[0][2] = fmaf(pa_[u], v2, o[0][2]);
+          o[0][3] = fmaf(pa_[u], v3, o[0][3]);
+          o[1][0] = fmaf(pb_[u], v0, o[1][0]);
+          o[1][1] = fmaf(pb_[u], v1, o[1][1]);
+          o[1][2] = fmaf(pb_[u], v2, o[1][2]);
+          o[1][3] = fmaf(pb_[u], v3, o[1][3]);
+        }
+      }
+      for (; kk < rows; ++kk) {
+        const float pa = s.p[warp][0][kk], pb = s.p[warp][1][kk];
+        const uint2 vr = *reinterpret_cast<const uint2 *>(Vt + kk * ROW_BYTES + 8 * lane);
+        const float v0 = bf16lo(vr.x), v1 = bf16hi(vr.x), v2 = bf16lo(vr.y), v3 = bf16hi(vr.y);
+        o[0][0] = fmaf(pa, v0, o[0][0]);
+        o[0][1] = fmaf(pa, v1, o[0][1]);
+        o[0][2] = fmaf(pa, v2, o[0][2]);
+        o[0][3] = fmaf(pa, v3, o[0][3]);
+        o[1][0] = fmaf(pb, v0, o[1][0]);
+        o[1][1] = fmaf(pb, v1, o[1][1]);
+        o[1][2] = fmaf(pb, v2, o[1][2]);
+        o[1][3] = fmaf(pb, v3, o[1][3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.empty[slot]);
+    }
+    // ---- publish this warp's state
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float l = l_run[hh];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+      if (lane == 0) {
+        s.red_m[warp][hh] = m_run[hh];
+        s.red_l[warp][hh] = l;
+      }
+      *reinterpret_cast<float4 *>(&s.red_o[warp][hh][4 * lane]) =
+          make_float4(o[hh][0], o[hh][1], o[hh][2], o[hh][3]);
+    }
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ CTA merge
+  // threads 0..127: dim d = tid, both heads.
+  float Mx[2] = {-INFINITY, -INFINITY}, Lx[2] = {0.f, 0.f}, Ox[2] = {0.f, 0.f};
+  if (tid < D) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) M = fmaxf(M, s.red_m[w][hh]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < NCW; ++w) {
+        const float mw = s.red_m[w][hh];
+        const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - M);
+        L = fmaf(s.red_l[w][hh], f, L);
+        O = fmaf(s.red_o[w][hh][tid], f, O);
+      }
+      Mx[hh] = M;
+      Lx[hh] = L;
+      Ox[hh] = O;
+    }
+  }
+  uint16_t *outp = p.out + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
+  if (nsplit == 1) {
+    if (tid < D) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        outp[hh * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(Ox[hh] / Lx[hh]));
+    }
+    return;
+  }
+  const size_t unit = static_cast<size_t>(b) * p.nkv + h;
+  if (tid < D) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const size_t pi = (unit * p.max_splits + split) * 2 + hh;
+      p.part_o[pi * D + tid] = Ox[hh];
+      if (tid == 0) {
+        p.part_ml[pi * 2 + 0] = Mx[hh];
+        p.part_ml[pi * 2 + 1] = Lx[hh];
+      }
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int prev = atomicAdd(&p.counters[unit], 1);
+    s.is_last = (prev == nsplit - 1);
+  }
+  __syncthreads();
+  if (!s.is_last) return;
+  __threadfence();
+  if (tid < D) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float M = -INFINITY;
+      for (int sp = 0; sp < nsplit; ++sp)
+        M = fmaxf(M, __ldcg(&p.part_ml[((unit * p.max_splits + sp) * 2 + hh) * 2]));
+      float L = 0.f, O = 0.f;
+      for (int sp = 0; sp < nsplit; ++sp) {
+        const size_t pi = (unit * p.max_splits + sp) * 2 + hh;
+        const float f = fast_exp2(__ldcg(&p.part_ml[pi * 2]) - M);
+        L = fmaf(__ldcg(&p.part_ml[pi * 2 + 1]), f, L);
+        O = fmaf(__ldcg(&p.part_o[pi * D + tid]), f, O);
+      }
+      outp[hh * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(O / L));
+    }
+  }
+  if (tid == 0) p.counters[unit] = 0;  // leave the workspace ready for the next call
+}
+
+}  // namespace decode
+}  // namespace rib

@@ -1,0 +1,406 @@
+// Causal GQA flash attention for prefill on sm_100a: tcgen05.mma with TMEM
+// accumulators, operands staged by TMA.
+//
+// Replaces the Metal kernel attention() of agent-test/v2/attention.py:18-185:
+// same layouts (Q [H, qLp, 128], K/V cache halves [nkv, cap, 128], O
+// [qL, H*128]), GQA pairing (both query heads of a KV head in one CTA,
+// attention.py:3-5), bottom-right aligned causal mask (query i sees keys
+// <= kL - qL + i, attention.py:24,111), online softmax in the exp2 domain
+// (attention.py:59), whole masked key tiles skipped (attention.py:87) and
+// heavy query blocks scheduled first (attention.py:26).
+//
+// CTA = 128 query rows x one KV head g (query heads 2g, 2g+1), 10 warps:
+//   warp 0      TMA producer: Q of both heads once, then K and V tiles of
+//               128 keys into a 2-stage ring (128B-swizzled panels).
+//   warp 1      TMEM owner and MMA issuer (one thread):
+//                 S_h = Q_h K^T       SS-MMA, M=N=128, K=128 (8 x K16)
+//                 O_h += P_h V        TS-MMA, A = P_h from TMEM, B = V (MN-major)
+//               issue order PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), so the tensor
+//               pipe works on one head while the other head's softmax runs.
+//   warps 2-5   softmax of head 2g   (one thread per query row / TMEM lane)
+//   warps 6-9   softmax of head 2g+1
+// TMEM (512 columns): S_0 [0,128), S_1 [128,256) as FP32; P_h is written as
+// packed BF16 over the first 64 columns of S_h; O_0 [256,384), O_1 [384,512).
+// The running max is only raised (and O rescaled) when it grows by more
+// than 8 in log2 units; until then exp2 arguments stay below 8 and P below
+// 256, which BF16 and the FP32 accumulators carry exactly enough.
+// Every wait is bounded (common.cuh); on a timeout the CTA sets a flag,
+// drains, frees TMEM and returns.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace rib {
+namespace prefill {
+
+constexpr int D = 128;
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // keys per tile
+constexpr int NS = 2;    // K/V pipeline stages
+constexpr int NWARPS = 10;
+constexpr int NTHREADS = NWARPS * 32;
+constexpr int PANEL_BYTES = 128 * 128;          // [128 rows][64 dims] BF16, one swizzle panel
+constexpr int TILE_BYTES = 2 * PANEL_BYTES;     // [128 rows][128 dims]
+constexpr uint32_t TMEM_COLS = 512;
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
+
+// Instruction descriptor, kind::f16: D = F32 (bits 4-5 = 1), A = B = BF16
+// (bits 7-9, 10-12 = 1), N >> 3 at bits 17-22, M >> 4 at bits 24-28;
+// bit 16 = B is MN-major.
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) |
+                                (static_cast<uint32_t>(BN >> 3) << 17) |
+                                (static_cast<uint32_t>(BM >> 4) << 24);
+constexpr uint32_t kIdescS = kIdescBase;              // A, B K-major
+constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);  // B (= V) MN-major
+
+struct Smem {
+  alignas(1024) uint8_t q[2][TILE_BYTES];
+  alignas(1024) uint8_t k[NS][TILE_BYTES];
+  alignas(1024) uint8_t v[NS][TILE_BYTES];
+  uint64_t q_full;
+  uint64_t k_full[NS], v_full[NS], kv_empty[NS];
+  uint64_t s_full[2], p_full[2], o_full[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Params {
+  CUtensorMap tm_q;  // (128, qLp, H)   box (64, 128, 1), 128B swizzle
+  CUtensorMap tm_k;  // (128, kL, nkv)  row stride 256 B, head stride cap*256 B
+  CUtensorMap tm_v;
+  uint16_t *out;     // [qL][H*128]
+  int qL, kL, H, nkv, off, nqb;
+  float scale_log2;
+};
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2 at bits
+// 61-63), sm100 version bit 46; address, LBO and SBO in 16-byte units.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ bool aborted(const Smem &s) {
+  return *reinterpret_cast<const volatile int *>(&s.abort_flag) != 0;
+}
+__device__ __forceinline__ void set_abort(Smem &s) {
+  *reinterpret_cast<volatile int *>(&s.abort_flag) = 1;
+}
+
+// Warp-uniform bounded wait: every lane waits, then all agree.
+__device__ __forceinline__ bool warp_wait(Smem &s, uint64_t *bar, uint32_t parity) {
+  bool ok = !aborted(s) && mbar_wait(bar, parity);
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) set_abort(s);
+  return ok;
+}
+
+__global__ void __maxnreg__(200) prefill_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int qb = p.nqb - 1 - static_cast<int>(blockIdx.x) / p.nkv;  // heavy blocks first
+  const int g = static_cast<int>(blockIdx.x) % p.nkv;
+  const int q0 = qb * BM;
+  const int q_last = min(q0 + BM - 1, p.qL - 1);
+  const int last_key = min(p.kL - 1, p.off + q_last);
+  const int nt = last_key / BN + 1;  // key tiles this CTA visits
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.v_full[i], 1);
+      mbar_init(&s.kv_empty[i], 1);
+    }
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&s.s_full[h], 1);
+      mbar_init(&s.p_full[h], 128);
+      mbar_init(&s.o_full[h], 1);
+    }
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tm_q);
+    prefetch_tmap(&p.tm_k);
+    prefetch_tmap(&p.tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&s.q_full, 2 * TILE_BYTES);
+      for (int h = 0; h < 2; ++h)
+        for (int c = 0; c < 2; ++c)
+          tma_load_3d(s.q[h] + c * PANEL_BYTES, &p.tm_q, c * 64, q0, 2 * g + h, &s.q_full);
+      int issued = 0;
+      for (int t = 0; t < nt; ++t) {
+        const int st = t % NS;
+        if (t >= NS && (aborted(s) || !mbar_wait(&s.kv_empty[st], ((t / NS) - 1) & 1))) {
+          set_abort(s);
+          break;
+        }
+        mbar_arrive_expect_tx(&s.k_full[st], TILE_BYTES);
+        for (int c = 0; c < 2; ++c)
+          tma_load_3d(s.k[st] + c * PANEL_BYTES, &p.tm_k, c * 64, t * BN, g, &s.k_full[st]);
+        mbar_arrive_expect_tx(&s.v_full[st], TILE_BYTES);
+        for (int c = 0; c < 2; ++c)
+          tma_load_3d(s.v[st] + c * PANEL_BYTES, &p.tm_v, c * 64, t * BN, g, &s.v_full[st]);
+        issued = t + 1;
+      }
+      // drain: every copy issued must land before the CTA may exit
+      mbar_wait(&s.q_full, 0);
+      for (int t = max(0, issued - NS); t < issued; ++t) {
+        mbar_wait(&s.k_full[t % NS], (t / NS) & 1);
+        mbar_wait(&s.v_full[t % NS], (t / NS) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      auto issue_s = [&](int h, int st) {
+        const uint32_t qa = smem_u32(s.q[h]), kb = smem_u32(s.k[st]);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k >> 2) * PANEL_BYTES + (k & 3) * 32;
+          tc_mma_ss(tmem + h * 128, sw128_desc(qa + off, 16, 1024), sw128_desc(kb + off, 16, 1024),
+                    kIdescS, k > 0);
+        }
+      };
+      auto issue_pv = [&](int h, int st, bool first) {
+        const uint32_t vb = smem_u32(s.v[st]);
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          tc_mma_ts(tmem + 256 + h * 128, tmem + h * 128 + k * 8,
+                    sw128_desc(vb + k * 2048, PANEL_BYTES, 1024), kIdescPV, (!first || k > 0));
+      };
+      bool ok = mbar_wait(&s.q_full, 0) && mbar_wait(&s.k_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        tc_commit(&s.s_full[0]);
+        issue_s(1, 0);
+        tc_commit(&s.s_full[1]);
+      }
+      for (int j = 0; ok && j < nt; ++j) {
+        const int st = j % NS, st1 = (j + 1) % NS;
+        ok = !aborted(s) && mbar_wait(&s.v_full[st], (j / NS) & 1) &&
+             mbar_wait(&s.p_full[0], j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(0, st, j == 0);
+        tc_commit(&s.o_full[0]);
+        if (j + 1 < nt) {
+          if (!(ok = mbar_wait(&s.k_full[st1], ((j + 1) / NS) & 1))) break;
+          tc_fence_after();
+          issue_s(0, st1);
+          tc_commit(&s.s_full[0]);
+        }
+        if (!(ok = !aborted(s) && mbar_wait(&s.p_full[1], j & 1))) break;
+        tc_fence_after();
+        issue_pv(1, st, j == 0);
+        tc_commit(&s.o_full[1]);
+        tc_commit(&s.kv_empty[st]);
+        if (j + 1 < nt) {
+          issue_s(1, st1);
+          tc_commit(&s.s_full[1]);
+        }
+      }
+      if (!ok) set_abort(s);
+      tc_commit(&s.mma_done);
+      mbar_wait(&s.mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int h = (warp - 2) >> 2;           // 0 for warps 2-5, 1 for warps 6-9
+    const int quad = warp & 3;               // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;        // query row within the block
+    const int q_row = q0 + row;
+    const int my_last = p.off + q_row;       // last visible key (inclusive)
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t tS = lane_base + h * 128;
+    const uint32_t tO = lane_base + 256 + h * 128;
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      if (!(ok = warp_wait(s, &s.s_full[h], j & 1))) break;
+      tc_fence_after();
+      uint32_t r[BN];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+      tmem_wait_ld();
+      const int k0 = j * BN;
+      if (k0 + BN - 1 > p.off + q0 || k0 + BN > p.kL) {  // tile crosses the diagonal or kL
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          const int key = k0 + c;
+          if (key > my_last || key >= p.kL) r[c] = __float_as_uint(-INFINITY);
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(r[c]));
+      const float mt = mx * sl2;
+      const bool need = mt > m + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float mn = fmaxf(m, mt);
+        if (j > 0) {
+          const float alpha = fast_exp2(m - mn);
+          if (!(ok = warp_wait(s, &s.o_full[h], (j - 1) & 1))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+          l *= alpha;
+        }
+        m = mn;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(r[half * 64 + 2 * c]), sl2, -m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(r[half * 64 + 2 * c + 1]), sl2, -m));
+          sum += p0 + p1;
+          pk[c] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(tS + half * 32, pk);
+      }
+      l += sum;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&s.p_full[h]);
+    }
+    // ---- epilogue: O / l -> BF16, row-major [qL, H*128]
+    if (ok && warp_wait(s, &s.o_full[h], (nt - 1) & 1)) {
+      tc_fence_after();
+      const float inv_l = 1.f / l;
+      uint16_t *dst = p.out + static_cast<size_t>(q_row) * (p.H * D) + (2 * g + h) * D;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+        if (q_row < p.qL) {
+          uint4 *d4 = reinterpret_cast<uint4 *>(dst + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+            w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+            w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+            w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+            d4[v] = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 3-D BF16 map (128, rows, heads), row stride 256 B, head stride
+// head_stride_rows*256 B; box (64, 128, 1); rows past `rows` read as zero.
+inline bool make_map(CUtensorMap *m, const void *base, int rows, int heads, long long head_stride_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(heads)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2),
+                           static_cast<cuuint64_t>(head_stride_rows) * D * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool g_smem_done[64];
+
+inline int launch(const void *Q, const void *K, const void *V, int qL, int kL, int qLp, int cap,
+                  int H, int nkv, float scale, void *O, void *stream, bool (*bind)(void *)) {
+  if (!Q || !K || !V || !O) return RIB_EINVAL;
+  if (nkv < 1 || H != 2 * nkv || qL < 1 || qLp < qL || kL < qL || cap < 1 || !(scale > 0.f))
+    return RIB_EINVAL;
+  if (kL > cap) return RIB_ECAPACITY;
+  auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (!a16(Q) || !a16(K) || !a16(V) || !a16(O)) return RIB_EALIGN;
+  if (!bind(stream)) return RIB_ECUDA;
+  Params p;
+  if (!make_map(&p.tm_q, Q, qLp, H, qLp) || !make_map(&p.tm_k, K, kL, nkv, cap) ||
+      !make_map(&p.tm_v, V, kL, nkv, cap))
+    return RIB_ECUDA;
+  p.out = static_cast<uint16_t *>(O);
+  p.qL = qL;
+  p.kL = kL;
+  p.H = H;
+  p.nkv = nkv;
+  p.off = kL - qL;
+  p.nqb = (qL + BM - 1) / BM;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int smem = static_cast<int>(sizeof(Smem)) + 1024;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RIB_ECUDA;
+  if (!g_smem_done[dev]) {
+    if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return RIB_ECUDA;
+    g_smem_done[dev] = true;
+  }
+  prefill_kernel<<<p.nqb * nkv, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? RIB_OK : RIB_ECUDA;
+}
+
+}  // namespace prefill
+}  // namespace rib

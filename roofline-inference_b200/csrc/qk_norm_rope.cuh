@@ -1,0 +1,132 @@
+// Fused per-head RMSNorm + RoPE with the KV-cache append folded in.
+//
+// Semantics follow the reference Metal kernels agent-test/v2/kernels.py:116-146
+// (one token) and :169-204 (L tokens):
+//   inv  = 1 / sqrt(mean(x^2) + 1e-6)                      (kernels.py:129-130)
+//   n_d  = bf16( w_d * bf16( x_d * inv ) )                  (kernels.py:131-133)
+//   non-traditional RoPE, pairs (d, d+64), d in [0, 64):    (kernels.py:136-143)
+//     theta_d = pos * base^(-d/64)
+//     o_d    = n_d cos - n_{d+64} sin,  o_{d+64} = n_d sin + n_{d+64} cos
+//   V heads are copied bit for bit                         (kernels.py:123-127)
+// Differences from the Metal source, by design:
+//   - theta is formed and reduced to [-pi, pi] in FP64 and evaluated with the
+//     full-range sincosf, so large positions (32k) keep full FP32 accuracy
+//     (the Metal code uses an FP32 product and fast::cos / fast::sin);
+//   - K and V are written straight into the cache rows (engine.py:42-48 fused).
+//
+// Layout of the work: one CTA per token; each warp owns two (token, head)
+// items, one per half-warp; lane j of a half-warp owns dims [8j, 8j+8), moved
+// as one 16-byte vector.  The RoPE partner of dim d < 64 lives in lane j ^ 8.
+#pragma once
+
+#include "common.cuh"
+
+namespace rib {
+namespace rope {
+
+constexpr int D = 128;
+constexpr int kMaxItems = 64;  // nq + 2*nkv per token
+
+struct Params {
+  const uint16_t *qkv;  // [L][items*128]
+  const uint16_t *qw;   // [128]
+  const uint16_t *kw;   // [128]
+  uint16_t *q_out;      // [nq][Lp][128]
+  uint16_t *kv;         // [2][nkv][kv_rows][128]
+  int L, Lp, offset, nq, nkv;
+  int kv_rows;          // rows per head in kv (L, or the cache capacity)
+  int kv_row0;          // first row written (0, or the cache offset)
+  double inv_freq[64];  // base^(-d/64), FP64
+};
+
+__global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constant__ Params p) {
+  __shared__ float cos_t[64], sin_t[64];
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (tid < 64) {
+    const double two_pi = 6.283185307179586476925286766559;
+    const double th = static_cast<double>(p.offset + t) * p.inv_freq[tid];
+    const double r = th - rint(th * (1.0 / two_pi)) * two_pi;
+    float s, c;
+    sincosf(static_cast<float>(r), &s, &c);
+    cos_t[tid] = c;
+    sin_t[tid] = s;
+  }
+  __syncthreads();
+
+  const int items = p.nq + 2 * p.nkv;
+  const int lane = tid & 31;
+  const int item = (tid >> 5) * 2 + (lane >> 4);
+  const int j = lane & 15;
+  if (item >= items) return;
+  const unsigned half_mask = 0xffffu << (lane & 16);
+
+  if (t >= p.L) {  // padding rows of Q are zero (kernels.py:223, init_value=0)
+    if (item < p.nq) {
+      uint4 z = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4 *>(p.q_out + (static_cast<size_t>(item) * p.Lp + t) * D + 8 * j) = z;
+    }
+    return;
+  }
+
+  const uint4 raw = *reinterpret_cast<const uint4 *>(
+      p.qkv + (static_cast<size_t>(t) * items + item) * D + 8 * j);
+
+  if (item >= p.nq + p.nkv) {  // V: bit-exact copy into the cache
+    const int hv = item - p.nq - p.nkv;
+    uint16_t *dst = p.kv + ((static_cast<size_t>(p.nkv + hv) * p.kv_rows) + p.kv_row0 + t) * D + 8 * j;
+    *reinterpret_cast<uint4 *>(dst) = raw;
+    return;
+  }
+
+  float x[8];
+  x[0] = bf16lo(raw.x); x[1] = bf16hi(raw.x);
+  x[2] = bf16lo(raw.y); x[3] = bf16hi(raw.y);
+  x[4] = bf16lo(raw.z); x[5] = bf16hi(raw.z);
+  x[6] = bf16lo(raw.w); x[7] = bf16hi(raw.w);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o, 16);
+  const float inv = 1.0f / sqrtf(ss / 128.0f + 1e-6f);
+
+  const uint4 wraw = *reinterpret_cast<const uint4 *>((item < p.nq ? p.qw : p.kw) + 8 * j);
+  float w[8];
+  w[0] = bf16lo(wraw.x); w[1] = bf16hi(wraw.x);
+  w[2] = bf16lo(wraw.y); w[3] = bf16hi(wraw.y);
+  w[4] = bf16lo(wraw.z); w[5] = bf16hi(wraw.z);
+  w[6] = bf16lo(wraw.w); w[7] = bf16hi(wraw.w);
+
+  float nv[8], pv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) nv[i] = round_bf16(w[i] * round_bf16(x[i] * inv));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(half_mask, nv[i], 8, 16);
+
+  const bool first_half = j < 8;
+  const int a0 = 8 * (j & 7);
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float c = cos_t[a0 + i], s = sin_t[a0 + i];
+    // first half: x1 = nv, x2 = pv ; second half: x1 = pv, x2 = nv
+    o[i] = first_half ? fmaf(nv[i], c, -pv[i] * s) : fmaf(pv[i], s, nv[i] * c);
+  }
+  uint4 out;
+  out.x = pack_bf16x2(o[0], o[1]);
+  out.y = pack_bf16x2(o[2], o[3]);
+  out.z = pack_bf16x2(o[4], o[5]);
+  out.w = pack_bf16x2(o[6], o[7]);
+  uint16_t *dst;
+  if (item < p.nq) {
+    dst = p.q_out + (static_cast<size_t>(item) * p.Lp + t) * D + 8 * j;
+  } else {
+    const int hk = item - p.nq;
+    dst = p.kv + ((static_cast<size_t>(hk) * p.kv_rows) + p.kv_row0 + t) * D + 8 * j;
+  }
+  *reinterpret_cast<uint4 *>(dst) = out;
+}
+
+}  // namespace rope
+}  // namespace rib

@@ -1,0 +1,262 @@
+// C ABI of the B200 attention hot path: host-side argument checks, launch
+// geometry and workspace layout for the kernels in the *.cuh files.
+// Built as one translation unit so that all kernels share the device status
+// word (common.cuh).
+#include <cmath>
+#include <cstdio>
+
+#include "common.cuh"
+#include "decode_attention.cuh"
+#include "prefill_attention.cuh"
+#include "qk_norm_rope.cuh"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return dev;
+}
+
+// SM count of the current device (148 on B200); 148 when no device is visible,
+// so that workspace sizing also answers on a host without a GPU.
+int sm_count() {
+  static int cached[kMaxDevices] = {0};
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// Dynamic shared memory opt-in, once per (kernel, device).
+template <typename Kernel>
+bool set_smem_once(Kernel kernel, int bytes, bool *done_table) {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return false;
+  if (!done_table[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+      return false;
+    done_table[dev] = true;
+  }
+  return true;
+}
+
+int launch_status() { return cudaGetLastError() == cudaSuccess ? RIB_OK : RIB_ECUDA; }
+
+// Makes the stream's device current for this library's runtime, so a launch
+// lands on the caller's device whatever this thread's runtime state says.
+bool bind_stream_device(void *stream) {
+  if (!stream) return true;
+  int dev = -1;
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != dev) {
+    cudaGetLastError();
+    if (cudaSetDevice(dev) != cudaSuccess) return false;
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ rope
+int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offset, int nq, int nkv,
+                double base, int Lp, void *q_out, void *kv, int kv_rows, int kv_row0, void *stream) {
+  if (L < 1 || Lp < L || nq < 1 || nkv < 1 || nq + 2 * nkv > rib::rope::kMaxItems || offset < 0 ||
+      !(base > 0.0) || kv_rows < 1)
+    return RIB_EINVAL;
+  if (!qkv || !qw || !kw || !q_out || !kv) return RIB_EINVAL;
+  if (!aligned16(qkv) || !aligned16(qw) || !aligned16(kw) || !aligned16(q_out) || !aligned16(kv))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return RIB_ECUDA;
+  rib::rope::Params p;
+  p.qkv = static_cast<const uint16_t *>(qkv);
+  p.qw = static_cast<const uint16_t *>(qw);
+  p.kw = static_cast<const uint16_t *>(kw);
+  p.q_out = static_cast<uint16_t *>(q_out);
+  p.kv = static_cast<uint16_t *>(kv);
+  p.L = L;
+  p.Lp = Lp;
+  p.offset = offset;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.kv_rows = kv_rows;
+  p.kv_row0 = kv_row0;
+  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
+  const int items = nq + 2 * nkv;
+  const int threads = ((items + 1) / 2) * 32;
+  rib::rope::qk_norm_rope_kernel<<<Lp, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
+// ------------------------------------------------------------------ decode
+struct DecodeGeometry {
+  int chunk;
+  int max_splits;
+  size_t counters_bytes, ml_bytes, o_bytes, total;
+};
+
+DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
+  using namespace rib::decode;
+  DecodeGeometry g;
+  const long long target = 2LL * sm_count();  // two CTAs per SM
+  const long long total = static_cast<long long>(batch) * nkv * max_n;
+  int chunk = ceil_div(total, target);
+  chunk = ceil_div(chunk, TK) * TK;
+  if (chunk < TK) chunk = TK;
+  if (chunk > 1024) chunk = 1024;
+  g.chunk = chunk;
+  g.max_splits = ceil_div(max_n, chunk);
+  const size_t units = static_cast<size_t>(batch) * nkv;
+  g.counters_bytes = ((units * sizeof(int) + 255) / 256) * 256;
+  g.ml_bytes = ((units * g.max_splits * 2 * 2 * sizeof(float) + 255) / 256) * 256;
+  g.o_bytes = units * g.max_splits * 2 * D * sizeof(float);
+  g.total = g.counters_bytes + g.ml_bytes + g.o_bytes;
+  return g;
+}
+
+bool g_decode_smem_done[kMaxDevices];
+
+int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, size_t workspace_bytes,
+                  void *stream) {
+  using namespace rib::decode;
+  if (!bind_stream_device(stream)) return RIB_ECUDA;
+  const DecodeGeometry g = decode_geometry(batch, max_n, p.nkv);
+  if (!workspace || workspace_bytes < g.total) return RIB_EINVAL;
+  if (!aligned16(workspace)) return RIB_EALIGN;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  p.counters = reinterpret_cast<int *>(ws);
+  p.part_ml = reinterpret_cast<float *>(ws + g.counters_bytes);
+  p.part_o = reinterpret_cast<float *>(ws + g.counters_bytes + g.ml_bytes);
+  p.chunk = g.chunk;
+  p.max_splits = g.max_splits;
+  p.max_n = max_n;
+  const int smem = static_cast<int>(sizeof(Smem)) + 128;
+  if (!set_smem_once(decode_kernel, smem, g_decode_smem_done)) return RIB_ECUDA;
+  dim3 grid(g.max_splits, p.nkv, batch);
+  decode_kernel<<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int rib_version(void) { return (1 << 16) | 0; }
+
+const char *rib_status_string(int status) {
+  switch (status) {
+    case RIB_OK: return "ok";
+    case RIB_EINVAL: return "invalid argument or shape";
+    case RIB_ECAPACITY: return "KV capacity exceeded";
+    case RIB_EALIGN: return "pointer not 16-byte aligned";
+    case RIB_ECUDA: return "CUDA runtime error";
+    case RIB_ETIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int rib_take_device_status(int *status_host) {
+  if (!status_host) return RIB_EINVAL;
+  if (cudaDeviceSynchronize() != cudaSuccess) return RIB_ECUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, rib::g_device_status, sizeof(int)) != cudaSuccess) return RIB_ECUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(rib::g_device_status, &zero, sizeof(int)) != cudaSuccess) return RIB_ECUDA;
+  *status_host = v;
+  return RIB_OK;
+}
+
+int rib_qk_norm_rope(const void *qkv, const void *qw, const void *kw, int pos, int nq, int nkv,
+                     double base, void *q_out, void *kv_out, void *stream) {
+  return rope_launch(qkv, 1, qw, kw, pos, nq, nkv, base, 1, q_out, kv_out, 1, 0, stream);
+}
+
+int rib_qk_norm_rope_prefill(const void *qkv, int L, const void *qw, const void *kw, int offset,
+                             int nq, int nkv, double base, int Lp, void *q_out, void *kv_out,
+                             void *stream) {
+  return rope_launch(qkv, L, qw, kw, offset, nq, nkv, base, Lp, q_out, kv_out, L, 0, stream);
+}
+
+int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw, const void *kw, int offset,
+                            int nq, int nkv, double base, int Lp, void *q_out, void *cache,
+                            int cap, void *stream) {
+  if (L < 1 || offset < 0 || cap < 1) return RIB_EINVAL;
+  if (static_cast<long long>(offset) + L > cap) return RIB_ECAPACITY;
+  return rope_launch(qkv, L, qw, kw, offset, nq, nkv, base, Lp, q_out, cache, cap, offset, stream);
+}
+
+size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv) {
+  if (batch < 1 || max_n < 1 || nkv < 1) return 0;
+  return decode_geometry(batch, max_n, nkv).total;
+}
+
+int rib_decode_attention(const void *q, const void *cache, int cap, int n, int nq, int nkv,
+                         float scale, void *out, void *workspace, size_t workspace_bytes,
+                         void *stream) {
+  if (!q || !cache || !out) return RIB_EINVAL;
+  if (nkv < 1 || nq != 2 * nkv || n < 1 || cap < 1 || !(scale > 0.f)) return RIB_EINVAL;
+  if (n > cap) return RIB_ECAPACITY;
+  if (!aligned16(q) || !aligned16(cache) || !aligned16(out)) return RIB_EALIGN;
+  rib::decode::Params p = {};
+  p.q = static_cast<const uint16_t *>(q);
+  p.cache = static_cast<const uint16_t *>(cache);
+  p.cache_ptrs = nullptr;
+  p.lens = nullptr;
+  p.n_single = n;
+  p.cap = cap;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t *>(out);
+  return decode_launch(p, 1, n, workspace, workspace_bytes, stream);
+}
+
+int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs, const int32_t *lens,
+                                 int batch, int max_n, int cap, int nq, int nkv, float scale,
+                                 void *out, void *workspace, size_t workspace_bytes, void *stream) {
+  if (!q || !cache_ptrs || !lens || !out) return RIB_EINVAL;
+  if (batch < 1 || nkv < 1 || nq != 2 * nkv || max_n < 1 || cap < 1 || !(scale > 0.f))
+    return RIB_EINVAL;
+  if (max_n > cap) return RIB_ECAPACITY;
+  if (!aligned16(q) || !aligned16(out) || (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) ||
+      (reinterpret_cast<uintptr_t>(lens) & 3u))
+    return RIB_EALIGN;
+  rib::decode::Params p = {};
+  p.q = static_cast<const uint16_t *>(q);
+  p.cache = nullptr;
+  p.cache_ptrs = cache_ptrs;
+  p.lens = lens;
+  p.n_single = 0;
+  p.cap = cap;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t *>(out);
+  return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
+}
+
+int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL, int kL, int qLp,
+                          int cap, int H, int nkv, float scale, void *O, void *stream) {
+  return rib::prefill::launch(Q, K, V, qL, kL, qLp, cap, H, nkv, scale, O, stream,
+                              bind_stream_device);
+}
+
+}  // extern "C"

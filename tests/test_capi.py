@@ -1,0 +1,100 @@
+"""CPU: the C-ABI library loads, exports every entry point the header
+declares, and rejects bad arguments on the host (before any launch) with the
+documented status codes.  No call here reaches a kernel launch."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "rib_attention.h"
+FAKE = 0x10000  # 16-byte aligned dummy address; never dereferenced
+MISALIGNED = 0x10008
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(rib_\w+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ["rib_qk_norm_rope", "rib_qk_norm_rope_prefill", "rib_qk_norm_rope_append",
+              "rib_decode_attention", "rib_decode_attention_batched", "rib_prefill_attention",
+              "rib_decode_workspace_bytes", "rib_version", "rib_status_string",
+              "rib_take_device_status"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(rib):
+    L = rib.load_library()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+
+
+def test_status_strings(rib):
+    L = rib.load_library()
+    assert L.rib_status_string(0) == b"ok"
+    assert L.rib_status_string(2) == b"KV capacity exceeded"
+    assert L.rib_version() >> 16 == 1
+
+
+def test_workspace_bytes(rib):
+    L = rib.load_library()
+    a = L.rib_decode_workspace_bytes(1, 513, 8)
+    b = L.rib_decode_workspace_bytes(1, 32769, 8)
+    c = L.rib_decode_workspace_bytes(64, 32768, 8)
+    assert 0 < a <= b < c
+    assert L.rib_decode_workspace_bytes(0, 10, 8) == 0
+
+
+def test_decode_rejects_bad_arguments(rib):
+    L = rib.load_library()
+    ws = L.rib_decode_workspace_bytes(1, 100, 8)
+    # GQA factor must be 2
+    assert L.rib_decode_attention(FAKE, FAKE, 256, 100, 15, 8, 0.088, FAKE, FAKE, ws, None) == 1
+    # n beyond capacity
+    assert L.rib_decode_attention(FAKE, FAKE, 256, 300, 16, 8, 0.088, FAKE, FAKE, ws, None) == 2
+    # misaligned pointer
+    assert L.rib_decode_attention(MISALIGNED, FAKE, 256, 100, 16, 8, 0.088, FAKE, FAKE, ws,
+                                  None) == 3
+    # null pointers
+    assert L.rib_decode_attention(None, FAKE, 256, 100, 16, 8, 0.088, FAKE, FAKE, ws, None) == 1
+    assert L.rib_decode_attention_batched(FAKE, None, FAKE, 2, 100, 256, 16, 8, 0.088, FAKE,
+                                          FAKE, ws, None) == 1
+    assert L.rib_decode_attention_batched(FAKE, FAKE, FAKE, 2, 300, 256, 16, 8, 0.088, FAKE,
+                                          FAKE, ws, None) == 2
+
+
+def test_rope_rejects_bad_arguments(rib):
+    L = rib.load_library()
+    # offset + L beyond the cache capacity -> "KV capacity exceeded"
+    assert L.rib_qk_norm_rope_append(FAKE, 37, FAKE, FAKE, 240, 16, 8, 1e6, 37, FAKE, FAKE, 256,
+                                     None) == 2
+    # Lp < L
+    assert L.rib_qk_norm_rope_prefill(FAKE, 37, FAKE, FAKE, 0, 16, 8, 1e6, 32, FAKE, FAKE,
+                                      None) == 1
+    # misaligned
+    assert L.rib_qk_norm_rope(MISALIGNED, FAKE, FAKE, 0, 16, 8, 1e6, FAKE, FAKE, None) == 3
+    # too many heads per token
+    assert L.rib_qk_norm_rope(FAKE, FAKE, FAKE, 0, 60, 8, 1e6, FAKE, FAKE, None) == 1
+
+
+def test_prefill_rejects_bad_arguments(rib):
+    L = rib.load_library()
+    # H != 2 * nkv
+    assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 64, 64, 256, 12, 8, 0.088, FAKE,
+                                   None) == 1
+    # kL < qL
+    assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 32, 64, 256, 16, 8, 0.088, FAKE,
+                                   None) == 1
+    # kL beyond cap
+    assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 300, 64, 256, 16, 8, 0.088, FAKE,
+                                   None) == 2
+    # misaligned
+    assert L.rib_prefill_attention(MISALIGNED, FAKE, FAKE, 64, 64, 64, 256, 16, 8, 0.088, FAKE,
+                                   None) == 3
