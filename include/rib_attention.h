@@ -46,6 +46,10 @@ int rib_version(void);
 /* Human-readable text for a status code (static storage). */
 const char *rib_status_string(int status);
 
+/* Text of the last host-side failure on the calling thread (which step and
+ * which CUDA error), "" if none yet.  Static thread-local storage. */
+const char *rib_last_error_string(void);
+
 /* Reads and clears the device-side status word of the current device: 0 if
  * no kernel recorded a timeout since the last call, RIB_ETIMEOUT otherwise.
  * Synchronises the current device. */

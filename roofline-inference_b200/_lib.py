@@ -94,6 +94,7 @@ def _bind(L: ctypes.CDLL) -> None:
     sig = {
         "rib_version": ([], i),
         "rib_status_string": ([i], ctypes.c_char_p),
+        "rib_last_error_string": ([], ctypes.c_char_p),
         "rib_take_device_status": ([ctypes.POINTER(ctypes.c_int)], i),
         "rib_qk_norm_rope": ([vp, vp, vp, i, i, i, d, vp, vp, vp], i),
         "rib_qk_norm_rope_prefill": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, vp], i),
@@ -128,7 +129,8 @@ def check(status: int, what: str) -> None:
     msg = load().rib_status_string(status).decode()
     if status in (RIB_EINVAL, RIB_ECAPACITY, RIB_EALIGN):
         raise ValueError(f"{what}: {msg}")
-    raise RuntimeError(f"{what}: {msg} (status {status})")
+    detail = load().rib_last_error_string().decode()
+    raise RuntimeError(f"{what}: {msg} (status {status}): {detail}")
 
 
 def take_device_status() -> int:

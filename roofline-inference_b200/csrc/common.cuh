@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 
 #include "../../include/rib_attention.h"
 
@@ -23,6 +24,21 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Host side: text of the last host-side failure on this thread (step and
+// CUDA error), returned by rib_last_error_string().
+inline thread_local char g_last_error[256] = "";
+
+inline int host_fail(int status, const char *step, int code) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s failed (code %d)", step, code);
+  return status;
+}
+
+inline int host_fail_cuda(const char *step, cudaError_t err) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s failed: %s (%s)", step, cudaGetErrorName(err),
+           cudaGetErrorString(err));
+  return RIB_ECUDA;
 }
 
 __device__ __forceinline__ void record_timeout() {

@@ -91,6 +91,15 @@ __device__ __forceinline__ void set_abort(Smem &s) {
   *reinterpret_cast<volatile int *>(&s.abort_flag) = 1;
 }
 
+// Causal / length mask of 32 score columns starting at key `key0`.
+__device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], int key0, int my_last, int kL) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const int key = key0 + e;
+    if (key > my_last || key >= kL) r[e] = __float_as_uint(-INFINITY);
+  }
+}
+
 // Warp-uniform bounded wait: every lane waits, then all agree.
 __device__ __forceinline__ bool warp_wait(Smem &s, uint64_t *bar, uint32_t parity) {
   bool ok = !aborted(s) && mbar_wait(bar, parity);
@@ -99,7 +108,7 @@ __device__ __forceinline__ bool warp_wait(Smem &s, uint64_t *bar, uint32_t parit
   return ok;
 }
 
-__global__ void __maxnreg__(200) prefill_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -243,21 +252,19 @@ __global__ void __maxnreg__(200) prefill_kernel(const __grid_constant__ Params p
     for (int j = 0; j < nt; ++j) {
       if (!(ok = warp_wait(s, &s.s_full[h], j & 1))) break;
       tc_fence_after();
-      uint32_t r[BN];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-      tmem_wait_ld();
       const int k0 = j * BN;
-      if (k0 + BN - 1 > p.off + q0 || k0 + BN > p.kL) {  // tile crosses the diagonal or kL
-#pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int key = k0 + c;
-          if (key > my_last || key >= p.kL) r[c] = __float_as_uint(-INFINITY);
-        }
-      }
+      const bool masked = k0 + BN - 1 > p.off + q0 || k0 + BN > p.kL;  // crosses diagonal or kL
+      // pass 1: row maximum over the tile, 32 columns at a time
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) mx = fmaxf(mx, __uint_as_float(r[c]));
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + c * 32, r);
+        tmem_wait_ld();
+        if (masked) mask_chunk(r, k0 + c * 32, my_last, p.kL);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+      }
       const float mt = mx * sl2;
       const bool need = mt > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
@@ -279,16 +286,26 @@ __global__ void __maxnreg__(200) prefill_kernel(const __grid_constant__ Params p
         }
         m = mn;
       }
+      // pass 2: P = exp2(S * scale*log2e - m) as packed BF16 over S's first
+      // 64 columns; S columns [32h', 32h'+64) are read before P half h' lands.
       float sum = 0.f;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(r[half * 64 + 2 * c]), sl2, -m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(r[half * 64 + 2 * c + 1]), sl2, -m));
-          sum += p0 + p1;
-          pk[c] = pack_bf16x2(p0, p1);
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;
+          uint32_t r[32];
+          tmem_ld32(tS + c * 32, r);
+          tmem_wait_ld();
+          if (masked) mask_chunk(r, k0 + c * 32, my_last, p.kL);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(r[2 * e]), sl2, -m));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(r[2 * e + 1]), sl2, -m));
+            sum += p0 + p1;
+            pk[cc * 16 + e] = pack_bf16x2(p0, p1);
+          }
         }
         tmem_st32(tS + half * 32, pk);
       }
@@ -339,10 +356,12 @@ inline EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
     void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess) {
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !ptr) {
       cudaGetLastError();
+      host_fail(RIB_ECUDA, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)",
+                e != cudaSuccess ? static_cast<int>(e) : static_cast<int>(q));
       return nullptr;
     }
     fn = reinterpret_cast<EncodeTiledFn>(ptr);
@@ -361,9 +380,14 @@ inline bool make_map(CUtensorMap *m, const void *base, int rows, int heads, long
                            static_cast<cuuint64_t>(head_stride_rows) * D * 2};
   cuuint32_t box[3] = {64, 128, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides,
+                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    host_fail(RIB_ECUDA, "cuTensorMapEncodeTiled", static_cast<int>(r));
+    return false;
+  }
+  return true;
 }
 
 inline bool g_smem_done[64];
@@ -376,7 +400,7 @@ inline int launch(const void *Q, const void *K, const void *V, int qL, int kL, i
   if (kL > cap) return RIB_ECAPACITY;
   auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   if (!a16(Q) || !a16(K) || !a16(V) || !a16(O)) return RIB_EALIGN;
-  if (!bind(stream)) return RIB_ECUDA;
+  if (!bind(stream)) return host_fail(RIB_ECUDA, "bind stream device", 0);
   Params p;
   if (!make_map(&p.tm_q, Q, qLp, H, qLp) || !make_map(&p.tm_k, K, kL, nkv, cap) ||
       !make_map(&p.tm_v, V, kL, nkv, cap))
@@ -391,15 +415,35 @@ inline int launch(const void *Q, const void *K, const void *V, int qL, int kL, i
   p.scale_log2 = scale * 1.4426950408889634f;
   const int smem = static_cast<int>(sizeof(Smem)) + 1024;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RIB_ECUDA;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return host_fail_cuda("cudaGetDevice", e);
   if (!g_smem_done[dev]) {
-    if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return host_fail_cuda("cudaFuncSetAttribute(prefill smem)", e);
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, prefill_kernel);
+    if (e != cudaSuccess) return host_fail_cuda("cudaFuncGetAttributes(prefill)", e);
+    if (fa.maxThreadsPerBlock < NTHREADS || fa.maxDynamicSharedSizeBytes < smem) {
+      snprintf(g_last_error, sizeof(g_last_error),
+               "prefill_kernel cannot launch: %d registers/thread, max %d threads/block (need %d), "
+               "max dynamic smem %d (need %d)",
+               fa.numRegs, fa.maxThreadsPerBlock, NTHREADS, fa.maxDynamicSharedSizeBytes, smem);
       return RIB_ECUDA;
+    }
     g_smem_done[dev] = true;
   }
   prefill_kernel<<<p.nqb * nkv, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? RIB_OK : RIB_ECUDA;
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFuncAttributes fa;
+    cudaFuncGetAttributes(&fa, prefill_kernel);
+    snprintf(g_last_error, sizeof(g_last_error),
+             "prefill_kernel launch failed: %s (regs/thread %d, max threads/block %d, smem %d, "
+             "max dyn smem %d)", cudaGetErrorName(e), fa.numRegs, fa.maxThreadsPerBlock, smem,
+             fa.maxDynamicSharedSizeBytes);
+    return RIB_ECUDA;
+  }
+  return RIB_OK;
 }
 
 }  // namespace prefill

@@ -57,7 +57,10 @@ bool set_smem_once(Kernel kernel, int bytes, bool *done_table) {
   return true;
 }
 
-int launch_status() { return cudaGetLastError() == cudaSuccess ? RIB_OK : RIB_ECUDA; }
+int launch_status(const char *what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda(what, e);
+}
 
 // Makes the stream's device current for this library's runtime, so a launch
 // lands on the caller's device whatever this thread's runtime state says.
@@ -85,7 +88,7 @@ int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offs
   if (!qkv || !qw || !kw || !q_out || !kv) return RIB_EINVAL;
   if (!aligned16(qkv) || !aligned16(qw) || !aligned16(kw) || !aligned16(q_out) || !aligned16(kv))
     return RIB_EALIGN;
-  if (!bind_stream_device(stream)) return RIB_ECUDA;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
   rib::rope::Params p;
   p.qkv = static_cast<const uint16_t *>(qkv);
   p.qw = static_cast<const uint16_t *>(qw);
@@ -103,7 +106,7 @@ int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offs
   const int items = nq + 2 * nkv;
   const int threads = ((items + 1) / 2) * 32;
   rib::rope::qk_norm_rope_kernel<<<Lp, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status();
+  return launch_status("qk_norm_rope_kernel launch");
 }
 
 // ------------------------------------------------------------------ decode
@@ -137,7 +140,7 @@ bool g_decode_smem_done[kMaxDevices];
 int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, size_t workspace_bytes,
                   void *stream) {
   using namespace rib::decode;
-  if (!bind_stream_device(stream)) return RIB_ECUDA;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
   const DecodeGeometry g = decode_geometry(batch, max_n, p.nkv);
   if (!workspace || workspace_bytes < g.total) return RIB_EINVAL;
   if (!aligned16(workspace)) return RIB_EALIGN;
@@ -149,10 +152,11 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   p.max_splits = g.max_splits;
   p.max_n = max_n;
   const int smem = static_cast<int>(sizeof(Smem)) + 128;
-  if (!set_smem_once(decode_kernel, smem, g_decode_smem_done)) return RIB_ECUDA;
+  if (!set_smem_once(decode_kernel, smem, g_decode_smem_done))
+    return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(decode smem)", 0);
   dim3 grid(g.max_splits, p.nkv, batch);
   decode_kernel<<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status();
+  return launch_status("decode_kernel launch");
 }
 
 }  // namespace
@@ -172,6 +176,8 @@ const char *rib_status_string(int status) {
     default: return "unknown status";
   }
 }
+
+const char *rib_last_error_string(void) { return rib::g_last_error; }
 
 int rib_take_device_status(int *status_host) {
   if (!status_host) return RIB_EINVAL;
