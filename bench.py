@@ -206,12 +206,10 @@ def max_over_ranks(x: float, world: int, device) -> float:
 
 
 # ---------------------------------------------------------------- CPU leg
-def cpu_decode_sample(layers_sample: int = 4, ctx: int = CTX, budget_s: float = 12.0) -> dict:
-    """Times the C oracle (all host threads) on `layers_sample` layers of the
-    decode sweep at `ctx`; value in GB/s of KV read."""
-    from oracle import oracle as coracle
+def cpu_sample_workload(layers_sample: int = 4, ctx: int = CTX):
+    """Host copies of `layers_sample` layers of the decode sweep (the same
+    seeds as the GPU workload), as uint16 BF16 bit patterns."""
     import numpy as np
-    threads = coracle.set_threads(os.cpu_count())
     wl = importlib.import_module("roofline-inference_b200.workloads")
     n = ctx + 1
     cap = wl.round_cap(n)
@@ -223,47 +221,69 @@ def cpu_decode_sample(layers_sample: int = 4, ctx: int = CTX, budget_s: float = 
                 t = wl.randn_bf16((n, 128), seed=(layer * 64 + h) * 2 + kv)
                 c[kv, h, :n] = t.view(torch.int16).numpy().view(np.uint16)
         caches.append(c)
-        qq = np.concatenate([wl.randn_bf16((2, 128), seed=900000 + layer * 64 + h)
-                             .view(torch.int16).numpy().view(np.uint16) for h in range(NKV_TOTAL)])
-        qs.append(qq)
-    q = np.stack(qs)
-    coracle.decode_attention_batched(q, caches, [n] * layers_sample, 128 ** -0.5)  # warm
+        qs.append(np.concatenate([wl.randn_bf16((2, 128), seed=900000 + layer * 64 + h)
+                                  .view(torch.int16).numpy().view(np.uint16)
+                                  for h in range(NKV_TOTAL)]))
+    return np.stack(qs), caches, n
+
+
+def cpu_pass(sample) -> float:
+    """One pass of the C oracle (all host threads) over the sample; seconds."""
+    from oracle import oracle as coracle
+    q, caches, n = sample
+    t0 = time.perf_counter()
+    coracle.decode_attention_batched(q, caches, [n] * len(caches), 128 ** -0.5)
+    return time.perf_counter() - t0
+
+
+def cpu_decode_sample(layers_sample: int = 4, ctx: int = CTX, budget_s: float = 12.0) -> dict:
+    """Times the C oracle (OpenMP, all host threads) on `layers_sample` layers
+    of the decode sweep at `ctx`, repeated for about `budget_s` seconds; value
+    in GB/s of KV read (4096 B per key per layer)."""
+    from oracle import oracle as coracle
+    threads = coracle.set_threads(os.cpu_count())
+    sample = cpu_sample_workload(layers_sample, ctx)
+    cpu_pass(sample)  # warm
     reps, t_total = 0, 0.0
     while t_total < budget_s and reps < 10000:
-        t0 = time.perf_counter()
-        coracle.decode_attention_batched(q, caches, [n] * layers_sample, 128 ** -0.5)
-        t_total += time.perf_counter() - t0
+        t_total += cpu_pass(sample)
         reps += 1
-    bytes_per = layers_sample * 4096 * n
+    bytes_per = layers_sample * 4096 * sample[2]
     return {"value": bytes_per * reps / t_total / 1e9, "unit": "GB/s", "cores": threads,
             "kind": "port",
             "sample": f"{layers_sample} of {N_LAYERS} layers at ctx {ctx} (all 8 KV heads), "
-                      f"{reps} repetitions, C oracle (OpenMP FP32)",
+                      f"{reps} passes in {t_total:.1f} s, C oracle (OpenMP FP32)",
             "seconds": t_total}
 
 
 def run_reference(args):
     """--impl reference: the reference's CPU path for this workload.  MLX (the
     reference's attention backend) is not installable here, so the CPU oracle
-    port of its semantics is timed on the host cores."""
+    port of its semantics is timed on the host cores; each step is one pass
+    over a 4-layer sample of the 28-layer sweep."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    samples = []
+    from oracle import oracle as coracle
+    threads = coracle.set_threads(os.cpu_count())
+    layers_sample = 4
+    sample = cpu_sample_workload(layers_sample)
     for _ in range(max(args.warmup, 0)):
-        cpu_decode_sample(layers_sample=1, budget_s=1.0)
-    for _ in range(args.steps):
-        samples.append(cpu_decode_sample(layers_sample=2, budget_s=4.0))
-    v = statistics.median(s["value"] for s in samples)
-    n = CTX + 1
+        cpu_pass(sample)
+    secs = [cpu_pass(sample) for _ in range(args.steps)]
+    bytes_per = layers_sample * 4096 * sample[2]
+    total = sum(secs)
+    v = bytes_per * len(secs) / total / 1e9
+    desc = (f"{layers_sample} of {N_LAYERS} layers at ctx {CTX} (all 8 KV heads) per step, "
+            f"C oracle (OpenMP FP32)")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 2 * 4096 * n / (v * 1e9) * 1e3, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16/f32", "data": "synthetic",
-            "config": {"workload": f"decode sweep, ctx {CTX}, {N_LAYERS} layers, 16q/8kv/128",
-                       "sample": "2 layers per step"},
-            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": samples[0]["cores"],
-                             "kind": "port", "sample": samples[0]["sample"]},
+            "ms_per_step": total / len(secs) * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"decode sweep: {N_LAYERS} layers x ctx {CTX} (+1 new token), "
+                                   f"16q/8kv heads, head_dim 128", "sample": desc},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": desc},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "MLX (the reference's attention backend) is not installable offline; "
                     "the oracle port of its semantics runs on the host cores"}
