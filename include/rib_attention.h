@@ -128,6 +128,24 @@ int rib_decode_attention(const void *q, const void *cache, int cap, int n,
                          void *stream);
 
 /* ------------------------------------------------------------------------ *
+ * Decode attention that allocates nothing (no counterpart in the reference).
+ * Same arguments and results as rib_decode_attention, minus the workspace:
+ * its scratch is a fixed 2 MiB array inside this library's device memory.
+ * For callers that cannot call cudaMalloc or hand over device scratch (a
+ * host whose device memory is owned by another allocator or a hard memory
+ * budget, a binding with no device allocator of its own).
+ *   - Sizes whose scratch (rib_decode_workspace_bytes(1, n, nkv)) exceeds
+ *     2 MiB are rejected with RIB_EINVAL (n <= 258048 keys at 8 KV heads).
+ *   - The first call on a device looks up the array's device address; make
+ *     that first call before any stream capture.
+ *   - Every call clears the array's counters on `stream` and then reuses it:
+ *     calls that overlap on the GPU (other streams, other threads) race.
+ * ------------------------------------------------------------------------ */
+int rib_decode_attention_noalloc(const void *q, const void *cache, int cap,
+                                 int n, int nq, int nkv, float scale,
+                                 void *out, void *stream);
+
+/* ------------------------------------------------------------------------ *
  * Batched ragged decode: B independent sequences, each with its own
  * contiguous per-sequence cache and its own length.  Generalises the
  * single-sequence call above (the reference is batch 1 only, README.md

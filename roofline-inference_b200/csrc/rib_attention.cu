@@ -4,6 +4,7 @@
 // word (common.cuh).
 #include <cmath>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "decode_attention.cuh"
@@ -159,6 +160,33 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   return launch_status("decode_kernel launch");
 }
 
+// ------------------------------------------------------------------ decode, no allocation
+// Scratch of rib_decode_attention_noalloc: a fixed array in the library's own
+// device memory, so that entry point needs no workspace from the caller.
+// Every GPU that loads the library holds it until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_scratch_addr[kMaxDevices];  // device address of the array, per device
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device with cudaGetSymbolAddress.
+void *noalloc_scratch(int dev) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_scratch_addr[dev]) {
+    void *ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr) {
+      rib::host_fail_cuda("cudaGetSymbolAddress(g_noalloc_scratch)", e);
+      return nullptr;
+    }
+    g_noalloc_scratch_addr[dev] = ptr;
+  }
+  return g_noalloc_scratch_addr[dev];
+}
+
 }  // namespace
 
 extern "C" {
@@ -233,6 +261,42 @@ int rib_decode_attention(const void *q, const void *cache, int cap, int n, int n
   p.qscale = scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t *>(out);
   return decode_launch(p, 1, n, workspace, workspace_bytes, stream);
+}
+
+int rib_decode_attention_noalloc(const void *q, const void *cache, int cap, int n, int nq, int nkv,
+                                 float scale, void *out, void *stream) {
+  if (!q || !cache || !out) return RIB_EINVAL;
+  if (nkv < 1 || nq != 2 * nkv || n < 1 || cap < 1 || !(scale > 0.f)) return RIB_EINVAL;
+  if (n > cap) return RIB_ECAPACITY;
+  if (!aligned16(q) || !aligned16(cache) || !aligned16(out)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const DecodeGeometry g = decode_geometry(1, n, nkv);
+  if (g.total > kNoAllocScratchBytes) {
+    snprintf(rib::g_last_error, sizeof(rib::g_last_error),
+             "rib_decode_attention_noalloc: n=%d with %d KV heads needs %zu bytes of scratch, "
+             "more than the %zu-byte static scratch", n, nkv, g.total, kNoAllocScratchBytes);
+    return RIB_EINVAL;
+  }
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return rib::host_fail(RIB_ECUDA, "cudaGetDevice", dev);
+  void *scratch = noalloc_scratch(dev);
+  if (!scratch) return RIB_ECUDA;
+  // The split counters must start at zero; the array keeps whatever the last
+  // call left, so clear them on the caller's stream first.
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, g.counters_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(noalloc counters)", e);
+  rib::decode::Params p = {};
+  p.q = static_cast<const uint16_t *>(q);
+  p.cache = static_cast<const uint16_t *>(cache);
+  p.cache_ptrs = nullptr;
+  p.lens = nullptr;
+  p.n_single = n;
+  p.cap = cap;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t *>(out);
+  return decode_launch(p, 1, n, scratch, kNoAllocScratchBytes, stream);
 }
 
 int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs, const int32_t *lens,
