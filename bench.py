@@ -126,8 +126,8 @@ def load_rib():
 def head_range(rank: int, world: int) -> tuple[int, int]:
     if NKV_TOTAL % world:
         raise SystemExit(f"--gpus must divide {NKV_TOTAL} KV heads")
-    per = NKV_TOTAL // world
-    return rank * per, (rank + 1) * per
+    return importlib.import_module("roofline-inference_b200.sharding").head_range(rank, world,
+                                                                                 NKV_TOTAL)
 
 
 def make_decode_workload(rank: int, world: int, device, ctx: int = CTX, layers: int = N_LAYERS):
@@ -307,7 +307,9 @@ def run_ours(args):
 
     w = make_decode_workload(rank, world, device)
     plan = DecodePlan(rib, w, device)
-    gathered = torch.empty((world,) + tuple(plan.out.shape), dtype=torch.bfloat16, device=device)
+    # all-gather output, concatenated along dim 0: [world * layers, nq_local, 128]
+    gathered = torch.empty((world * plan.out.shape[0],) + tuple(plan.out.shape[1:]),
+                           dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
 
     def step(ev_pair=None):
@@ -407,6 +409,7 @@ def run_e2e(rib, w, rank, world, device, args, gathered):
     norm + RoPE + append (28 launches, new token at position 32768) and one
     layer-batched decode, and read the outputs back to pinned host memory."""
     wl = importlib.import_module("roofline-inference_b200.workloads")
+    sharding = importlib.import_module("roofline-inference_b200.sharding")
     nkv, pos = w["nkv"], w["n"] - 1
     nq = 2 * nkv
     width = (nq + 2 * nkv) * 128
@@ -430,7 +433,7 @@ def run_e2e(rib, w, rank, world, device, args, gathered):
         out = rib.decode_attention_batched(q, caches, lens, 128 ** -0.5, max_n=w["n"])
         if world > 1:
             torch.distributed.all_gather_into_tensor(gathered, out)
-            full = gathered.permute(1, 0, 2, 3).reshape(N_LAYERS, NKV_TOTAL * 2, 128)
+            full = sharding.assemble_heads(gathered.view((world,) + tuple(out.shape)))
         else:
             full = out
         out_host.copy_(full, non_blocking=True)
@@ -495,7 +498,8 @@ def run_prefill(rib, device, args, pk):
 def run_case(case: str):
     """Bounded workloads for ncu captures: decode-small is the layer-batched
     decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
-    prefill-small is causal prefill at L = 4096 (3 launches)."""
+    prefill-small is causal prefill at L = 16384 (128 MB of Q/K/V, above L2;
+    3 launches)."""
     rib = load_rib()
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
@@ -506,7 +510,7 @@ def run_case(case: str):
         for _ in range(3):
             plan.launch()
     else:
-        L = 4096
+        L = 16384
         Q = wl.randn_bf16((16, L, 128), seed=71, device=device)
         K = wl.randn_bf16((1, 8, L, 128), seed=72, device=device)
         V = wl.randn_bf16((1, 8, L, 128), seed=73, device=device)
