@@ -46,6 +46,18 @@ NKV_TOTAL = 8
 PREFILL_L = 32768
 
 
+def decode_traffic_ratio() -> float | None:
+    """DRAM bytes (read + write) per algorithmic KV byte of the decode kernel,
+    from the committed ncu summary of a 4-layer capture; traffic grows with
+    the keys processed, so it scales to any launch of the same kernel."""
+    p = ROOT / "profiles" / "decode_kernel_ctx32k_4layers.md"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if "traffic_per_algorithmic_byte:" in line:
+                return float(line.split("traffic_per_algorithmic_byte:")[1].strip(" `\n"))
+    return None
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -345,6 +357,7 @@ def run_ours(args):
     value = bytes_step_total / (ms * 1e-3) / 1e9
     achieved = bytes_launch_local / (launch_ms * 1e-3) / 1e9
     clk = clocks.summary()
+    ratio = decode_traffic_ratio()
 
     # ---- engine-style: 28 per-layer launches of the same sweep
     for i in range(N_LAYERS):
@@ -385,7 +398,10 @@ def run_ours(args):
                    "kv_bytes_per_step": bytes_step_total},
         "pct_of_hbm_peak": value / pk["hbm_gbs"] / world * 100.0,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None,
+                     "frac": achieved / pk["hbm_gbs"],
+                     "traffic": None if ratio is None else bytes_launch_local * ratio,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                       "profiles/decode_kernel_ctx32k_4layers.md, scaled by keys",
                      "kernel": "rib::decode::decode_kernel",
                      "peak_source": pk["source"] + " hbm_gbs (copy, burst)",
                      "bytes_per_launch": bytes_launch_local, "launch_ms": launch_ms},
