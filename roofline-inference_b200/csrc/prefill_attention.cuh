@@ -9,7 +9,8 @@
 // (attention.py:59), whole masked key tiles skipped (attention.py:87) and
 // heavy query blocks scheduled first (attention.py:26).
 //
-// CTA = 128 query rows x one KV head g (query heads 2g, 2g+1), 10 warps:
+// CTA = 128 query rows x one KV head g (query heads 2g, 2g+1), 12 warps in
+// three warpgroups:
 //   warp 0      TMA producer: Q of both heads once, then K and V tiles of
 //               128 keys into a 2-stage ring (128B-swizzled panels).
 //   warp 1      TMEM owner and MMA issuer (one thread):
@@ -17,8 +18,15 @@
 //                 O_h += P_h V        TS-MMA, A = P_h from TMEM, B = V (MN-major)
 //               issue order PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), so the tensor
 //               pipe works on one head while the other head's softmax runs.
-//   warps 2-5   softmax of head 2g   (one thread per query row / TMEM lane)
-//   warps 6-9   softmax of head 2g+1
+//   warps 2-3   idle
+//   warps 4-7   softmax of head 2g   (one thread per query row / TMEM lane)
+//   warps 8-11  softmax of head 2g+1
+// Registers: launched at 168 per thread; warpgroup 0 gives back to 40
+// (setmaxnreg.dec) and the softmax warpgroups take 232 (setmaxnreg.inc), so a
+// softmax thread holds its whole 128-column score row after one TMEM read.
+// Per SM sub-partition that is 40 + 232 + 232 = 504 <= 512 registers per
+// lane, and 128*40 + 256*232 = 384*168, the launch allocation exactly; the
+// host refuses to launch unless the kernel really was built at 168.
 // TMEM (512 columns): S_0 [0,128), S_1 [128,256) as FP32; P_h is written as
 // packed BF16 over the first 64 columns of S_h; O_0 [256,384), O_1 [384,512).
 // The running max is only raised (and O rescaled) when it grows by more
@@ -39,12 +47,18 @@ constexpr int D = 128;
 constexpr int BM = 128;  // query rows per CTA
 constexpr int BN = 128;  // keys per tile
 constexpr int NS = 2;    // K/V pipeline stages
-constexpr int NWARPS = 10;
+constexpr int NWARPS = 12;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int PANEL_BYTES = 128 * 128;          // [128 rows][64 dims] BF16, one swizzle panel
 constexpr int TILE_BYTES = 2 * PANEL_BYTES;     // [128 rows][128 dims]
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
+constexpr int kLaunchRegs = 168;                 // registers per thread at launch
+constexpr int kRegsLow = 40;                     // warpgroup 0 after setmaxnreg.dec
+constexpr int kRegsHigh = 232;                   // softmax warpgroups after setmaxnreg.inc
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= NTHREADS * kLaunchRegs,
+              "register split exceeds the launch allocation");
+static_assert(kRegsLow + 2 * kRegsHigh <= 512, "register split exceeds one sub-partition");
 
 // Instruction descriptor, kind::f16: D = F32 (bits 4-5 = 1), A = B = BF16
 // (bits 7-9, 10-12 = 1), N >> 3 at bits 17-22, M >> 4 at bits 24-28;
@@ -89,6 +103,31 @@ __device__ __forceinline__ bool aborted(const Smem &s) {
 }
 __device__ __forceinline__ void set_abort(Smem &s) {
   *reinterpret_cast<volatile int *>(&s.abort_flag) = 1;
+}
+
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ uint64_t pack2u(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+__device__ __forceinline__ void unpack2f(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// Two FP32 lanes per instruction (sm_100 packed FP32).
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 // Causal / length mask of 32 score columns starting at key `key0`.
@@ -150,6 +189,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
+  if (warp < 4) {
+    // warpgroup 0: producer, MMA issuer, two idle warps
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -236,9 +278,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
       mbar_wait(&s.mma_done, 0);
     }
     __syncwarp();
+  }
   } else {
+    // warpgroups 1 and 2: softmax
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax
-    const int h = (warp - 2) >> 2;           // 0 for warps 2-5, 1 for warps 6-9
+    const int h = (warp - 4) >> 2;           // 0 for warps 4-7, 1 for warps 8-11
     const int quad = warp & 3;               // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;        // query row within the block
     const int q_row = q0 + row;
@@ -247,25 +292,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
     const uint32_t tS = lane_base + h * 128;
     const uint32_t tO = lane_base + 256 + h * 128;
     const float sl2 = p.scale_log2;
+    const uint64_t sl2x2 = pack2f(sl2, sl2);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       if (!(ok = warp_wait(s, &s.s_full[h], j & 1))) break;
       tc_fence_after();
       const int k0 = j * BN;
-      const bool masked = k0 + BN - 1 > p.off + q0 || k0 + BN > p.kL;  // crosses diagonal or kL
-      // pass 1: row maximum over the tile, 32 columns at a time
-      float mx = -INFINITY;
+      uint32_t r[BN];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
-        tmem_wait_ld();
-        if (masked) mask_chunk(r, k0 + c * 32, my_last, p.kL);
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+      tmem_wait_ld();
+      if (k0 + BN - 1 > p.off + q0 || k0 + BN > p.kL) {  // tile crosses the diagonal or kL
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+        for (int c = 0; c < 4; ++c)
+          mask_chunk(*reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]), k0 + c * 32, my_last, p.kL);
       }
-      const float mt = mx * sl2;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < BN; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(r[c]));
+      const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * sl2;
       const bool need = mt > m + kRescaleThreshold;
       if (__any_sync(0xffffffffu, need)) {
         const float mn = fmaxf(m, mt);
@@ -286,30 +332,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
         }
         m = mn;
       }
-      // pass 2: P = exp2(S * scale*log2e - m) as packed BF16 over S's first
-      // 64 columns; S columns [32h', 32h'+64) are read before P half h' lands.
-      float sum = 0.f;
+      // P = exp2(S * scale*log2e - m), packed BF16 over S's first 64 columns
+      // (the whole row is already in registers).
+      const uint64_t nm2 = pack2f(-m, -m);
+      uint64_t acc0 = pack2f(0.f, 0.f), acc1 = acc0;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t pk[32];
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = half * 2 + cc;
-          uint32_t r[32];
-          tmem_ld32(tS + c * 32, r);
-          tmem_wait_ld();
-          if (masked) mask_chunk(r, k0 + c * 32, my_last, p.kL);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(r[2 * e]), sl2, -m));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(r[2 * e + 1]), sl2, -m));
-            sum += p0 + p1;
-            pk[cc * 16 + e] = pack_bf16x2(p0, p1);
-          }
+        for (int e = 0; e < 32; ++e) {
+          const int c = half * 64 + 2 * e;
+          float a, b;
+          unpack2f(ffma2(pack2u(r[c], r[c + 1]), sl2x2, nm2), a, b);
+          a = fast_exp2(a);
+          b = fast_exp2(b);
+          if (e & 1) acc1 = fadd2(acc1, pack2f(a, b));
+          else acc0 = fadd2(acc0, pack2f(a, b));
+          pk[e] = pack_bf16x2(a, b);
         }
         tmem_st32(tS + half * 32, pk);
       }
-      l += sum;
+      float s0, s1, s2, s3;
+      unpack2f(acc0, s0, s1);
+      unpack2f(acc1, s2, s3);
+      l += (s0 + s1) + (s2 + s3);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&s.p_full[h]);
@@ -318,23 +364,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
     if (ok && warp_wait(s, &s.o_full[h], (nt - 1) & 1)) {
       tc_fence_after();
       const float inv_l = 1.f / l;
-      uint16_t *dst = p.out + static_cast<size_t>(q_row) * (p.H * D) + (2 * g + h) * D;
+      uint32_t o[D];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_wait_ld();
-        if (q_row < p.qL) {
-          uint4 *d4 = reinterpret_cast<uint4 *>(dst + c * 32);
+      for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&o[c * 32]));
+      tmem_wait_ld();
+      if (q_row < p.qL) {
+        uint4 *d4 = reinterpret_cast<uint4 *>(p.out + static_cast<size_t>(q_row) * (p.H * D) + (2 * g + h) * D);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-            w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-            w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-            w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-            d4[v] = w;
-          }
+        for (int v = 0; v < D / 8; ++v) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+          w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+          w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+          w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+          d4[v] = w;
         }
       }
     }
@@ -423,11 +466,13 @@ inline int launch(const void *Q, const void *K, const void *V, int qL, int kL, i
     cudaFuncAttributes fa;
     e = cudaFuncGetAttributes(&fa, prefill_kernel);
     if (e != cudaSuccess) return host_fail_cuda("cudaFuncGetAttributes(prefill)", e);
-    if (fa.maxThreadsPerBlock < NTHREADS || fa.maxDynamicSharedSizeBytes < smem) {
+    if (fa.numRegs != kLaunchRegs || fa.maxThreadsPerBlock < NTHREADS ||
+        fa.maxDynamicSharedSizeBytes < smem) {
       snprintf(g_last_error, sizeof(g_last_error),
-               "prefill_kernel cannot launch: %d registers/thread, max %d threads/block (need %d), "
-               "max dynamic smem %d (need %d)",
-               fa.numRegs, fa.maxThreadsPerBlock, NTHREADS, fa.maxDynamicSharedSizeBytes, smem);
+               "prefill_kernel not launched: %d registers/thread (register split needs exactly %d), "
+               "max %d threads/block (need %d), max dynamic smem %d (need %d)",
+               fa.numRegs, kLaunchRegs, fa.maxThreadsPerBlock, NTHREADS,
+               fa.maxDynamicSharedSizeBytes, smem);
       return RIB_ECUDA;
     }
     g_smem_done[dev] = true;
