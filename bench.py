@@ -412,6 +412,21 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "clocks": clk,
     }
+    rl = importlib.import_module("roofline-inference_b200.roofline_line")
+    dline = rl.decode_attention_line(w["n"])
+    line["reference_line"] = {
+        "model": "Level-A bound max(FLOPs/P, bytes/B, exps/rate), configs/b200.yaml "
+                 "(measured peaks), attention only, cold start",
+        "decode_sweep": {"time_s": dline["time_s"] / world, "bottleneck": dline["bottleneck"],
+                         "measured_s": ms * 1e-3,
+                         "fraction": dline["time_s"] / world / (ms * 1e-3)},
+    }
+    if prefill and "ms" in prefill:
+        pline = rl.prefill_attention_line(PREFILL_L)
+        line["reference_line"]["prefill_32k"] = {
+            "time_s": pline["time_s"], "bottleneck": pline["bottleneck"],
+            "measured_s": prefill["ms"] * 1e-3,
+            "fraction": pline["time_s"] / (prefill["ms"] * 1e-3)}
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_decode_sample()
     print(json.dumps(line), flush=True)

@@ -1,0 +1,80 @@
+"""Level-A reference lines for the attention scenarios on B200.
+
+Restates the reference's calibrated resource bound
+    T >= max(FLOPs / P_peak, DRAM bytes / B, exp count / exp rate)
+(src/roofline/bound.py:96-145, README.md:76-84) for the attention-only
+workloads this repository measures, using configs/b200.yaml, which follows
+the reference's device-spec schema (src/roofline/device.py:102-130).  Each
+measured number is reported as a fraction of the line: line time / measured
+time (1.0 = at the bound).
+
+Counts follow src/roofline/workload.py:
+  decode   one new token per sequence attends n keys: FLOPs 2*H*d*(keys +
+           values) per layer (workload.py:149), KV bytes 2*nkv*d*2 per key
+           (workload.py:156), one exp per score; q in and o out are added.
+  prefill  causal, pairs = qL*off + qL(qL+1)/2: FLOPs 4*H*d*pairs
+           (workload.py:176-179), one exp per score; Q, K, V read and O
+           written once (the resident-input credit is 0: a cold start,
+           bound.py:96-105 with initial_resident_bytes=0).
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import yaml
+
+SPEC = Path(__file__).resolve().parent / "configs" / "b200.yaml"
+
+
+def _eff(q: dict) -> float:
+    """Quantity.effective (device.py:24-26): measured overrides value."""
+    return float(q["measured"]) if q.get("measured") is not None else float(q["value"])
+
+
+def load_spec(path: str | Path = SPEC) -> dict:
+    data = yaml.safe_load(Path(path).read_text())
+    gpu = data["engines"]["gpu"]
+    return {
+        "name": data["name"],
+        "bf16": _eff(gpu["compute"]["bf16"]),
+        "bf16_datasheet": float(gpu["compute"]["bf16"]["value"]),
+        "bandwidth": min(_eff(gpu["bandwidth"]), _eff(data["memory"]["total_bandwidth"])),
+        "bandwidth_datasheet": float(gpu["bandwidth"]["value"]),
+        "exp": _eff(gpu["special"]["exp"]),
+    }
+
+
+def _line(flops: float, dram_bytes: float, exps: float, spec: dict) -> dict:
+    res = {"compute": flops / spec["bf16"], "dram_bandwidth": dram_bytes / spec["bandwidth"],
+           "exp": exps / spec["exp"]}
+    t = max(res.values())
+    return {"time_s": t, "bottleneck": max(res, key=res.get), "resource_time_s": res,
+            "flops": flops, "dram_bytes": dram_bytes, "exps": exps,
+            "device": spec["name"]}
+
+
+def decode_attention_line(n_keys: int, layers: int = 28, batch: int = 1, nq: int = 16,
+                          nkv: int = 8, head_dim: int = 128, spec: dict | None = None) -> dict:
+    """Decode attention over `n_keys` keys (new token included) per layer."""
+    spec = spec or load_spec()
+    flops = 2 * layers * nq * head_dim * (n_keys + n_keys) * batch
+    kv = layers * batch * 2 * nkv * head_dim * 2 * n_keys
+    qo = layers * batch * 2 * nq * head_dim * 2
+    exps = layers * batch * nq * n_keys
+    return _line(flops, kv + qo, exps, spec)
+
+
+def prefill_attention_line(qL: int, kL: int | None = None, nq: int = 16, nkv: int = 8,
+                           head_dim: int = 128, spec: dict | None = None) -> dict:
+    """Causal prefill attention of one layer."""
+    spec = spec or load_spec()
+    kL = qL if kL is None else kL
+    pairs = qL * (kL - qL) + qL * (qL + 1) // 2
+    flops = 4 * nq * head_dim * pairs
+    dram = 2 * head_dim * (2 * nq * qL + 2 * nkv * kL)  # Q in, O out, K and V in
+    return _line(flops, dram, nq * pairs, spec)
+
+
+def fraction(line: dict, measured_s: float) -> float:
+    """Line time / measured time: 1.0 means the measurement sits on the bound."""
+    return line["time_s"] / measured_s
