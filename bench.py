@@ -7,9 +7,11 @@ N(0,1) caches, 16 q heads / 8 KV heads / head_dim 128, one new token attending
 to 32769 keys per layer.  A step decodes all 28 layers in one layer-batched
 launch of the split-KV kernel (the layers are independent, so one launch does
 the same work as 28 and does not pay 28 launch latencies).  With N GPUs the
-8 KV heads are sharded (8/N per rank, no cross-rank softmax) and the head
-outputs are all-gathered over NCCL inside the step.  Metric: algorithmic KV
-bytes (4096 B per key per layer) / step time, whole job.
+8 KV heads are sharded (8/N per rank, no cross-rank softmax) and the decode
+kernel itself stores each head output into every rank's buffer over NVLink
+(nvlink_gather.py), so the step is one launch; decode + an NCCL all-gather
+is timed beside it as the baseline.  Metric: algorithmic KV bytes (4096 B
+per key per layer) / step time, whole job.
 
 Also reported: the same sweep as 28 per-layer launches (engine-style), the
 causal prefill attention TFLOP/s at L = 32768 (tcgen05 kernel), the end-to-end
@@ -324,14 +326,20 @@ def run_ours(args):
                            dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
 
+    gather = None
+    if world > 1:  # decode fused with the NVLink all-gather of head outputs
+        gather = importlib.import_module("roofline-inference_b200.nvlink_gather").NVLinkGather(
+            N_LAYERS, 2 * w["nkv"], device)
+
     def step(ev_pair=None):
         if ev_pair is not None:
             ev_pair[0].record(stream)
-        plan.launch()
+        if gather is not None:
+            gather.decode(w["q"], plan.ptrs, plan.lens, w["n"], w["cap"], plan.scale, plan.ws)
+        else:
+            plan.launch()
         if ev_pair is not None:
             ev_pair[1].record(stream)
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(gathered, plan.out)
 
     for _ in range(args.warmup):
         step()
@@ -359,6 +367,27 @@ def run_ours(args):
     clk = clocks.summary()
     ratio = decode_traffic_ratio()
 
+    # ---- N > 1 baseline: the same step as decode + a separate NCCL all-gather
+    nccl = None
+    if world > 1:
+        def nccl_step():
+            plan.launch()
+            torch.distributed.all_gather_into_tensor(gathered, plan.out)
+        for _ in range(args.warmup):
+            nccl_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(args.steps):
+            nccl_step()
+        b0.record(stream)
+        torch.cuda.synchronize()
+        nccl_ms = max_over_ranks(a0.elapsed_time(b0) / args.steps, world, device)
+        nccl = {"value": bytes_step_total / (nccl_ms * 1e-3) / 1e9, "unit": "GB/s",
+                "ms_per_step": nccl_ms,
+                "path": "decode kernel + torch.distributed.all_gather_into_tensor (NCCL)"}
+
     # ---- engine-style: 28 per-layer launches of the same sweep
     for i in range(N_LAYERS):
         plan.launch_layer(i)
@@ -374,11 +403,14 @@ def run_ours(args):
     per_layer_gbs = bytes_launch_local / (per_layer_ms * 1e-3) / 1e9
 
     # ---- end to end through the public API with host buffers
-    e2e = run_e2e(rib, w, rank, world, device, args, gathered)
+    e2e = run_e2e(rib, w, rank, world, device, args, gather, plan)
 
     # ---- prefill (tcgen05 kernel), one GPU's view
     prefill = run_prefill(rib, device, args, pk) if not args.no_prefill else None
 
+    device_status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
+    if gather is not None:
+        gather.close()
     if rank != 0:
         if world > 1:
             torch.distributed.destroy_process_group()
@@ -392,8 +424,9 @@ def run_ours(args):
                                f"16q/8kv heads, head_dim 128, independent seeded BF16 N(0,1) "
                                f"caches",
                    "launch": "layer-batched (one decode launch per step for all 28 layers)",
-                   "parallelism": f"kv-head shard x{world}" + (", NCCL all-gather" if world > 1
-                                                               else ""),
+                   "parallelism": f"kv-head shard x{world}" + (
+                       ", all-gather fused into the decode kernel (NVLink peer stores)"
+                       if world > 1 else ""),
                    "l2": f"inputs {bytes_step_total / 1e9:.2f} GB per step > 126 MB L2, no flush",
                    "kv_bytes_per_step": bytes_step_total},
         "pct_of_hbm_peak": value / pk["hbm_gbs"] / world * 100.0,
@@ -405,11 +438,13 @@ def run_ours(args):
                      "kernel": "rib::decode::decode_kernel",
                      "peak_source": pk["source"] + " hbm_gbs (copy, burst)",
                      "bytes_per_launch": bytes_launch_local, "launch_ms": launch_ms},
+        "nccl_allgather_baseline": nccl,
         "per_layer_launches": {"value": per_layer_gbs, "unit": "GB/s", "ms_per_step": per_layer_ms,
                                "frac": per_layer_gbs / pk["hbm_gbs"]},
         "prefill": prefill,
         "e2e": e2e,
         "gpu_launches": args.steps,
+        "device_status": device_status,
         "clocks": clk,
     }
     rl = importlib.import_module("roofline-inference_b200.roofline_line")
@@ -434,13 +469,12 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
-def run_e2e(rib, w, rank, world, device, args, gathered):
+def run_e2e(rib, w, rank, world, device, args, gather, plan):
     """Same sweep through the public API: per step, copy the 28 layers' qkv
     rows of the new token from pinned host memory, run the fused
     norm + RoPE + append (28 launches, new token at position 32768) and one
     layer-batched decode, and read the outputs back to pinned host memory."""
     wl = importlib.import_module("roofline-inference_b200.workloads")
-    sharding = importlib.import_module("roofline-inference_b200.sharding")
     nkv, pos = w["nkv"], w["n"] - 1
     nq = 2 * nkv
     width = (nq + 2 * nkv) * 128
@@ -461,12 +495,10 @@ def run_e2e(rib, w, rank, world, device, args, gathered):
         qs = [rib.qk_norm_rope_append(qkv_dev[i], qw, kw, pos, nq, nkv, 1e6, caches[i])
               for i in range(N_LAYERS)]
         q = torch.stack([x.reshape(nq, 128) for x in qs])
-        out = rib.decode_attention_batched(q, caches, lens, 128 ** -0.5, max_n=w["n"])
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(gathered, out)
-            full = sharding.assemble_heads(gathered.view((world,) + tuple(out.shape)))
+        if gather is not None:
+            full = gather.decode(q, plan.ptrs, lens, w["n"], w["cap"], 128 ** -0.5, plan.ws)
         else:
-            full = out
+            full = rib.decode_attention_batched(q, caches, lens, 128 ** -0.5, max_n=w["n"])
         out_host.copy_(full, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -485,7 +517,8 @@ def run_e2e(rib, w, rank, world, device, args, gathered):
             "h2d_bytes_per_step": qkv_host.numel() * 2,
             "d2h_bytes_per_step": out_host.numel() * 2,
             "gpu_launches_per_step": launches,
-            "path": "qk_norm_rope_append x28 + decode_attention_batched (public API)"}
+            "path": "qk_norm_rope_append x28 + decode_attention_batched (public API)"
+                    + ("; NVLinkGather.decode (fused all-gather) at N > 1" if world > 1 else "")}
 
 
 def run_prefill(rib, device, args, pk):

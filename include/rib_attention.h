@@ -165,6 +165,51 @@ int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs,
                                  size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ *
+ * Decode attention fused with the all-gather of head outputs over NVLink.
+ * The KV heads of a model are sharded over the ranks of one node (rank r of
+ * `world` owns nkv = 8/world of them and query heads 2h, 2h+1); this call
+ * runs the batched decode above for the local heads and stores each finished
+ * output straight into every rank's gathered buffer (peer stores through
+ * CUDA IPC mappings), then exchanges an epoch flag with every peer.  When it
+ * completes on `stream`, this rank's buffer holds all ranks' outputs.  It
+ * replaces the decode SDPA (engine.py:155) plus the NCCL all-gather a
+ * head-sharded engine would need (the reference is single-GPU).
+ *   Gathered layout: region (epoch & 1) of each buffer,
+ *     [batch][world * nq][128] BF16, rank r's heads at [r*nq, (r+1)*nq).
+ *   Signal slots: 8 uint64 after the two regions; slot s holds the last
+ *     epoch rank s published.  Buffers start zeroed.
+ *   epoch: 1 for the first call, +1 per call, the same on every rank.
+ * Every rank must make the call with the same epoch; a rank that does not
+ * arrive within 2 s makes the others record RIB_ETIMEOUT and return.
+ * Setup: rib_peer_buffer_alloc on each rank, exchange the 64-byte IPC
+ * handles (e.g. torch.distributed all_gather_object), rib_peer_buffer_open
+ * the peers' handles; tear down with rib_peer_buffer_close / _free.
+ * ------------------------------------------------------------------------ */
+#define RIB_MAX_PEERS 8
+
+typedef struct rib_peer_gather {
+  int world;                       /* ranks in the gather, 1..8             */
+  int rank;                        /* this rank                             */
+  uint64_t out[RIB_MAX_PEERS];     /* per rank: buffer base, as mapped here */
+  uint64_t sig[RIB_MAX_PEERS];     /* per rank: address of its signal slots */
+  size_t region_bytes;             /* bytes of one output region            */
+} rib_peer_gather;
+
+size_t rib_peer_buffer_bytes(int batch, int nq_total);
+int rib_peer_buffer_alloc(int device, size_t bytes, void **dev_ptr,
+                          void *ipc_handle /* 64 bytes out */);
+int rib_peer_buffer_open(int device, const void *ipc_handle, void **peer_ptr);
+int rib_peer_buffer_close(int device, void *peer_ptr);
+int rib_peer_buffer_free(int device, void *dev_ptr);
+
+int rib_decode_attention_gather(const void *q, const uint64_t *cache_ptrs,
+                                const int32_t *lens, int batch, int max_n,
+                                int cap, int nq, int nkv, float scale,
+                                const rib_peer_gather *g,
+                                unsigned long long epoch, void *workspace,
+                                size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ *
  * Causal GQA prefill attention (tcgen05 / TMEM flash attention).
  * Replaces attention(Q, K, V, qL, kL, scale, ...) (agent-test/v2/attention.py
  * :177-185, Metal source attention.py:18-166).

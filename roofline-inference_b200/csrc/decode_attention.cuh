@@ -41,6 +41,7 @@ constexpr int SPW = 2;                 // ring slots owned by each consumer warp
 constexpr int STAGES = NCW * SPW;      // ring depth
 constexpr int NTHREADS = (NCW + 1) * 32;
 constexpr int ROW_BYTES = D * 2;       // one key row, BF16
+constexpr int kMaxPeers = 8;           // ranks of one NVLink all-gather
 constexpr int TILE_BYTES = TK * ROW_BYTES;
 
 struct Smem {
@@ -70,7 +71,72 @@ struct Params {
   float *part_ml;              // [B][nkv][max_splits][2][2]  (m, l)
   float *part_o;               // [B][nkv][max_splits][2][128]
   int *counters;               // [B][nkv]
+  // All-gather over NVLink (world > 0): the outputs of this rank's heads go
+  // straight into every rank's gathered buffer instead of `out`.
+  int world, rank, nq_total;
+  uint16_t *gout[kMaxPeers];              // per rank: output region of this call
+  unsigned long long *gsig[kMaxPeers];    // per rank: signal slots [kMaxPeers]
+  unsigned long long epoch;               // > 0, increases by one per call
+  int *done;                              // units finalised in this call
+  int total_units;
 };
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *addr, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *addr) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Final outputs of one (sequence, KV head) unit: res[hh] is dim `tid` of
+// query head 2h + hh.  Without gather they go to `out`.  With gather every
+// rank's buffer receives them (plain peer stores over NVLink); the rank's
+// last unit then publishes the call's epoch to every peer and waits, bounded,
+// until every peer's epoch has arrived, so when the kernel ends this rank's
+// buffer holds the outputs of all ranks.
+__device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int tid,
+                                              const float (&res)[2], int &flag) {
+  if (p.world == 0) {
+    if (tid < D) {
+      uint16_t *outp = p.out + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) outp[hh * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(res[hh]));
+    }
+    return;
+  }
+  if (tid < D) {
+    const size_t row = static_cast<size_t>(b) * p.nq_total + p.rank * p.nq + 2 * h;
+    for (int r = 0; r < p.world; ++r) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        p.gout[r][(row + hh) * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(res[hh]));
+    }
+    __threadfence_system();
+  }
+  __syncthreads();
+  if (tid == 0) flag = (atomicAdd(p.done, 1) == p.total_units - 1);
+  __syncthreads();
+  if (!flag) return;
+  // last unit of this rank: signal every peer, then wait for every peer
+  __threadfence_system();
+  if (tid < p.world) st_release_sys(p.gsig[tid] + p.rank, p.epoch);
+  if (tid < p.world) {
+    const unsigned long long *slot = p.gsig[p.rank] + tid;
+    if (ld_acquire_sys(slot) < p.epoch) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(slot) < p.epoch) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_timeout();
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) *p.done = 0;  // ready for the next call
+}
 
 __device__ __forceinline__ void unpack8(const uint4 &r, float *f) {
   f[0] = bf16lo(r.x); f[1] = bf16hi(r.x);
@@ -300,13 +366,13 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
       Ox[hh] = O;
     }
   }
-  uint16_t *outp = p.out + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
+  float res[2] = {0.f, 0.f};
   if (nsplit == 1) {
     if (tid < D) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-        outp[hh * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(Ox[hh] / Lx[hh]));
+      for (int hh = 0; hh < 2; ++hh) res[hh] = Ox[hh] / Lx[hh];
     }
+    finalize_unit(p, b, h, tid, res, s.is_last);
     return;
   }
   const size_t unit = static_cast<size_t>(b) * p.nkv + h;
@@ -343,10 +409,12 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
         L = fmaf(__ldcg(&p.part_ml[pi * 2 + 1]), f, L);
         O = fmaf(__ldcg(&p.part_o[pi * D + tid]), f, O);
       }
-      outp[hh * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(O / L));
+      res[hh] = O / L;
     }
   }
   if (tid == 0) p.counters[unit] = 0;  // leave the workspace ready for the next call
+  __syncthreads();
+  finalize_unit(p, b, h, tid, res, s.is_last);
 }
 
 }  // namespace decode

@@ -4,6 +4,7 @@
 // word (common.cuh).
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -129,7 +130,8 @@ DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
   g.chunk = chunk;
   g.max_splits = ceil_div(max_n, chunk);
   const size_t units = static_cast<size_t>(batch) * nkv;
-  g.counters_bytes = ((units * sizeof(int) + 255) / 256) * 256;
+  // per-unit split counters, then one counter of units finalised (all-gather)
+  g.counters_bytes = (((units + 1) * sizeof(int) + 255) / 256) * 256;
   g.ml_bytes = ((units * g.max_splits * 2 * 2 * sizeof(float) + 255) / 256) * 256;
   g.o_bytes = units * g.max_splits * 2 * D * sizeof(float);
   g.total = g.counters_bytes + g.ml_bytes + g.o_bytes;
@@ -147,6 +149,7 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   if (!aligned16(workspace)) return RIB_EALIGN;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
   p.counters = reinterpret_cast<int *>(ws);
+  p.done = p.counters + static_cast<size_t>(batch) * p.nkv;
   p.part_ml = reinterpret_cast<float *>(ws + g.counters_bytes);
   p.part_o = reinterpret_cast<float *>(ws + g.counters_bytes + g.ml_bytes);
   p.chunk = g.chunk;
@@ -297,6 +300,90 @@ int rib_decode_attention_noalloc(const void *q, const void *cache, int cap, int 
   p.qscale = scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t *>(out);
   return decode_launch(p, 1, n, scratch, kNoAllocScratchBytes, stream);
+}
+
+size_t rib_peer_buffer_bytes(int batch, int nq_total) {
+  if (batch < 1 || nq_total < 1) return 0;
+  const size_t region = ((static_cast<size_t>(batch) * nq_total * 128 * 2 + 255) / 256) * 256;
+  return 2 * region + 256;  // two output regions, then the signal slots
+}
+
+int rib_peer_buffer_alloc(int device, size_t bytes, void **dev_ptr, void *ipc_handle) {
+  if (!dev_ptr || !ipc_handle || bytes == 0) return RIB_EINVAL;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaSetDevice", e);
+  void *ptr = nullptr;
+  if ((e = cudaMalloc(&ptr, bytes)) != cudaSuccess) return rib::host_fail_cuda("cudaMalloc(peer buffer)", e);
+  if ((e = cudaMemset(ptr, 0, bytes)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+    cudaFree(ptr);
+    return rib::host_fail_cuda("cudaMemset(peer buffer)", e);
+  }
+  if ((e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t *>(ipc_handle), ptr)) != cudaSuccess) {
+    cudaFree(ptr);
+    return rib::host_fail_cuda("cudaIpcGetMemHandle", e);
+  }
+  *dev_ptr = ptr;
+  return RIB_OK;
+}
+
+int rib_peer_buffer_open(int device, const void *ipc_handle, void **peer_ptr) {
+  if (!ipc_handle || !peer_ptr) return RIB_EINVAL;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaSetDevice", e);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  if ((e = cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess)
+    return rib::host_fail_cuda("cudaIpcOpenMemHandle", e);
+  return RIB_OK;
+}
+
+int rib_peer_buffer_close(int device, void *peer_ptr) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaIpcCloseMemHandle(peer_ptr);
+  return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda("cudaIpcCloseMemHandle", e);
+}
+
+int rib_peer_buffer_free(int device, void *dev_ptr) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda("cudaFree(peer buffer)", e);
+}
+
+int rib_decode_attention_gather(const void *q, const uint64_t *cache_ptrs, const int32_t *lens,
+                                int batch, int max_n, int cap, int nq, int nkv, float scale,
+                                const rib_peer_gather *g, unsigned long long epoch,
+                                void *workspace, size_t workspace_bytes, void *stream) {
+  if (!q || !cache_ptrs || !lens || !g) return RIB_EINVAL;
+  if (batch < 1 || nkv < 1 || nq != 2 * nkv || max_n < 1 || cap < 1 || !(scale > 0.f))
+    return RIB_EINVAL;
+  if (g->world < 1 || g->world > RIB_MAX_PEERS || g->rank < 0 || g->rank >= g->world || epoch == 0)
+    return RIB_EINVAL;
+  if (g->region_bytes < static_cast<size_t>(batch) * g->world * nq * 128 * 2) return RIB_EINVAL;
+  if (max_n > cap) return RIB_ECAPACITY;
+  if (!aligned16(q) || (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) ||
+      (reinterpret_cast<uintptr_t>(lens) & 3u))
+    return RIB_EALIGN;
+  rib::decode::Params p = {};
+  for (int r = 0; r < g->world; ++r) {
+    if (!g->out[r] || !g->sig[r] || (g->out[r] & 15u) || (g->sig[r] & 7u)) return RIB_EALIGN;
+    p.gout[r] = reinterpret_cast<uint16_t *>(g->out[r] + (epoch & 1ull) * g->region_bytes);
+    p.gsig[r] = reinterpret_cast<unsigned long long *>(g->sig[r]);
+  }
+  p.q = static_cast<const uint16_t *>(q);
+  p.cache = nullptr;
+  p.cache_ptrs = cache_ptrs;
+  p.lens = lens;
+  p.cap = cap;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = nullptr;
+  p.world = g->world;
+  p.rank = g->rank;
+  p.nq_total = g->world * nq;
+  p.epoch = epoch;
+  p.total_units = batch * nkv;
+  return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
 }
 
 int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs, const int32_t *lens,

@@ -1,0 +1,96 @@
+"""GPU, 2 ranks (one process per GPU, NCCL for set-up only): decode attention
+fused with the NVLink all-gather, against the oracle on all 8 heads.
+
+Each rank owns 4 of the 8 KV heads of a 4-layer, 4096-context sweep, runs
+three calls (epochs 1-3, both output regions) with different queries, and
+checks that its gathered buffer holds every rank's heads within the decode
+tolerance.  Skips unless two GPUs are visible."""
+from __future__ import annotations
+
+import datetime
+import importlib
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+LAYERS, CTX = 4, 4096
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q_out):
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                             timeout=datetime.timedelta(seconds=60))
+        from oracle import oracle
+        rib = importlib.import_module("roofline-inference_b200")
+        wl = importlib.import_module("roofline-inference_b200.workloads")
+        sh = importlib.import_module("roofline-inference_b200.sharding")
+        ng = importlib.import_module("roofline-inference_b200.nvlink_gather")
+        h0, h1 = sh.head_range(rank, world)
+        nkv = h1 - h0
+        n = CTX + 1
+        cap = wl.round_cap(n)
+        full = wl.randn_bf16((LAYERS, 2, 8, cap, 128), seed=77)       # same on every rank
+        caches = full[:, :, h0:h1].contiguous().to(dev)
+        stride = caches[0].numel() * 2
+        ptrs = torch.tensor([caches.data_ptr() + i * stride for i in range(LAYERS)],
+                            dtype=torch.int64, device=dev)
+        lens = torch.full((LAYERS,), n, dtype=torch.int32, device=dev)
+        L = rib.load_library()
+        ws = torch.zeros(L.rib_decode_workspace_bytes(LAYERS, n, nkv), dtype=torch.uint8, device=dev)
+        G = ng.NVLinkGather(LAYERS, 2 * nkv, dev)
+        u16 = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        worst = 0.0
+        for call in range(3):
+            q_full = wl.randn_bf16((LAYERS, 16, 128), seed=100 + call)
+            out = G.decode(q_full[:, 2 * h0:2 * h1].contiguous().to(dev), ptrs, lens, n, cap,
+                           wl.SCALE, ws)
+            torch.cuda.synchronize(dev)
+            got = out.float().cpu().numpy()
+            of, _ = oracle.decode_attention_batched(u16(q_full), [u16(full[i]) for i in range(LAYERS)],
+                                                    [n] * LAYERS, wl.SCALE)
+            d = np.abs(got - of)
+            assert d.max() <= 2e-2 and d.mean() <= 2e-3, (call, d.max(), d.mean())
+            worst = max(worst, float(d.max()))
+        status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
+        G.close()
+        torch.distributed.destroy_process_group()
+        q_out.put((rank, (worst, status)))
+    except Exception as e:  # report to the parent
+        q_out.put((rank, repr(e)))
+
+
+def test_decode_nvlink_gather_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert not isinstance(v, str), f"rank {r}: {v}"
+        assert v[1] == 0, f"rank {r}: device status {v[1]}"
