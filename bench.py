@@ -405,6 +405,9 @@ def run_ours(args):
     # ---- end to end through the public API with host buffers
     e2e = run_e2e(rib, w, rank, world, device, args, gather, plan)
 
+    # ---- batched ragged decode (64 sequences), sequence-sharded
+    ragged = run_ragged(rib, rank, world, device, args, pk)
+
     # ---- prefill (tcgen05 kernel), one GPU's view
     prefill = run_prefill(rib, device, args, pk) if not args.no_prefill else None
 
@@ -442,6 +445,7 @@ def run_ours(args):
         "per_layer_launches": {"value": per_layer_gbs, "unit": "GB/s", "ms_per_step": per_layer_ms,
                                "frac": per_layer_gbs / pk["hbm_gbs"]},
         "prefill": prefill,
+        "ragged_batch": ragged,
         "e2e": e2e,
         "gpu_launches": args.steps,
         "device_status": device_status,
@@ -467,6 +471,75 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def run_ragged(rib, rank, world, device, args, pk):
+    """Batched ragged decode: 64 sequences, contexts U[512, 32768] (seeded),
+    one contiguous cache each, one new token each.  Sequences are balanced
+    over the ranks by total context (LPT); at N > 1 every rank's outputs
+    reach every rank through the decode kernel's NVLink stores (all 16 heads
+    per rank, one slot per sequence).  Metric: KV bytes / step time."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    sh = importlib.import_module("roofline-inference_b200.sharding")
+    lens = wl.ragged_lengths(64, 512, 32768, seed=0)
+    assign = sh.balance_sequences(lens, world)
+    slots = sh.slots_per_rank(assign)
+    mine = assign[rank]
+    cap = wl.round_cap(max(lens))
+    pool = torch.zeros((slots, 2, NKV_TOTAL, cap, 128), dtype=torch.bfloat16, device=device)
+    q = torch.zeros((slots, 16, 128), dtype=torch.bfloat16, device=device)
+    my_lens = []
+    for j, i in enumerate(mine):
+        pool[j, :, :, :lens[i]] = wl.randn_bf16((2, NKV_TOTAL, lens[i], 128), seed=1000 + i,
+                                                device=device)
+        q[j] = wl.randn_bf16((16, 128), seed=2000 + i, device=device)
+        my_lens.append(lens[i])
+    my_lens += [1] * (slots - len(mine))  # padding slots: one key, output ignored
+    L = rib.load_library()
+    stride = pool[0].numel() * 2
+    ptrs = torch.tensor([pool.data_ptr() + j * stride for j in range(slots)], dtype=torch.int64,
+                        device=device)
+    lens_d = torch.tensor(my_lens, dtype=torch.int32, device=device)
+    max_n = max(my_lens)
+    ws = torch.zeros(L.rib_decode_workspace_bytes(slots, max_n, NKV_TOTAL), dtype=torch.uint8,
+                     device=device)
+    out = torch.empty((slots, 16, 128), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+    gather = None
+    if world > 1:
+        gather = importlib.import_module("roofline-inference_b200.nvlink_gather").NVLinkGather(
+            slots, 16, device)
+
+    def step():
+        if gather is not None:
+            gather.decode(q, ptrs, lens_d, max_n, cap, 128 ** -0.5, ws)
+        else:
+            st = L.rib_decode_attention_batched(q.data_ptr(), ptrs.data_ptr(), lens_d.data_ptr(),
+                                                slots, max_n, cap, 16, NKV_TOTAL, 128 ** -0.5,
+                                                out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                                stream.cuda_stream)
+            if st != 0:
+                raise RuntimeError(f"ragged decode failed: status {st}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / args.steps, world, device)
+    if gather is not None:
+        gather.close()
+    total = sum(4096 * n for n in lens)
+    v = total / (ms * 1e-3) / 1e9
+    return {"value": v, "unit": "GB/s", "ms_per_step": ms, "sequences": len(lens),
+            "kv_bytes_per_step": total, "frac_of_hbm_peak_x_gpus": v / (pk["hbm_gbs"] * world),
+            "sharding": f"sequences, LPT by context, {slots} slots per rank",
+            "contexts": "U[512, 32768], seed 0"}
 
 
 def run_e2e(rib, w, rank, world, device, args, gather, plan):

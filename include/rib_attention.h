@@ -12,7 +12,8 @@
  *     layout stated per argument.  The caller owns every buffer; the library
  *     never allocates or frees on these paths and keeps no per-call state.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
- *     only enqueues work and returns; none synchronises.
+ *     only enqueues work (kernels, and for decode a small memset of its
+ *     counters) and returns; none synchronises.
  *   - Return value: RIB_OK (0) or one of the RIB_E* codes below.  Argument
  *     checks run on the host before anything is launched, so an error return
  *     means nothing was enqueued.
@@ -114,10 +115,10 @@ int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw,
  *   n      number of valid keys (offset + 1 in Engine.decode, engine.py:149)
  *   out    [nq, 128]             == [1, nq, 1, 128], o_proj input layout
  *   workspace / workspace_bytes  device scratch of at least
- *          rib_decode_workspace_bytes(1, n, nkv) bytes.  Its first
- *          4 * nkv bytes are counters that must be zero before the first
- *          call; every call leaves them zero again.  Calls that share a
- *          workspace must not overlap on the device.
+ *          rib_decode_workspace_bytes(1, n, nkv) bytes, no initialisation
+ *          needed: each call first clears its counters with an enqueued
+ *          memset on `stream`.  Calls that share a workspace must not
+ *          overlap on the device.
  * Softmax and accumulation in FP32; output rounded to BF16 once.
  * ------------------------------------------------------------------------ */
 size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv);
@@ -135,7 +136,7 @@ int rib_decode_attention(const void *q, const void *cache, int cap, int n,
  * host whose device memory is owned by another allocator or a hard memory
  * budget, a binding with no device allocator of its own).
  *   - Sizes whose scratch (rib_decode_workspace_bytes(1, n, nkv)) exceeds
- *     2 MiB are rejected with RIB_EINVAL (n <= 258048 keys at 8 KV heads).
+ *     2 MiB are rejected with RIB_EINVAL (every n <= 911232 fits at 8 KV heads).
  *   - The first call on a device looks up the array's device address; make
  *     that first call before any stream capture.
  *   - Every call clears the array's counters on `stream` and then reuses it:
@@ -156,7 +157,7 @@ int rib_decode_attention_noalloc(const void *q, const void *cache, int cap,
  *   max_n      host upper bound on lens[] (sizes the launch)
  *   out        [B, nq, 128]
  *   workspace  at least rib_decode_workspace_bytes(B, max_n, nkv) bytes,
- *              same zero-counter contract as above.
+ *              same contract as above.
  * ------------------------------------------------------------------------ */
 int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs,
                                  const int32_t *lens, int batch, int max_n,

@@ -44,6 +44,8 @@ constexpr int ROW_BYTES = D * 2;       // one key row, BF16
 constexpr int kMaxPeers = 8;           // ranks of one NVLink all-gather
 constexpr int TILE_BYTES = TK * ROW_BYTES;
 
+constexpr int kMergeSplits = 512;     // splits whose (m, l) the final merge stages in smem
+
 struct Smem {
   alignas(128) uint8_t k[STAGES][TILE_BYTES];
   alignas(128) uint8_t v[STAGES][TILE_BYTES];
@@ -51,6 +53,8 @@ struct Smem {
   alignas(16) float red_o[NCW][2][D];
   float red_m[NCW][2];
   float red_l[NCW][2];
+  float merge_m[2][kMergeSplits];
+  float merge_l[2][kMergeSplits];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   int is_last;
@@ -396,18 +400,44 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
   __syncthreads();
   if (!s.is_last) return;
   __threadfence();
-  if (tid < D) {
+  // Merge the splits.  The (m, l) pairs of all splits are staged in shared
+  // memory by parallel loads; each thread then weighs its dimension of every
+  // split's partial o with loads issued in independent batches.
+  const float *ml = p.part_ml + unit * p.max_splits * 4;  // [split][head][m, l]
+  const float *po = p.part_o + unit * p.max_splits * 2 * D;
+  if (nsplit <= kMergeSplits) {
+    for (int i = tid; i < 2 * nsplit; i += NTHREADS) {
+      const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + i);
+      s.merge_m[i & 1][i >> 1] = v.x;
+      s.merge_l[i & 1][i >> 1] = v.y;
+    }
+    __syncthreads();
+    if (tid < D) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float M = -INFINITY;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, s.merge_m[hh][sp]);
+        float L = 0.f, O = 0.f;
+#pragma unroll 8
+        for (int sp = 0; sp < nsplit; ++sp) {
+          const float f = fast_exp2(s.merge_m[hh][sp] - M);
+          L = fmaf(s.merge_l[hh][sp], f, L);
+          O = fmaf(__ldcg(&po[(sp * 2 + hh) * D + tid]), f, O);
+        }
+        res[hh] = O / L;
+      }
+    }
+  } else if (tid < D) {
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       float M = -INFINITY;
-      for (int sp = 0; sp < nsplit; ++sp)
-        M = fmaxf(M, __ldcg(&p.part_ml[((unit * p.max_splits + sp) * 2 + hh) * 2]));
+      for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&ml[(sp * 2 + hh) * 2]));
       float L = 0.f, O = 0.f;
+#pragma unroll 8
       for (int sp = 0; sp < nsplit; ++sp) {
-        const size_t pi = (unit * p.max_splits + sp) * 2 + hh;
-        const float f = fast_exp2(__ldcg(&p.part_ml[pi * 2]) - M);
-        L = fmaf(__ldcg(&p.part_ml[pi * 2 + 1]), f, L);
-        O = fmaf(__ldcg(&p.part_o[pi * D + tid]), f, O);
+        const float f = fast_exp2(__ldcg(&ml[(sp * 2 + hh) * 2]) - M);
+        L = fmaf(__ldcg(&ml[(sp * 2 + hh) * 2 + 1]), f, L);
+        O = fmaf(__ldcg(&po[(sp * 2 + hh) * D + tid]), f, O);
       }
       res[hh] = O / L;
     }

@@ -4,6 +4,7 @@
 // word (common.cuh).
 #include <cmath>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -11,6 +12,11 @@
 #include "decode_attention.cuh"
 #include "prefill_attention.cuh"
 #include "qk_norm_rope.cuh"
+
+// Largest split of the decode kernel, in keys (a build-time tuning constant).
+#ifndef RIB_DECODE_MAX_CHUNK
+#define RIB_DECODE_MAX_CHUNK 4096
+#endif
 
 namespace {
 
@@ -121,14 +127,32 @@ struct DecodeGeometry {
 DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
   using namespace rib::decode;
   DecodeGeometry g;
-  const long long target = 2LL * sm_count();  // two CTAs per SM
-  const long long total = static_cast<long long>(batch) * nkv * max_n;
-  int chunk = ceil_div(total, target);
-  chunk = ceil_div(chunk, TK) * TK;
-  if (chunk < TK) chunk = TK;
-  if (chunk > 1024) chunk = 1024;
-  g.chunk = chunk;
-  g.max_splits = ceil_div(max_n, chunk);
+  // Split count: start from the larger of "chunks of at most
+  // RIB_DECODE_MAX_CHUNK keys" and
+  // "at least one full wave of 2 CTAs per SM", then take the smallest count
+  // up to twice that whose CTA total fills whole waves (>= 97% of the last
+  // wave's slots), so no nearly empty wave trails the launch; otherwise the
+  // best wave fill in that range.
+  const long long slots = 2LL * sm_count();
+  const long long n_units = static_cast<long long>(batch) * nkv;
+  const int lo = std::max(ceil_div(max_n, RIB_DECODE_MAX_CHUNK),
+                          std::min(ceil_div(slots, n_units), ceil_div(max_n, TK)));
+  const int hi = std::max(lo, std::min(2 * lo, ceil_div(max_n, TK)));
+  int best_chunk = ceil_div(ceil_div(max_n, lo), TK) * TK;
+  double best_eff = -1.0;
+  for (int splits = lo; splits <= hi; ++splits) {
+    const int chunk = max(TK, ceil_div(ceil_div(max_n, splits), TK) * TK);
+    const long long ctas = n_units * ceil_div(max_n, chunk);
+    const long long waves = (ctas + slots - 1) / slots;
+    const double eff = static_cast<double>(ctas) / static_cast<double>(waves * slots);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best_chunk = chunk;
+    }
+    if (eff >= 0.97) break;
+  }
+  g.chunk = best_chunk;
+  g.max_splits = ceil_div(max_n, best_chunk);
   const size_t units = static_cast<size_t>(batch) * nkv;
   // per-unit split counters, then one counter of units finalised (all-gather)
   g.counters_bytes = (((units + 1) * sizeof(int) + 255) / 256) * 256;
@@ -148,6 +172,11 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   if (!workspace || workspace_bytes < g.total) return RIB_EINVAL;
   if (!aligned16(workspace)) return RIB_EALIGN;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
+  // The split counters must start at zero.  A workspace shared with a call
+  // of another shape holds that call's FP32 partials where this call keeps
+  // counters, so they are cleared on the stream before every launch.
+  const cudaError_t ze = cudaMemsetAsync(ws, 0, g.counters_bytes, static_cast<cudaStream_t>(stream));
+  if (ze != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(decode counters)", ze);
   p.counters = reinterpret_cast<int *>(ws);
   p.done = p.counters + static_cast<size_t>(batch) * p.nkv;
   p.part_ml = reinterpret_cast<float *>(ws + g.counters_bytes);
@@ -284,10 +313,7 @@ int rib_decode_attention_noalloc(const void *q, const void *cache, int cap, int 
   if (dev < 0 || dev >= kMaxDevices) return rib::host_fail(RIB_ECUDA, "cudaGetDevice", dev);
   void *scratch = noalloc_scratch(dev);
   if (!scratch) return RIB_ECUDA;
-  // The split counters must start at zero; the array keeps whatever the last
-  // call left, so clear them on the caller's stream first.
-  const cudaError_t e = cudaMemsetAsync(scratch, 0, g.counters_bytes, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(noalloc counters)", e);
+  // (decode_launch clears the split counters on the stream before launching.)
   rib::decode::Params p = {};
   p.q = static_cast<const uint16_t *>(q);
   p.cache = static_cast<const uint16_t *>(cache);

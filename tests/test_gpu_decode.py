@@ -106,6 +106,21 @@ def test_decode_ragged_batch(rib, wl, oracle, batch, lo, hi):
     _assert_parity(out, of)
 
 
+def test_decode_workspace_shared_across_shapes(rib, wl, oracle):
+    """Calls of different shapes share one cached workspace; the partials of a
+    small call sit where a larger call keeps split counters, which the library
+    clears before every launch (a stale counter makes a unit merge early)."""
+    for B, n in [(2, 4097), (28, 4160), (2, 4097), (28, 4097)]:
+        cap = wl.round_cap(n)
+        caches = wl.randn_bf16((B, 2, 8, cap, 128), seed=B + n, device="cuda")
+        q = wl.randn_bf16((B, 16, 128), seed=B * n, device="cuda")
+        out = rib.decode_attention_batched(q, caches, [n] * B, wl.SCALE)
+        torch.cuda.synchronize()
+        of, _ = oracle.decode_attention_batched(u16(q), [u16(caches[i]) for i in range(B)],
+                                                [n] * B, wl.SCALE)
+        _assert_parity(out, of)
+
+
 def test_decode_device_status_clean(rib):
     from importlib import import_module
     lib = import_module("roofline-inference_b200._lib")
