@@ -24,10 +24,12 @@ LIB_PATH = PKG_DIR / "librib_attention.so"
 STAMP = PKG_DIR / "librib_attention.so.srchash"
 MAIN_SOURCE = CSRC / "rib_attention.cu"
 
+EXPORTS = CSRC / "exports.map"
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo", "-O3", "-std=c++17",
     "-Xcompiler", "-fPIC", "-shared",
+    "-Xlinker", f"--version-script={EXPORTS}",
 ]
 
 # status codes (include/rib_attention.h)
@@ -37,7 +39,7 @@ _lib: ctypes.CDLL | None = None
 
 
 def _sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HEADER]
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [HEADER, EXPORTS]
 
 
 def source_hash() -> str:
@@ -45,7 +47,7 @@ def source_hash() -> str:
     for p in _sources():
         h.update(p.name.encode())
         h.update(p.read_bytes())
-    h.update(" ".join(NVCC_FLAGS).encode())
+    h.update(" ".join(f for f in NVCC_FLAGS if not f.startswith("--version-script")).encode())
     return h.hexdigest()
 
 
