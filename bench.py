@@ -621,15 +621,33 @@ def run_prefill(rib, device, args, pk):
         a.record(stream)
         rib.attention(Q, K, V, L, L, wl.SCALE)
         b.record(stream)
+    sm_mhz = sm_clock_mhz(device)  # sampled while the last launches still run
     torch.cuda.synchronize()
     ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     flops = wl.prefill_flops(L)
     tf = flops / (ms * 1e-3) / 1e12
-    return {"value": tf, "unit": "TFLOP/s", "L": L, "ms": ms, "flops": flops,
+    # The loop runs back to back for reps * ms, long enough for the 1000 W cap to
+    # lower the SM clock, so the sustained cuBLAS figure is reported beside the burst one.
+    return {"value": tf, "unit": "TFLOP/s", "L": L, "ms": ms, "flops": flops, "launches": reps,
+            "sm_mhz_in_loop": sm_mhz,
             "roofline": {"bound": "tensor", "achieved": tf, "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": tf / pk["bf16_tflops"],
                          "peak_source": pk["source"] + " bf16_tflops (burst)",
+                         "peak_sustained": pk["bf16_tflops_sustained"],
+                         "frac_of_sustained": tf / pk["bf16_tflops_sustained"],
                          "kernel": "rib::prefill::prefill_kernel"}}
+
+
+def sm_clock_mhz(device):
+    """Current SM clock of `device` through NVML, or None."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return int(pynvml.nvmlDeviceGetClockInfo(pynvml.nvmlDeviceGetHandleByIndex(idx),
+                                                 pynvml.NVML_CLOCK_SM))
+    except Exception:
+        return None
 
 
 def run_case(case: str):
