@@ -225,6 +225,76 @@ int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL,
                           int kL, int qLp, int cap, int H, int nkv,
                           float scale, void *O, void *stream);
 
+/* ======================================================================== *
+ * Qwen3 forward around the attention path (agent-test/v2/engine.py:102-163).
+ * ======================================================================== */
+
+/* Fused RMSNorm + RoPE + KV append with the position read on the device, so
+ * a captured CUDA graph can replay a decode step at a new position.  Same as
+ * rib_qk_norm_rope_append with offset = *offset_dev (an int32 in device
+ * memory); the reference passes the position as an int32 array too
+ * (qk_norm_rope(qkv, qw, kw, pos, ...), agent-test/v2/kernels.py:157-164).
+ * offset + L > cap is detected on the device: nothing is written and the
+ * device status word (rib_take_device_status) reads RIB_ECAPACITY. */
+int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw,
+                                const void *kw, const int32_t *offset_dev,
+                                int nq, int nkv, double base, int Lp,
+                                void *q_out, void *cache, int cap, void *stream);
+
+/* Epilogues of rib_gemv. */
+#define RIB_EPI_NONE 0     /* y = bf16(W x), or FP32 W x when out_f32      */
+#define RIB_EPI_RESIDUAL 1 /* y = bf16(res + bf16(W x))                    */
+#define RIB_EPI_SWIGLU 2   /* W = [gate; up] (N = 2F rows), y[F]:
+                              g = bf16(W_g x), u = bf16(W_u x),
+                              y = bf16(bf16(g * bf16(sigmoid(g))) * u)     */
+
+/* Batch-1 GEMV with fused input RMSNorm and epilogue.  Replaces
+ * gemv(W, x, nw=, res=, swiglu=, out_float=) (agent-test/v2/kernels.py
+ * :103-113, Metal source :19-97).
+ *   W    [N, K] BF16 row-major, K a multiple of 256, K <= 8192
+ *   x    [K] BF16
+ *   nw   [K] RMSNorm weight or NULL; with it the kernel uses
+ *        bf16(nw * bf16(x / sqrt(mean(x^2) + 1e-6))) in place of x
+ *   res  [N] BF16 residual (RIB_EPI_RESIDUAL only, NULL otherwise)
+ *   y    [N] BF16 ([N/2] for RIB_EPI_SWIGLU), or [N] FP32 when out_f32
+ *        (RIB_EPI_NONE only: the logits, gemv(..., out_float=True)). */
+int rib_gemv(const void *W, int N, int K, const void *x, const void *nw,
+             const void *res, int epi, int out_f32, void *y, void *stream);
+
+/* Residual add + RMSNorm over `rows` rows of width W (multiple of 8,
+ * <= 8192).  Replaces add_rms(a, b, weight) (agent-test/v2/kernels.py
+ * :262-268, Metal source :227-259): residual = bf16(a + b), normalized =
+ * bf16(w * bf16(residual / sqrt(mean(residual^2) + 1e-6))). */
+int rib_add_rms(const void *a, const void *b, const void *w, int rows, int W,
+                void *residual, void *normalized, void *stream);
+
+/* RMSNorm of `rows` rows: out = bf16(w * bf16(x / sqrt(mean(x^2) + 1e-6))).
+ * Replaces mx.fast.rms_norm(h, w, eps) (agent-test/v2/engine.py:109, 140). */
+int rib_rms_norm(const void *x, const void *w, int rows, int W, void *out,
+                 void *stream);
+
+/* SwiGLU of a fused gate/up product: gu [rows, 2F] (gate columns first) ->
+ * out [rows, F] with the RIB_EPI_SWIGLU rounding.  Replaces
+ * swiglu(*mx.split(x @ W_gu^T, 2, -1)) (agent-test/v2/engine.py:28-30, 133-134).
+ * F is a multiple of 8. */
+int rib_swiglu(const void *gu, int rows, int F, void *out, void *stream);
+
+/* Embedding gather out[i] = table[tokens[i]] for n int32 token ids in device
+ * memory.  Replaces self.embed[tokens] (agent-test/v2/engine.py:108, 147).
+ * An id outside [0, vocab) writes a zero row and sets the device status
+ * word to RIB_EINVAL. */
+int rib_embed(const void *table, int vocab, int hidden, const int32_t *tokens,
+              int n, void *out, void *stream);
+
+/* Greedy token: out[0] = index of the largest of n FP32 logits (the first on
+ * ties).  Replaces mx.argmax(logits) (agent-test/v2/engine.py:163, 183).
+ * workspace: rib_argmax_workspace_bytes() bytes of device memory, 16-byte
+ * aligned; cleared by the call itself, so it needs no initialisation, but
+ * calls that overlap in time need separate workspaces. */
+size_t rib_argmax_workspace_bytes(void);
+int rib_argmax_f32(const float *x, int n, int32_t *out, void *workspace,
+                   void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,4 +1,4 @@
-"""B200-native (sm_100a) Qwen3 attention hot path.
+"""B200-native (sm_100a) Qwen3 attention hot path, and the Qwen3 forward around it.
 
 Drop-in for the attention entry points of the reference's v2 engine
 (aeilot/roofline-inference, agent-test/v2): fused QK-RMSNorm + RoPE (+ KV
@@ -13,10 +13,25 @@ The directory name contains a hyphen, so it is imported with importlib:
 from . import _lib
 from .attention import attention, decode_attention, decode_attention_batched
 from .cache import Cache
-from .kernels import qk_norm_rope, qk_norm_rope_append, qk_norm_rope_prefill
+from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope, qk_norm_rope_append,
+                      qk_norm_rope_append_at, qk_norm_rope_prefill, rms_norm, swiglu)
+from .model import QWEN3_0_6B, DecodeGraph, Engine, Qwen3Config, Qwen3Weights, random_weights
 
 __all__ = [
     "Cache",
+    "DecodeGraph",
+    "Engine",
+    "QWEN3_0_6B",
+    "Qwen3Config",
+    "Qwen3Weights",
+    "add_rms",
+    "argmax",
+    "embedding",
+    "gemv",
+    "qk_norm_rope_append_at",
+    "random_weights",
+    "rms_norm",
+    "swiglu",
     "attention",
     "decode_attention",
     "decode_attention_batched",

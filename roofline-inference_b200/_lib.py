@@ -106,6 +106,14 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_decode_attention_noalloc": ([vp, vp, i, i, i, i, f, vp, vp], i),
         "rib_decode_attention_batched": ([vp, vp, vp, i, i, i, i, i, f, vp, vp, sz, vp], i),
         "rib_prefill_attention": ([vp, vp, vp, i, i, i, i, i, i, f, vp, vp], i),
+        "rib_qk_norm_rope_append_dev": ([vp, i, vp, vp, vp, i, i, d, i, vp, vp, i, vp], i),
+        "rib_gemv": ([vp, i, i, vp, vp, vp, i, i, vp, vp], i),
+        "rib_add_rms": ([vp, vp, vp, i, i, vp, vp, vp], i),
+        "rib_rms_norm": ([vp, vp, i, i, vp, vp], i),
+        "rib_swiglu": ([vp, i, i, vp, vp], i),
+        "rib_embed": ([vp, i, i, vp, i, vp, vp], i),
+        "rib_argmax_workspace_bytes": ([], sz),
+        "rib_argmax_f32": ([vp, i, vp, vp, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

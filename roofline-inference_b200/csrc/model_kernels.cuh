@@ -1,0 +1,319 @@
+// Kernels of the Qwen3 forward around the attention path: decode GEMVs with
+// fused RMSNorm / residual / SwiGLU, the prefill residual+RMSNorm, RMSNorm,
+// SwiGLU, the embedding gather and the greedy argmax.
+//
+// Rounding points follow the reference Metal kernels (agent-test/v2/kernels.py):
+//   RMSNorm     inv = 1/sqrt(sum(x^2)/K + 1e-6), n = bf16(w * bf16(x * inv))
+//               (kernels.py:48-55, 247-260)
+//   GEMV        y = W x with FP32 accumulation, rounded once to BF16 (or kept
+//               FP32 for the logits)                       (kernels.py:58-81)
+//   residual    y = bf16(res + bf16(W x))                  (kernels.py:84-85)
+//   SwiGLU      g = bf16(W_g x), u = bf16(W_u x), s = bf16(sigmoid(g)),
+//               a = bf16(g s), y = bf16(a u)                (kernels.py:86-93)
+//   add_rms     r = bf16(a + b), n = bf16(w * bf16(r * inv)) (kernels.py:227-268)
+// The GEMVs are HBM-bound at batch 1: every weight byte is read once with
+// 16-byte non-allocating loads, each warp owns R output rows and each lane
+// covers K/256 16-byte chunks of a row, so one CTA of 8 warps keeps up to
+// 8 * R * K * 2 bytes of weights in flight.  The input vector (normalised
+// once per CTA when the RMSNorm is fused) sits in shared memory as FP32.
+#pragma once
+
+#include "common.cuh"
+
+namespace rib {
+namespace model {
+
+constexpr float kEps = 1e-6f;
+constexpr int kGemvWarps = 8;
+constexpr int kMaxK = 8192;
+
+enum Epilogue { kNone = 0, kResidual = 1, kSwiGLU = 2 };
+
+__device__ __forceinline__ void record_status(int status) { atomicExch(&g_device_status, status); }
+
+// 16-byte streaming load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum over the CTA (blockDim.x a multiple of 32, at most 1024); every thread
+// gets the total.  `red` holds 32 floats of shared memory.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ float dot8(const uint4 w, const float4 xa, const float4 xb, float acc) {
+  acc = fmaf(bf16lo(w.x), xa.x, acc);
+  acc = fmaf(bf16hi(w.x), xa.y, acc);
+  acc = fmaf(bf16lo(w.y), xa.z, acc);
+  acc = fmaf(bf16hi(w.y), xa.w, acc);
+  acc = fmaf(bf16lo(w.z), xb.x, acc);
+  acc = fmaf(bf16hi(w.z), xb.y, acc);
+  acc = fmaf(bf16lo(w.w), xb.z, acc);
+  acc = fmaf(bf16hi(w.w), xb.w, acc);
+  return acc;
+}
+
+__device__ __forceinline__ float sigmoid_bf16(float g) { return round_bf16(1.0f / (1.0f + expf(-g))); }
+
+// ------------------------------------------------------------------ GEMV
+struct GemvParams {
+  const uint16_t *W;    // [N][K] BF16 row-major
+  const uint16_t *x;    // [K]
+  const uint16_t *nw;   // [K] RMSNorm weight, or null (no norm)
+  const uint16_t *res;  // [rows_out] residual, epilogue kResidual
+  void *y;              // [rows_out] BF16, or FP32 when out_f32
+  int N, K, rows_out, epi, out_f32;
+};
+
+// C = K / 256 chunks of 8 elements per lane (0: runtime count).  R rows per warp.
+template <int R, int C>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ float xs[];  // [K]
+  __shared__ float red[32];
+  const int K = p.K;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // ---- x into shared memory (normalised when nw is given)
+  float ss = 0.f;
+  for (int i = tid * 8; i < K; i += blockDim.x * 8) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(p.x + i);
+    float f[8] = {bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y),
+                  bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w)};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      xs[i + e] = f[e];
+      ss = fmaf(f[e], f[e], ss);
+    }
+  }
+  if (p.nw) {
+    const float inv = 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(K) + kEps);
+    for (int i = tid * 8; i < K; i += blockDim.x * 8) {
+      const uint4 w = *reinterpret_cast<const uint4 *>(p.nw + i);
+      const float wf[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                           bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xs[i + e] = round_bf16(wf[e] * round_bf16(xs[i + e] * inv));
+    }
+  }
+  __syncthreads();
+
+  // ---- rows of this warp
+  const int row0 = (blockIdx.x * kGemvWarps + warp) * R;
+  if (row0 >= p.rows_out) return;
+  const bool swiglu = p.epi == kSwiGLU;
+  const int F = p.rows_out;  // up rows start at F in the SwiGLU case
+  const int nrow = swiglu ? 2 * R : R;
+  float acc[2 * R];
+#pragma unroll
+  for (int r = 0; r < 2 * R; ++r) acc[r] = 0.f;
+  const uint16_t *wrow[2 * R];
+#pragma unroll
+  for (int r = 0; r < 2 * R; ++r) {
+    const int rr = r < R ? min(row0 + r, p.rows_out - 1) : min(row0 + r - R, p.rows_out - 1) + F;
+    wrow[r] = p.W + static_cast<size_t>(r < nrow ? rr : row0) * K;
+  }
+  const int nchunks = C > 0 ? C : K / 256;
+#pragma unroll(C > 0 ? C : 1)
+  for (int c = 0; c < nchunks; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    const float4 xa = *reinterpret_cast<const float4 *>(xs + col);
+    const float4 xb = *reinterpret_cast<const float4 *>(xs + col + 4);
+    uint4 w[2 * R];
+#pragma unroll
+    for (int r = 0; r < 2 * R; ++r)
+      if (r < nrow) w[r] = ldg_stream(wrow[r] + col);
+#pragma unroll
+    for (int r = 0; r < 2 * R; ++r)
+      if (r < nrow) acc[r] = dot8(w[r], xa, xb, acc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < 2 * R; ++r)
+    if (r < nrow) acc[r] = warp_sum(acc[r]);
+  if (lane != 0) return;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
+    if (row >= p.rows_out) break;
+    if (p.out_f32) {
+      static_cast<float *>(p.y)[row] = acc[r];
+      continue;
+    }
+    float v;
+    if (swiglu) {
+      const float g = round_bf16(acc[r]), u = round_bf16(acc[R + r]);
+      const float a = round_bf16(g * sigmoid_bf16(g));
+      v = a * u;
+    } else if (p.epi == kResidual) {
+      v = __uint_as_float(static_cast<uint32_t>(p.res[row]) << 16) + round_bf16(acc[r]);
+    } else {
+      v = acc[r];
+    }
+    static_cast<uint16_t *>(p.y)[row] = static_cast<uint16_t>(pack_bf16x2(v, 0.f) & 0xffffu);
+  }
+}
+
+// ------------------------------------------------------------------ row norms (prefill)
+struct RowParams {
+  const uint16_t *a;   // [rows][W]
+  const uint16_t *b;   // [rows][W] added to a (add_rms), or null
+  const uint16_t *w;   // [W] norm weight
+  uint16_t *residual;  // [rows][W] a + b, or null
+  uint16_t *out;       // [rows][W] normalised
+  int rows, W;
+};
+
+// One CTA per row, 8 elements per thread per step.  The row is kept in
+// shared memory between the sum of squares and the normalisation.
+__global__ void __launch_bounds__(256) add_rms_kernel(const __grid_constant__ RowParams p) {
+  extern __shared__ float rs[];  // [W]
+  __shared__ float red[32];
+  const size_t base = static_cast<size_t>(blockIdx.x) * p.W;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < p.W; i += blockDim.x * 8) {
+    const uint4 va = *reinterpret_cast<const uint4 *>(p.a + base + i);
+    float f[8] = {bf16lo(va.x), bf16hi(va.x), bf16lo(va.y), bf16hi(va.y),
+                  bf16lo(va.z), bf16hi(va.z), bf16lo(va.w), bf16hi(va.w)};
+    if (p.b) {
+      const uint4 vb = *reinterpret_cast<const uint4 *>(p.b + base + i);
+      const float g[8] = {bf16lo(vb.x), bf16hi(vb.x), bf16lo(vb.y), bf16hi(vb.y),
+                          bf16lo(vb.z), bf16hi(vb.z), bf16lo(vb.w), bf16hi(vb.w)};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = round_bf16(f[e] + g[e]);
+      uint4 o;
+      o.x = pack_bf16x2(f[0], f[1]);
+      o.y = pack_bf16x2(f[2], f[3]);
+      o.z = pack_bf16x2(f[4], f[5]);
+      o.w = pack_bf16x2(f[6], f[7]);
+      *reinterpret_cast<uint4 *>(p.residual + base + i) = o;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      rs[i + e] = f[e];
+      ss = fmaf(f[e], f[e], ss);
+    }
+  }
+  const float inv = 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(p.W) + kEps);
+  for (int i = threadIdx.x * 8; i < p.W; i += blockDim.x * 8) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(p.w + i);
+    const float wf[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                         bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+    float n[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) n[e] = wf[e] * round_bf16(rs[i + e] * inv);
+    uint4 o;
+    o.x = pack_bf16x2(n[0], n[1]);
+    o.y = pack_bf16x2(n[2], n[3]);
+    o.z = pack_bf16x2(n[4], n[5]);
+    o.w = pack_bf16x2(n[6], n[7]);
+    *reinterpret_cast<uint4 *>(p.out + base + i) = o;
+  }
+}
+
+// ------------------------------------------------------------------ SwiGLU (prefill)
+// gu [rows][2F] (gate columns [0, F), up columns [F, 2F)) -> out [rows][F].
+__global__ void swiglu_kernel(const uint16_t *__restrict__ gu, int rows, int F, uint16_t *__restrict__ out) {
+  const long long total = static_cast<long long>(rows) * (F / 8);
+  for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < total;
+       v += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = v / (F / 8);
+    const int c = static_cast<int>(v - r * (F / 8)) * 8;
+    const uint4 g4 = *reinterpret_cast<const uint4 *>(gu + r * 2 * F + c);
+    const uint4 u4 = *reinterpret_cast<const uint4 *>(gu + r * 2 * F + F + c);
+    const float g[8] = {bf16lo(g4.x), bf16hi(g4.x), bf16lo(g4.y), bf16hi(g4.y),
+                        bf16lo(g4.z), bf16hi(g4.z), bf16lo(g4.w), bf16hi(g4.w)};
+    const float u[8] = {bf16lo(u4.x), bf16hi(u4.x), bf16lo(u4.y), bf16hi(u4.y),
+                        bf16lo(u4.z), bf16hi(u4.z), bf16lo(u4.w), bf16hi(u4.w)};
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = round_bf16(g[e] * sigmoid_bf16(g[e])) * u[e];
+    uint4 o;
+    o.x = pack_bf16x2(y[0], y[1]);
+    o.y = pack_bf16x2(y[2], y[3]);
+    o.z = pack_bf16x2(y[4], y[5]);
+    o.w = pack_bf16x2(y[6], y[7]);
+    *reinterpret_cast<uint4 *>(out + r * F + c) = o;
+  }
+}
+
+// ------------------------------------------------------------------ embedding gather
+// out[i] = table[tokens[i]]; a token outside [0, vocab) writes zeros and
+// records RIB_EINVAL in the device status word.
+__global__ void embed_kernel(const uint16_t *__restrict__ table, int vocab, int hidden,
+                             const int32_t *__restrict__ tokens, uint16_t *__restrict__ out) {
+  const int i = blockIdx.x;
+  const int tok = tokens[i];
+  const bool ok = tok >= 0 && tok < vocab;
+  if (!ok && threadIdx.x == 0) record_status(RIB_EINVAL);
+  for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (ok) v = *reinterpret_cast<const uint4 *>(table + static_cast<size_t>(tok) * hidden + c);
+    *reinterpret_cast<uint4 *>(out + static_cast<size_t>(i) * hidden + c) = v;
+  }
+}
+
+// ------------------------------------------------------------------ greedy argmax
+// Index of the largest FP32 value (the first one on ties, as numpy/MLX argmax).
+// Keys order (value, -index) as unsigned 64-bit integers; each CTA folds its
+// slice into ws->best with atomicMax, and the last CTA to finish (counted in
+// ws->done) writes the index.  The caller clears the workspace first.
+struct ArgmaxWs {
+  unsigned long long best;
+  unsigned int done;
+};
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // monotone in v
+  return (static_cast<unsigned long long>(b) << 32) | (0xffffffffu - static_cast<uint32_t>(i));
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int n, ArgmaxWs *ws,
+                                                      int32_t *__restrict__ out) {
+  __shared__ unsigned long long red[32];
+  __shared__ bool last;
+  unsigned long long best = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long k = argmax_key(x[i], i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    atomicMax(&ws->best, best);
+    __threadfence();
+    last = atomicAdd(&ws->done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long b = atomicAdd(&ws->best, 0ull);
+    out[0] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffull));
+  }
+}
+
+}  // namespace model
+}  // namespace rib

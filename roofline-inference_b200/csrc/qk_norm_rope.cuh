@@ -36,6 +36,7 @@ struct Params {
   int L, Lp, offset, nq, nkv;
   int kv_rows;          // rows per head in kv (L, or the cache capacity)
   int kv_row0;          // first row written (0, or the cache offset)
+  const int32_t *offset_dev;  // when set: the offset (and first cache row) read on the device
   double inv_freq[64];  // base^(-d/64), FP64
 };
 
@@ -43,9 +44,18 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
   __shared__ float cos_t[64], sin_t[64];
   const int t = blockIdx.x;
   const int tid = threadIdx.x;
+  int offset = p.offset, kv_row0 = p.kv_row0;
+  if (p.offset_dev) {  // position kept on the device (CUDA-graph replay)
+    offset = *p.offset_dev;
+    kv_row0 = offset;
+    if (offset < 0 || static_cast<long long>(offset) + p.L > p.kv_rows) {
+      if (t == 0 && tid == 0) atomicExch(&g_device_status, RIB_ECAPACITY);
+      return;
+    }
+  }
   if (tid < 64) {
     const double two_pi = 6.283185307179586476925286766559;
-    const double th = static_cast<double>(p.offset + t) * p.inv_freq[tid];
+    const double th = static_cast<double>(offset + t) * p.inv_freq[tid];
     const double r = th - rint(th * (1.0 / two_pi)) * two_pi;
     float s, c;
     sincosf(static_cast<float>(r), &s, &c);
@@ -74,7 +84,7 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
 
   if (item >= p.nq + p.nkv) {  // V: bit-exact copy into the cache
     const int hv = item - p.nq - p.nkv;
-    uint16_t *dst = p.kv + ((static_cast<size_t>(p.nkv + hv) * p.kv_rows) + p.kv_row0 + t) * D + 8 * j;
+    uint16_t *dst = p.kv + ((static_cast<size_t>(p.nkv + hv) * p.kv_rows) + kv_row0 + t) * D + 8 * j;
     *reinterpret_cast<uint4 *>(dst) = raw;
     return;
   }
@@ -123,7 +133,7 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
     dst = p.q_out + (static_cast<size_t>(item) * p.Lp + t) * D + 8 * j;
   } else {
     const int hk = item - p.nq;
-    dst = p.kv + ((static_cast<size_t>(hk) * p.kv_rows) + p.kv_row0 + t) * D + 8 * j;
+    dst = p.kv + ((static_cast<size_t>(hk) * p.kv_rows) + kv_row0 + t) * D + 8 * j;
   }
   *reinterpret_cast<uint4 *>(dst) = out;
 }

@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "decode_attention.cuh"
 #include "prefill_attention.cuh"
+#include "model_kernels.cuh"
 #include "qk_norm_rope.cuh"
 
 // Largest split of the decode kernel, in keys (a build-time tuning constant).
@@ -74,6 +75,14 @@ int launch_status(const char *what) {
 // lands on the caller's device whatever this thread's runtime state says.
 bool bind_stream_device(void *stream) {
   if (!stream) return true;
+  // A stream under graph capture refuses cudaStreamGetDevice (and the refusal
+  // invalidates the capture); the capturing caller has its device current.
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return true;
   int dev = -1;
   if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev) != cudaSuccess) {
     cudaGetLastError();
@@ -89,7 +98,8 @@ bool bind_stream_device(void *stream) {
 
 // ------------------------------------------------------------------ rope
 int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offset, int nq, int nkv,
-                double base, int Lp, void *q_out, void *kv, int kv_rows, int kv_row0, void *stream) {
+                double base, int Lp, void *q_out, void *kv, int kv_rows, int kv_row0, void *stream,
+                const int32_t *offset_dev = nullptr) {
   if (L < 1 || Lp < L || nq < 1 || nkv < 1 || nq + 2 * nkv > rib::rope::kMaxItems || offset < 0 ||
       !(base > 0.0) || kv_rows < 1)
     return RIB_EINVAL;
@@ -110,6 +120,7 @@ int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offs
   p.nkv = nkv;
   p.kv_rows = kv_rows;
   p.kv_row0 = kv_row0;
+  p.offset_dev = offset_dev;
   for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
   const int items = nq + 2 * nkv;
   const int threads = ((items + 1) / 2) * 32;
@@ -217,6 +228,25 @@ void *noalloc_scratch(int dev) {
     g_noalloc_scratch_addr[dev] = ptr;
   }
   return g_noalloc_scratch_addr[dev];
+}
+
+// ------------------------------------------------------------------ model kernels
+template <int R, int C>
+int gemv_launch_rc(const rib::model::GemvParams &p, cudaStream_t st) {
+  const int rows_per_cta = rib::model::kGemvWarps * R;
+  const int grid = ceil_div(p.rows_out, rows_per_cta);
+  rib::model::gemv_kernel<R, C><<<grid, rib::model::kGemvWarps * 32, p.K * sizeof(float), st>>>(p);
+  return launch_status("gemv_kernel launch");
+}
+
+template <int R>
+int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
+  switch (p.K) {
+    case 1024: return gemv_launch_rc<R, 4>(p, st);
+    case 2048: return gemv_launch_rc<R, 8>(p, st);
+    case 3072: return gemv_launch_rc<R, 12>(p, st);
+    default: return gemv_launch_rc<R, 0>(p, st);
+  }
 }
 
 }  // namespace
@@ -440,6 +470,110 @@ int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL, i
                           int cap, int H, int nkv, float scale, void *O, void *stream) {
   return rib::prefill::launch(Q, K, V, qL, kL, qLp, cap, H, nkv, scale, O, stream,
                               bind_stream_device);
+}
+
+
+// ------------------------------------------------------------------ model kernels
+int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw, const void *kw,
+                                const int32_t *offset_dev, int nq, int nkv, double base, int Lp,
+                                void *q_out, void *cache, int cap, void *stream) {
+  if (L < 1 || cap < 1 || !offset_dev) return RIB_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(offset_dev) & 3u)) return RIB_EALIGN;
+  return rope_launch(qkv, L, qw, kw, 0, nq, nkv, base, Lp, q_out, cache, cap, 0, stream, offset_dev);
+}
+
+int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const void *res, int epi,
+             int out_f32, void *y, void *stream) {
+  using namespace rib::model;
+  if (!W || !x || !y || N < 1 || K < 256 || K % 256 || K > kMaxK) return RIB_EINVAL;
+  if (epi != kNone && epi != kResidual && epi != kSwiGLU) return RIB_EINVAL;
+  if ((epi == kResidual) != (res != nullptr)) return RIB_EINVAL;
+  if (epi == kSwiGLU && (N % 2 || out_f32)) return RIB_EINVAL;
+  if (epi == kResidual && out_f32) return RIB_EINVAL;
+  if (!aligned16(W) || !aligned16(x) || (nw && !aligned16(nw)) || !aligned16(y) ||
+      (res && (reinterpret_cast<uintptr_t>(res) & 1u)))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  GemvParams p;
+  p.W = static_cast<const uint16_t *>(W);
+  p.x = static_cast<const uint16_t *>(x);
+  p.nw = static_cast<const uint16_t *>(nw);
+  p.res = static_cast<const uint16_t *>(res);
+  p.y = y;
+  p.N = N;
+  p.K = K;
+  p.rows_out = epi == kSwiGLU ? N / 2 : N;
+  p.epi = epi;
+  p.out_f32 = out_f32 ? 1 : 0;
+  // Rows per warp: one while that still gives at least 4 CTAs per SM, more
+  // for tall matrices (the LM head) so that each CTA's x load and norm are
+  // amortised over more weight bytes.
+  const int target_ctas = 4 * sm_count();
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p.rows_out >= target_ctas * kGemvWarps * 4) return gemv_launch_r<4>(p, st);
+  if (p.rows_out >= target_ctas * kGemvWarps * 2) return gemv_launch_r<2>(p, st);
+  return gemv_launch_r<1>(p, st);
+}
+
+int rib_add_rms(const void *a, const void *b, const void *w, int rows, int W, void *residual,
+                void *normalized, void *stream) {
+  if (!a || !b || !w || !residual || !normalized || rows < 1 || W < 8 || W % 8 || W > rib::model::kMaxK)
+    return RIB_EINVAL;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(w) || !aligned16(residual) || !aligned16(normalized))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  rib::model::RowParams p = {static_cast<const uint16_t *>(a), static_cast<const uint16_t *>(b),
+                             static_cast<const uint16_t *>(w), static_cast<uint16_t *>(residual),
+                             static_cast<uint16_t *>(normalized), rows, W};
+  rib::model::add_rms_kernel<<<rows, 128, W * sizeof(float), static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status("add_rms_kernel launch");
+}
+
+int rib_rms_norm(const void *x, const void *w, int rows, int W, void *out, void *stream) {
+  if (!x || !w || !out || rows < 1 || W < 8 || W % 8 || W > rib::model::kMaxK) return RIB_EINVAL;
+  if (!aligned16(x) || !aligned16(w) || !aligned16(out)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  rib::model::RowParams p = {static_cast<const uint16_t *>(x), nullptr, static_cast<const uint16_t *>(w),
+                             nullptr, static_cast<uint16_t *>(out), rows, W};
+  rib::model::add_rms_kernel<<<rows, 128, W * sizeof(float), static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status("rms_norm launch");
+}
+
+int rib_swiglu(const void *gu, int rows, int F, void *out, void *stream) {
+  if (!gu || !out || rows < 1 || F < 8 || F % 8) return RIB_EINVAL;
+  if (!aligned16(gu) || !aligned16(out)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const long long vec = static_cast<long long>(rows) * (F / 8);
+  const int grid = static_cast<int>(std::min<long long>(ceil_div(vec, 256), 16LL * sm_count()));
+  rib::model::swiglu_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(gu), rows, F, static_cast<uint16_t *>(out));
+  return launch_status("swiglu_kernel launch");
+}
+
+int rib_embed(const void *table, int vocab, int hidden, const int32_t *tokens, int n, void *out,
+              void *stream) {
+  if (!table || !tokens || !out || vocab < 1 || hidden < 8 || hidden % 8 || n < 1) return RIB_EINVAL;
+  if (!aligned16(table) || !aligned16(out) || (reinterpret_cast<uintptr_t>(tokens) & 3u)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  rib::model::embed_kernel<<<n, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(table), vocab, hidden, tokens, static_cast<uint16_t *>(out));
+  return launch_status("embed_kernel launch");
+}
+
+size_t rib_argmax_workspace_bytes(void) { return 256; }
+
+int rib_argmax_f32(const float *x, int n, int32_t *out, void *workspace, void *stream) {
+  if (!x || !out || !workspace || n < 1) return RIB_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15u))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(rib::model::ArgmaxWs), st);
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(argmax workspace)", e);
+  const int grid = std::max(1, std::min(ceil_div(n, 1024 * 4), sm_count()));
+  rib::model::argmax_kernel<<<grid, 1024, 0, st>>>(x, n, static_cast<rib::model::ArgmaxWs *>(workspace), out);
+  return launch_status("argmax_kernel launch");
 }
 
 }  // extern "C"

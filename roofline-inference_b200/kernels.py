@@ -96,3 +96,193 @@ def qk_norm_rope_append(qkv, qw, kw, offset, nq: int, nkv: int, base: float, cac
                                              stream_handle(qkv.device))
     _lib.check(st, "qk_norm_rope_append")
     return q
+
+
+def qk_norm_rope_append_at(qkv, qw, kw, offset_dev, nq: int, nkv: int, base: float, cache_layer,
+                           Lp: int | None = None, out=None):
+    """qk_norm_rope_append with the offset read on the device.
+
+    offset_dev: int32 CUDA tensor of one element (the reference's `pos` array,
+    agent-test/v2/engine.py:148), read by the kernel, so a captured CUDA graph
+    replays at whatever position the tensor holds.  offset + L > cap is caught
+    on the device (no write; rib_take_device_status reports RIB_ECAPACITY)."""
+    L = _check_common(qkv, qw, kw, nq, nkv)
+    require_bf16_cuda("cache_layer", cache_layer)
+    require_same_device(qkv, cache_layer)
+    if cache_layer.dim() != 4 or cache_layer.shape[0] != 2 or cache_layer.shape[1] != nkv \
+            or cache_layer.shape[3] != HEAD_DIM:
+        raise ValueError(f"cache_layer must be [2, {nkv}, cap, 128], got {tuple(cache_layer.shape)}")
+    _require_i32_scalar("offset_dev", offset_dev, qkv.device)
+    Lp = L if Lp is None else Lp
+    if Lp < L:
+        raise ValueError(f"Lp ({Lp}) must be >= L ({L})")
+    q = _out_or_new(out, (nq, Lp, HEAD_DIM), torch.bfloat16, qkv.device, "out")
+    st = _lib.load().rib_qk_norm_rope_append_dev(qkv.data_ptr(), L, qw.data_ptr(), kw.data_ptr(),
+                                                 offset_dev.data_ptr(), nq, nkv, float(base), Lp,
+                                                 q.data_ptr(), cache_layer.data_ptr(),
+                                                 cache_layer.shape[2], stream_handle(qkv.device))
+    _lib.check(st, "qk_norm_rope_append_at")
+    return q
+
+
+# ----------------------------------------------------------------- model ops
+# The remaining operations of the Qwen3 forward (agent-test/v2/engine.py:102-163):
+# fused GEMVs for decode, residual + RMSNorm, RMSNorm, SwiGLU, embedding gather
+# and greedy argmax, each one kernel of csrc/model_kernels.cuh.
+
+EPI_NONE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+
+
+def _require_i32_scalar(name, t, device):
+    if not isinstance(t, torch.Tensor) or t.dtype != torch.int32 or not t.is_cuda or t.numel() != 1:
+        raise ValueError(f"{name} must be a one-element int32 CUDA tensor")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+
+def _out_or_new(out, shape, dtype, device, name):
+    if out is None:
+        return torch.empty(shape, dtype=dtype, device=device)
+    if not isinstance(out, torch.Tensor) or out.dtype != dtype or out.device != device \
+            or not out.is_contiguous() or out.numel() != int(torch.Size(shape).numel()):
+        raise ValueError(f"{name} must be a contiguous {dtype} tensor of {tuple(shape)} on {device}")
+    return out
+
+
+def gemv(W, x, *, nw=None, res=None, swiglu=False, out_float=False, cfg=None, out=None):
+    """y = epi(W @ pre(x)) for one token (agent-test/v2/kernels.py:103-113).
+
+    W [N, K] BF16 (K a multiple of 256); x [K]; nw: fuse the input RMSNorm
+    (eps 1e-6) with this weight; res: y = bf16(res + bf16(W x)); swiglu: W is
+    [gate; up] and y[N/2] = bf16(bf16(g * bf16(sigmoid(g))) * u); out_float:
+    FP32 output (the logits).  `cfg` (Metal launch tuning) is accepted and
+    ignored."""
+    del cfg
+    require_bf16_cuda("W", W)
+    require_bf16_cuda("x", x)
+    require_same_device(W, x)
+    if W.dim() != 2:
+        raise ValueError(f"W must be [N, K], got {tuple(W.shape)}")
+    N, K = W.shape
+    if x.numel() != K:
+        raise ValueError(f"x holds {x.numel()} elements, W has K = {K}")
+    if K % 256:
+        raise ValueError(f"K ({K}) must be a multiple of 256")
+    if nw is not None:
+        require_bf16_cuda("nw", nw)
+        require_same_device(W, nw)
+        if nw.numel() != K:
+            raise ValueError("nw must hold K elements")
+    if swiglu and (res is not None or out_float):
+        raise ValueError("swiglu takes neither res nor out_float")
+    if res is not None and out_float:
+        raise ValueError("res and out_float do not combine")
+    epi = EPI_SWIGLU if swiglu else (EPI_RESIDUAL if res is not None else EPI_NONE)
+    n_out = N // 2 if swiglu else N
+    if res is not None:
+        require_bf16_cuda("res", res)
+        require_same_device(W, res)
+        if res.numel() != N:
+            raise ValueError("res must hold N elements")
+    y = _out_or_new(out, (n_out,), torch.float32 if out_float else torch.bfloat16, W.device, "out")
+    st = _lib.load().rib_gemv(W.data_ptr(), N, K, x.data_ptr(),
+                              nw.data_ptr() if nw is not None else None,
+                              res.data_ptr() if res is not None else None, epi, int(bool(out_float)),
+                              y.data_ptr(), stream_handle(W.device))
+    _lib.check(st, "gemv")
+    return y
+
+
+def add_rms(a, b, weight, *, out=None):
+    """(a + b, rms_norm(a + b) * weight) over rows of a, b [..., W]
+    (agent-test/v2/kernels.py:262-268).  Returns (residual, normalized)."""
+    for name, t in (("a", a), ("b", b), ("weight", weight)):
+        require_bf16_cuda(name, t)
+    require_same_device(a, b, weight)
+    if a.shape != b.shape:
+        raise ValueError(f"a {tuple(a.shape)} and b {tuple(b.shape)} differ")
+    W = a.shape[-1]
+    if weight.numel() != W:
+        raise ValueError("weight must hold the row width")
+    rows = a.numel() // W
+    r, n = (None, None) if out is None else out
+    r = _out_or_new(r, a.shape, torch.bfloat16, a.device, "out[0]")
+    n = _out_or_new(n, a.shape, torch.bfloat16, a.device, "out[1]")
+    st = _lib.load().rib_add_rms(a.data_ptr(), b.data_ptr(), weight.data_ptr(), rows, W, r.data_ptr(),
+                                 n.data_ptr(), stream_handle(a.device))
+    _lib.check(st, "add_rms")
+    return r.view(a.shape), n.view(a.shape)
+
+
+def rms_norm(x, weight, eps: float = 1e-6, *, out=None):
+    """bf16(weight * bf16(x / sqrt(mean(x^2) + 1e-6))) per row (mx.fast.rms_norm as
+    called at agent-test/v2/engine.py:109, 140; eps is fixed at 1e-6)."""
+    if abs(float(eps) - 1e-6) > 1e-12:
+        raise ValueError("the kernel's eps is 1e-6 (Qwen3 rms_norm_eps)")
+    require_bf16_cuda("x", x)
+    require_bf16_cuda("weight", weight)
+    require_same_device(x, weight)
+    W = x.shape[-1]
+    if weight.numel() != W:
+        raise ValueError("weight must hold the row width")
+    y = _out_or_new(out, x.shape, torch.bfloat16, x.device, "out")
+    st = _lib.load().rib_rms_norm(x.data_ptr(), weight.data_ptr(), x.numel() // W, W, y.data_ptr(),
+                                  stream_handle(x.device))
+    _lib.check(st, "rms_norm")
+    return y.view(x.shape)
+
+
+def swiglu(gu, *, out=None):
+    """gu [rows, 2F] (gate columns, then up) -> [rows, F]: the prefill SwiGLU
+    (agent-test/v2/engine.py:28-30 applied to mx.split(x @ W_gu^T, 2, -1))."""
+    require_bf16_cuda("gu", gu)
+    F2 = gu.shape[-1]
+    if F2 % 16:
+        raise ValueError("gate/up width must be a multiple of 16")
+    rows = gu.numel() // F2
+    y = _out_or_new(out, (*gu.shape[:-1], F2 // 2), torch.bfloat16, gu.device, "out")
+    st = _lib.load().rib_swiglu(gu.data_ptr(), rows, F2 // 2, y.data_ptr(), stream_handle(gu.device))
+    _lib.check(st, "swiglu")
+    return y
+
+
+def embedding(table, tokens, *, out=None):
+    """table[tokens] for int32 CUDA token ids (agent-test/v2/engine.py:108, 147)."""
+    require_bf16_cuda("table", table)
+    if not isinstance(tokens, torch.Tensor) or tokens.dtype != torch.int32 or not tokens.is_cuda \
+            or not tokens.is_contiguous():
+        raise ValueError("tokens must be a contiguous int32 CUDA tensor")
+    require_same_device(table, tokens)
+    vocab, hidden = table.shape
+    n = tokens.numel()
+    if n < 1:
+        raise ValueError("no tokens")
+    y = _out_or_new(out, (n, hidden), torch.bfloat16, table.device, "out")
+    st = _lib.load().rib_embed(table.data_ptr(), vocab, hidden, tokens.data_ptr(), n, y.data_ptr(),
+                               stream_handle(table.device))
+    _lib.check(st, "embedding")
+    return y
+
+
+_argmax_ws: dict = {}
+
+
+def argmax(logits, *, out=None, workspace=None):
+    """Index of the largest FP32 logit (the first on ties) as an int32 [1]
+    CUDA tensor (mx.argmax at agent-test/v2/engine.py:163)."""
+    if not isinstance(logits, torch.Tensor) or logits.dtype != torch.float32 or not logits.is_cuda \
+            or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous float32 CUDA tensor")
+    dev = logits.device
+    y = _out_or_new(out, (1,), torch.int32, dev, "out")
+    if workspace is None:
+        key = (dev.index, stream_handle(dev))
+        workspace = _argmax_ws.get(key)
+        if workspace is None:
+            workspace = torch.empty(int(_lib.load().rib_argmax_workspace_bytes()), dtype=torch.uint8,
+                                    device=dev)
+            _argmax_ws[key] = workspace
+    st = _lib.load().rib_argmax_f32(logits.data_ptr(), logits.numel(), y.data_ptr(), workspace.data_ptr(),
+                                    stream_handle(dev))
+    _lib.check(st, "argmax")
+    return y

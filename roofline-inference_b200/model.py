@@ -1,0 +1,388 @@
+"""Qwen3 forward on B200 around the attention kernels: the reference's v2
+engine (agent-test/v2/engine.py) restated for CUDA.
+
+  Qwen3Config, random_weights(cfg, seed)   dense Qwen3 with tied embeddings
+                                           (engine.py:58-88 preconditions)
+  Engine(weights)
+    .new_cache(capacity)                   Cache [L, 2, nkv, cap, 128]
+    .prefill(tokens, cache, last=...)      engine.py:102-142
+    .decode(token, cache)                  engine.py:145-163 (eager)
+    .decode_graph(cache)                   the same step captured in a CUDA graph
+    .generate(prompt, max_tokens, ...)     engine.py:165-192, one token of lookahead
+
+Per decode step and layer the engine launches the reference's seven kernels
+with two of them fused: norm + QKV GEMV, qk-norm + RoPE + KV append (one
+kernel), split-KV decode attention, O GEMV + residual, norm + gate/up GEMV +
+SwiGLU, down GEMV + residual; then the final norm + LM-head GEMV and argmax.
+Prefill uses cuBLAS GEMMs (torch.matmul) for the projections, the tcgen05
+prefill kernel for attention and this library's add_rms / SwiGLU kernels; as
+in the reference, the last layer runs attention and MLP for the final row only
+and the logits cover the final row only.
+"""
+from __future__ import annotations
+
+import threading
+from collections.abc import Iterator
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .attention import attention, decode_attention
+from .cache import Cache
+from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope_append, qk_norm_rope_append_at,
+                      rms_norm, swiglu)
+from ._tensors import HEAD_DIM, stream_handle
+
+
+@dataclass(frozen=True)
+class Qwen3Config:
+    num_layers: int = 28
+    hidden_size: int = 1024
+    num_heads: int = 16
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 3072
+    vocab_size: int = 151936
+    rope_theta: float = 1e6
+    rms_norm_eps: float = 1e-6
+
+    def validate(self) -> None:
+        """The kernels' preconditions (engine.py:69-70 plus the GEMV's K % 256)."""
+        if self.head_dim != HEAD_DIM or self.num_heads != 2 * self.num_kv_heads:
+            raise ValueError("Kernels assume head_dim 128 and GQA factor 2")
+        if self.hidden_size % 256 or self.intermediate_size % 256 or (self.num_heads * 128) % 256:
+            raise ValueError("hidden, intermediate and q widths must be multiples of 256")
+        if abs(self.rms_norm_eps - 1e-6) > 1e-12:
+            raise ValueError("the kernels' RMSNorm eps is 1e-6")
+
+    @property
+    def q_dim(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+
+QWEN3_0_6B = Qwen3Config()
+
+
+class Qwen3Weights:
+    """BF16 weights in the engine's fused layout (engine.py:80-88): per layer
+    qkv = [q_proj; k_proj; v_proj], gu = [gate_proj; up_proj], o, down and the
+    four norm vectors; `embed` doubles as the LM head (tied)."""
+
+    def __init__(self, config: Qwen3Config, embed, final_norm, layers: list[dict]):
+        config.validate()
+        self.config = config
+        self.embed = embed
+        self.final_norm = final_norm
+        self.layers = layers
+
+    def to(self, device) -> "Qwen3Weights":
+        mv = lambda t: t.to(device)
+        return Qwen3Weights(self.config, mv(self.embed), mv(self.final_norm),
+                            [{k: mv(v) for k, v in l.items()} for l in self.layers])
+
+    def nbytes(self) -> int:
+        n = self.embed.numel() + self.final_norm.numel()
+        n += sum(v.numel() for l in self.layers for v in l.values())
+        return 2 * n
+
+
+def random_weights(config: Qwen3Config = QWEN3_0_6B, seed: int = 0, device="cpu", std: float = 0.02,
+                   norm_std: float = 0.1) -> Qwen3Weights:
+    """Random-init weights: matrices N(0, std), norm weights 1 + N(0, norm_std),
+    drawn from torch.Generator(device).manual_seed(seed) in a fixed order."""
+    config.validate()
+    dev = torch.device(device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    d, q, kv, f = config.hidden_size, config.q_dim, config.kv_dim, config.intermediate_size
+
+    def mat(r, c):
+        return (torch.randn((r, c), generator=g, device=dev) * std).to(torch.bfloat16)
+
+    def norm(n):
+        return (1.0 + norm_std * torch.randn((n,), generator=g, device=dev)).to(torch.bfloat16)
+
+    embed = mat(config.vocab_size, d)
+    layers = []
+    for _ in range(config.num_layers):
+        layers.append(dict(qkv=mat(q + 2 * kv, d), o=mat(d, q), gu=mat(2 * f, d), down=mat(d, f),
+                           in_norm=norm(d), post_norm=norm(d), q_norm=norm(HEAD_DIM), k_norm=norm(HEAD_DIM)))
+    return Qwen3Weights(config, embed, norm(d), layers)
+
+
+def _linear(x, W):
+    """x [m, k] @ W[n, k]^T: a plain cuBLAS BF16 GEMM (FP32 accumulate, BF16 out)."""
+    return torch.matmul(x, W.t())
+
+
+class Engine:
+    def __init__(self, weights: Qwen3Weights):
+        cfg = weights.config
+        cfg.validate()
+        if not weights.embed.is_cuda:
+            raise ValueError("weights must be on a CUDA device")
+        _lib.load()  # fail loudly now if the CUDA library is missing
+        self.cfg = cfg
+        self.w = weights
+        self.device = weights.embed.device
+        self.n_heads, self.n_kv = cfg.num_heads, cfg.num_kv_heads
+        self.scale = HEAD_DIM ** -0.5
+        self.base = cfg.rope_theta
+        self.layers = weights.layers
+        self.embed = weights.embed
+        self.final_norm = weights.final_norm
+        self._sessions: dict[int, tuple[Cache, DecodeGraph]] = {}
+
+    def new_cache(self, capacity: int) -> Cache:
+        return Cache(self.cfg.num_layers, self.n_kv, HEAD_DIM, capacity, device=self.device)
+
+    # ---------------- prefill (M >= 1) ----------------
+    def prefill(self, tokens, cache: Cache, *, last: bool, all_logits: bool = False):
+        """tokens: int32 CUDA [1, n] or [n].  Writes the K/V of every layer at
+        [offset, offset+n) and advances cache.offset.  If `last`, returns the
+        FP32 logits [1, 1, vocab] of the final row ([1, n, vocab] with
+        all_logits), as engine.py:102-142."""
+        tokens = tokens.reshape(-1)
+        n = tokens.numel()
+        off = cache.offset
+        if off + n > cache.capacity:
+            raise ValueError("KV capacity exceeded")
+        Lp = (n + 31) // 32 * 32
+        nl = len(self.layers)
+        h = embedding(self.embed, tokens)                                   # [n, hidden]
+        x = rms_norm(h, self.layers[0]["in_norm"])
+        for i, w in enumerate(self.layers):
+            q = qk_norm_rope_append(_linear(x, w["qkv"]), w["q_norm"], w["k_norm"], off, self.n_heads,
+                                    self.n_kv, self.base, cache.kv[i], Lp)    # [nq, Lp, 128]
+            final = i == nl - 1
+            if final and not last:
+                break        # last layer's K/V written; its outputs are dead for a middle chunk
+            if final and not all_logits:
+                # Only the final row feeds the logits: attention/MLP for one row (engine.py:118-121).
+                qrow = q[:, n - 1, :].contiguous()
+                o = decode_attention(qrow, cache.kv[i], off + n, self.scale).reshape(1, -1)
+                h = h[n - 1:]
+            else:
+                kvl = cache.kv[i]
+                o = attention(q, kvl[0], kvl[1], n, off + n, self.scale)     # [n, H*128]
+            h, x = add_rms(h, _linear(o, w["o"]), w["post_norm"])
+            r = _linear(swiglu(_linear(x, w["gu"])), w["down"])
+            if final:
+                h = h + r
+            else:
+                h, x = add_rms(h, r, self.layers[i + 1]["in_norm"])
+        cache.offset += n
+        if not last:
+            return None
+        if all_logits:
+            hn = rms_norm(h, self.final_norm)
+            return torch.matmul(hn.float(), self.embed.float().t())[None]
+        return gemv(self.embed, h.reshape(-1), nw=self.final_norm, out_float=True)[None, None]
+
+    # ---------------- decode (M = 1), eager ----------------
+    def decode(self, token, cache: Cache, *, return_logits: bool = False):
+        """token: int32 CUDA [1].  Returns the next greedy token, int32 CUDA [1]
+        (or the FP32 logits [vocab]), as engine.py:145-163."""
+        pos = cache.offset
+        n = pos + 1
+        if n > cache.capacity:
+            raise ValueError("KV capacity exceeded")
+        h = embedding(self.embed, token.reshape(-1)).reshape(-1)
+        for i, w in enumerate(self.layers):
+            qkv = gemv(w["qkv"], h, nw=w["in_norm"])
+            q = qk_norm_rope_append(qkv, w["q_norm"], w["k_norm"], pos, self.n_heads, self.n_kv,
+                                    self.base, cache.kv[i])
+            o = decode_attention(q, cache.kv[i], n, self.scale)
+            h = gemv(w["o"], o.reshape(-1), res=h)
+            a = gemv(w["gu"], h, nw=w["post_norm"], swiglu=True)
+            h = gemv(w["down"], a, res=h)
+        cache.offset += 1
+        logits = gemv(self.embed, h, nw=self.final_norm, out_float=True)
+        if return_logits:
+            return logits
+        return argmax(logits)
+
+    def decode_graph(self, cache: Cache) -> "DecodeGraph":
+        return DecodeGraph(self, cache)
+
+    def session(self, capacity: int) -> tuple[Cache, "DecodeGraph"]:
+        """A cache of at least `capacity` positions with its captured decode
+        graph, reused across requests (capacity rounded up to 1024): rows
+        past the offset are never read, so a request only resets the offset.
+        One request at a time per session."""
+        bucket = (capacity + 1023) // 1024 * 1024
+        sess = self._sessions.get(bucket)
+        if sess is None:
+            cache = self.new_cache(bucket)
+            sess = (cache, DecodeGraph(self, cache))
+            self._sessions[bucket] = sess
+        sess[0].offset = 0
+        return sess
+
+    # ---------------- generation ----------------
+    def generate(self, prompt: list[int], *, max_tokens: int = 65, chunk: int = 4096, eos_ids=(),
+                 use_graph: bool = True) -> Iterator[int]:
+        """Greedy generation (engine.py:165-192): chunked prefill, the first
+        token, then decode steps with one step of lookahead (step t+1 is
+        enqueued before token t is read on the host).  With use_graph the
+        steps replay the session's captured CUDA graph."""
+        if not prompt or max_tokens < 0 or chunk < 1:
+            raise ValueError("Nonempty prompt, nonnegative max_tokens, positive chunk required")
+        if min(prompt) < 0 or max(prompt) >= self.cfg.vocab_size:
+            raise ValueError("Token outside vocabulary")
+        if max_tokens == 0:
+            return
+        eos_ids = set(eos_ids)
+        need = len(prompt) + max_tokens + 1
+        if use_graph:
+            cache, graph = self.session(need)
+        else:
+            cache, graph = self.new_cache(need), None
+        tokens = torch.tensor(prompt, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
+        logits = None
+        for start in range(0, len(prompt), chunk):
+            end = min(len(prompt), start + chunk)
+            logits = self.prefill(tokens[start:end], cache, last=end == len(prompt))
+        y = argmax(logits.reshape(-1))
+        if graph is not None:
+            yield from graph.run(y, max_tokens, eos_ids)
+            return
+        host = torch.empty(1, dtype=torch.int32).pin_memory()
+        for _ in range(max_tokens):
+            host.copy_(y, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            nxt = self.decode(y, cache) if cache.offset + 1 <= cache.capacity else None
+            ev.synchronize()
+            token = int(host[0])
+            yield token
+            if token in eos_ids or nxt is None:
+                break
+            y = nxt
+
+
+class DecodeGraph:
+    """One decode step captured in a CUDA graph.
+
+    Static device state: the input token (overwritten in place by the step's
+    argmax), the position and the key count (advanced by the step itself), the
+    per-layer cache pointers and every intermediate buffer.  The decode
+    attention geometry is fixed at capture time for max_n = cache.capacity and
+    reads the live key count from the device, so one graph serves every
+    position of this cache.  Replays on the stream that was current at
+    construction."""
+
+    _capture_lock = threading.Lock()
+
+    def __init__(self, engine: Engine, cache: Cache):
+        self.e, self.cache = engine, cache
+        cfg, dev = engine.cfg, engine.device
+        self.device = dev
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.nkeys = torch.ones(1, dtype=torch.int32, device=dev)
+        self.ptrs = torch.tensor([cache.kv[i].data_ptr() for i in range(cfg.num_layers)],
+                                 dtype=torch.int64, device=dev)
+        d, qkvw = cfg.hidden_size, cfg.q_dim + 2 * cfg.kv_dim
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.h = [torch.empty(d, **bf), torch.empty(d, **bf), torch.empty(d, **bf)]
+        self.x = torch.empty((1, d), **bf)
+        self.qkv = torch.empty(qkvw, **bf)
+        self.q = torch.empty((self.e.n_heads, 1, HEAD_DIM), **bf)
+        self.o = torch.empty((1, self.e.n_heads, HEAD_DIM), **bf)
+        self.a = torch.empty(cfg.intermediate_size, **bf)
+        self.logits = torch.empty(cfg.vocab_size, dtype=torch.float32, device=dev)
+        L = _lib.load()
+        self.max_n = cache.capacity
+        ws_bytes = int(L.rib_decode_workspace_bytes(1, self.max_n, cfg.num_kv_heads))
+        self.ws = torch.empty(max(ws_bytes, 1 << 20), dtype=torch.uint8, device=dev)
+        self.argmax_ws = torch.empty(int(L.rib_argmax_workspace_bytes()), dtype=torch.uint8, device=dev)
+        self.launches_per_step = 0
+        self.stream = torch.cuda.current_stream(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        with DecodeGraph._capture_lock:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(self.stream)
+            with torch.cuda.stream(side):
+                # Warm-up run outside the graph (first-call set-up of every launch).
+                # It appends at the last cache row, which no position below it
+                # reads and a real step at that position overwrites first.
+                if cache.offset < cache.capacity - 1:
+                    self.pos.fill_(cache.capacity - 1)
+                    self.nkeys.fill_(cache.capacity)
+                    self._step(count=True)
+            self.stream.wait_stream(side)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(self.graph, stream=side):
+                self._step(count=False)
+            self.stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+
+    def _step(self, count: bool) -> None:
+        e, cfg, L = self.e, self.e.cfg, _lib.load()
+        st = stream_handle(self.device)
+        launches = 0
+        h = embedding(e.embed, self.tok, out=self.h[0].view(1, -1)).view(-1)
+        launches += 1
+        for i, w in enumerate(e.layers):
+            gemv(w["qkv"], h, nw=w["in_norm"], out=self.qkv)
+            qk_norm_rope_append_at(self.qkv, w["q_norm"], w["k_norm"], self.pos, e.n_heads, e.n_kv, e.base,
+                                   self.cache.kv[i], out=self.q)
+            rc = L.rib_decode_attention_batched(self.q.data_ptr(), self.ptrs.data_ptr() + 8 * i,
+                                                self.nkeys.data_ptr(), 1, self.max_n, self.cache.capacity,
+                                                e.n_heads, e.n_kv, float(e.scale), self.o.data_ptr(),
+                                                self.ws.data_ptr(), self.ws.numel(), st)
+            _lib.check(rc, "decode_attention_batched")
+            h1 = gemv(w["o"], self.o.view(-1), res=h, out=self.h[1])
+            gemv(w["gu"], h1, nw=w["post_norm"], swiglu=True, out=self.a)
+            h = gemv(w["down"], self.a, res=h1, out=self.h[2 if h is not self.h[2] else 0])
+            launches += 5
+        gemv(e.embed, h, nw=e.final_norm, out_float=True, out=self.logits)
+        argmax(self.logits, out=self.tok, workspace=self.argmax_ws)
+        launches += 2
+        self.pos.add_(1)
+        self.nkeys.add_(1)
+        if count:
+            self.launches_per_step = launches
+
+    def set_state(self, token, pos: int) -> None:
+        """Next replay decodes `token` (int32 CUDA [1] or int) at position `pos`."""
+        if isinstance(token, torch.Tensor):
+            self.tok.copy_(token.reshape(-1)[:1])
+        else:
+            self.tok.fill_(int(token))
+        self.pos.fill_(int(pos))
+        self.nkeys.fill_(int(pos) + 1)
+
+    def replay(self) -> None:
+        """One decode step: reads tok/pos, appends K/V at pos, writes the next
+        token into tok and advances pos.  Advances cache.offset on the host."""
+        if self.cache.offset + 1 > self.cache.capacity:
+            raise ValueError("KV capacity exceeded")
+        self.graph.replay()
+        self.cache.offset += 1
+
+    def run(self, first_token, max_tokens: int, eos_ids=()) -> Iterator[int]:
+        """Yields max_tokens tokens starting with first_token (int32 CUDA [1]),
+        replaying the graph for each next one with one step of lookahead."""
+        self.set_state(first_token, self.cache.offset)
+        host = torch.empty(max_tokens, dtype=torch.int32).pin_memory()
+        events = []
+        for t in range(max_tokens):
+            host[t:t + 1].copy_(self.tok, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+            events.append(ev)
+            more = t + 1 < max_tokens and self.cache.offset + 1 <= self.cache.capacity
+            if more:
+                self.replay()
+            ev.synchronize()
+            token = int(host[t])
+            yield token
+            if token in eos_ids or not more:
+                break

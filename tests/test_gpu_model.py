@@ -1,0 +1,235 @@
+"""GPU: the model kernels (csrc/model_kernels.cuh) and the Qwen3 engine
+against the numpy model oracle (oracle/model_np.py).
+
+Tolerances: the CUDA path sums in FP32, the oracle in FP64, so a BF16 result
+may sit one BF16 step away where the exact value is near a rounding boundary;
+the checks allow one step (2^-8 relative) on a small fraction of elements and
+exact equality elsewhere.  Engine logits: max-abs <= 2e-2 and mean-abs <= 2e-3,
+both relative to the largest logit; greedy tokens equal wherever the oracle's
+top-2 margin exceeds the measured logit error."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT  # noqa: F401
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def mnp():
+    from oracle import model_np
+    return model_np
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def bf(x: np.ndarray) -> np.ndarray:
+    from oracle.reference_np import bf16_to_f32
+    return bf16_to_f32(x)
+
+
+def rand_bf16(shape, seed, scale=1.0, device=DEV):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(torch.bfloat16).to(device)
+
+
+def assert_bf16_close(got: np.ndarray, want: np.ndarray, frac_exact=0.98, rel=2.0 ** -7, abs_tol=0.0):
+    """Every element within `rel` of the oracle (one BF16 step is 2^-8) plus
+    `abs_tol` (FP32-vs-FP64 summation error); most elements identical."""
+    a, b = bf(got).astype(np.float64), bf(want).astype(np.float64)
+    tol = rel * np.abs(b) + abs_tol + 1e-30
+    assert np.all(np.abs(a - b) <= tol), float(np.max(np.abs(a - b) / tol))
+    assert np.mean(a == b) >= frac_exact, float(np.mean(a == b))
+
+
+def gemv_abs_tol(mnp, W, x, nw):
+    """Per-row bound for a dot product summed in FP32 instead of FP64, plus one
+    BF16 step of the pre-epilogue value (residual and SwiGLU round it first)."""
+    xin = mnp.rms_norm(u16(x), u16(nw)) if nw is not None else u16(x)
+    Wf, xf = np.abs(bf(u16(W)).astype(np.float64)), np.abs(bf(xin).astype(np.float64))
+    acc = bf(u16(W)).astype(np.float64) @ bf(xin).astype(np.float64)
+    return 1e-5 * (Wf @ xf) + 2.0 ** -7 * np.abs(acc)
+
+
+# ------------------------------------------------------------------ GEMV
+@pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 2048), (1024, 3072), (1000, 512), (40, 256)])
+@pytest.mark.parametrize("epi", ["none", "norm", "res", "swiglu"])
+def test_gemv(rib, mnp, N, K, epi):
+    W = rand_bf16((N, K), 1, 0.05)
+    x = rand_bf16((K,), 2)
+    nw = rand_bf16((K,), 3, 0.1) + 1 if epi in ("norm", "swiglu") else None
+    res = rand_bf16((N,), 4) if epi == "res" else None
+    y = rib.gemv(W, x, nw=nw, res=res, swiglu=epi == "swiglu")
+    want = mnp.gemv(u16(W), u16(x), nw=None if nw is None else u16(nw), res=None if res is None else u16(res),
+                    swiglu_epi=epi == "swiglu")
+    assert y.shape == ((N // 2,) if epi == "swiglu" else (N,))
+    tol = gemv_abs_tol(mnp, W, x, nw)
+    if epi == "swiglu":  # y = bf16(silu(g) * u): the gate and up errors both scale y
+        g, u = bf(mnp.gemv(u16(W), u16(x), nw=u16(nw))).astype(np.float64).reshape(2, -1)
+        tol = 2 * (tol[:N // 2] * np.abs(u) + tol[N // 2:] * np.abs(g))
+        assert_bf16_close(u16(y), want, rel=2.0 ** -6, abs_tol=tol)
+    else:
+        assert_bf16_close(u16(y), want, abs_tol=tol)
+
+
+def test_gemv_lm_head_logits(rib, mnp):
+    """The tall LM-head shape (rows-per-warp 4 path), FP32 out, fused final norm."""
+    V, K = 151936, 1024
+    W = rand_bf16((V, K), 5, 0.02)
+    x, nw = rand_bf16((K,), 6), rand_bf16((K,), 7, 0.1) + 1
+    y = rib.gemv(W, x, nw=nw, out_float=True)
+    want = mnp.gemv(u16(W), u16(x), nw=u16(nw), out_float=True)
+    yh = y.cpu().numpy()
+    scale = np.abs(bf(u16(W))).astype(np.float64) @ np.abs(bf(mnp.rms_norm(u16(x), u16(nw))))
+    assert np.all(np.abs(yh - want) <= 1e-5 * scale + 1e-6)
+    assert int(rib.argmax(y).item()) == int(np.argmax(want)) or \
+        abs(np.sort(want)[-1] - np.sort(want)[-2]) < 1e-4
+
+
+def test_gemv_output_buffer_and_errors(rib):
+    W, x = rand_bf16((64, 256), 8), rand_bf16((256,), 9)
+    out = torch.empty(64, dtype=torch.bfloat16, device=DEV)
+    assert rib.gemv(W, x, out=out).data_ptr() == out.data_ptr()
+    with pytest.raises(ValueError):
+        rib.gemv(W, rand_bf16((128,), 1))
+    with pytest.raises(ValueError):
+        rib.gemv(W, x, res=rand_bf16((64,), 1), out_float=True)
+
+
+# ------------------------------------------------------------------ row kernels
+@pytest.mark.parametrize("rows,W", [(1, 1024), (37, 1024), (5, 256), (3, 3072)])
+def test_add_rms_and_rms_norm(rib, mnp, rows, W):
+    a, b, w = rand_bf16((rows, W), 10), rand_bf16((rows, W), 11), rand_bf16((W,), 12, 0.1) + 1
+    r, n = rib.add_rms(a, b, w)
+    wr, wn = mnp.add_rms(u16(a), u16(b), u16(w))
+    np.testing.assert_array_equal(u16(r), wr)           # one rounded add: exact
+    assert_bf16_close(u16(n), wn)
+    assert_bf16_close(u16(rib.rms_norm(a, w)), mnp.rms_norm(u16(a), u16(w)))
+
+
+@pytest.mark.parametrize("rows,F", [(1, 3072), (33, 3072), (4, 16)])
+def test_swiglu(rib, mnp, rows, F):
+    gu = rand_bf16((rows, 2 * F), 13, 2.0)
+    assert_bf16_close(u16(rib.swiglu(gu)), mnp.swiglu(u16(gu)), frac_exact=0.98, rel=2.0 ** -6)
+
+
+def test_embedding_and_bad_token(rib):
+    table = rand_bf16((1000, 1024), 14)
+    toks = torch.tensor([0, 999, 5, 5], dtype=torch.int32, device=DEV)
+    y = rib.embedding(table, toks)
+    assert torch.equal(y, table[toks.long()])
+    rib._lib.take_device_status()
+    bad = rib.embedding(table, torch.tensor([3, 1000], dtype=torch.int32, device=DEV))
+    assert rib._lib.take_device_status() == 1          # RIB_EINVAL recorded on the device
+    assert torch.equal(bad[0], table[3]) and not bad[1].any()
+
+
+def test_argmax_first_on_ties(rib):
+    x = torch.randn(151936, device=DEV)
+    assert int(rib.argmax(x).item()) == int(torch.argmax(x).item())
+    x[:] = -1.0
+    x[700] = 5.0
+    x[70000] = 5.0
+    x[150000] = 5.0
+    assert int(rib.argmax(x).item()) == 700
+    small = torch.tensor([-3.0, -1.0, -2.0], device=DEV)
+    assert int(rib.argmax(small).item()) == 1
+
+
+def test_append_at_device_offset(rib):
+    nq, nkv = 16, 8
+    qkv = rand_bf16((3, (nq + 2 * nkv) * 128), 15)
+    qw, kw = rand_bf16((128,), 16, 0.1) + 1, rand_bf16((128,), 17, 0.1) + 1
+    c1 = torch.zeros((2, nkv, 256, 128), dtype=torch.bfloat16, device=DEV)
+    c2 = c1.clone()
+    q1 = rib.qk_norm_rope_append(qkv, qw, kw, 77, nq, nkv, 1e6, c1, 32)
+    off = torch.tensor([77], dtype=torch.int32, device=DEV)
+    q2 = rib.qk_norm_rope_append_at(qkv, qw, kw, off, nq, nkv, 1e6, c2, 32)
+    assert torch.equal(q1, q2) and torch.equal(c1, c2)
+    # offset + L past the capacity: caught on the device, nothing written
+    rib._lib.take_device_status()
+    c3 = torch.zeros_like(c1)
+    rib.qk_norm_rope_append_at(qkv, qw, kw, torch.tensor([254], dtype=torch.int32, device=DEV), nq, nkv,
+                               1e6, c3, 32)
+    assert rib._lib.take_device_status() == 2          # RIB_ECAPACITY
+    assert not c3.any()
+
+
+# ------------------------------------------------------------------ engine
+def _engine_check(rib, mnp, cfg, n_prompt, n_decode, seed):
+    wt = rib.random_weights(cfg, seed=seed)               # CPU, seeded
+    oracle = mnp.Qwen3Oracle(mnp.weights_to_numpy(wt), cfg, n_prompt + n_decode + 8)
+    eng = rib.Engine(wt.to(DEV))
+    cache = eng.new_cache(n_prompt + n_decode + 8)
+    toks = np.random.default_rng(seed).integers(0, cfg.vocab_size, n_prompt).astype(np.int32)
+    got = [eng.prefill(torch.tensor(toks, device=DEV), cache, last=True).reshape(-1).cpu().numpy()]
+    want = [oracle.prefill(toks)]
+    tok = int(np.argmax(want[0]))
+    for _ in range(n_decode):
+        got.append(eng.decode(torch.tensor([tok], dtype=torch.int32, device=DEV), cache,
+                              return_logits=True).cpu().numpy())
+        want.append(oracle.decode(tok))
+        tok = int(np.argmax(want[-1]))
+    assert cache.offset == oracle.offset == n_prompt + n_decode
+    for g, w in zip(got, want):
+        scale = np.abs(w).max()
+        err = np.abs(g - w)
+        assert err.max() <= 2e-2 * scale and err.mean() <= 2e-3 * scale, (err.max() / scale, err.mean() / scale)
+        top2 = np.sort(w)[-2:]
+        if top2[1] - top2[0] > 2 * err.max():
+            assert int(np.argmax(g)) == int(np.argmax(w))
+    return eng
+
+
+def test_engine_tiny_matches_oracle(rib, mnp):
+    cfg = rib.Qwen3Config(num_layers=2, hidden_size=256, num_heads=2, num_kv_heads=1,
+                          intermediate_size=512, vocab_size=1000)
+    _engine_check(rib, mnp, cfg, n_prompt=40, n_decode=5, seed=21)
+
+
+def test_engine_qwen3_shapes_two_layers(rib, mnp):
+    """Qwen3-0.6B widths (hidden 1024, 16/8 heads, FFN 3072, vocab 151936), 2 layers."""
+    cfg = rib.Qwen3Config(num_layers=2)
+    _engine_check(rib, mnp, cfg, n_prompt=300, n_decode=3, seed=22)
+
+
+def test_decode_graph_matches_eager(rib):
+    cfg = rib.Qwen3Config(num_layers=3, hidden_size=256, num_heads=2, num_kv_heads=1,
+                          intermediate_size=512, vocab_size=1000)
+    eng = rib.Engine(rib.random_weights(cfg, seed=23).to(DEV))
+    prompt = list(np.random.default_rng(23).integers(0, cfg.vocab_size, 50))
+    eager = list(eng.generate(prompt, max_tokens=12, use_graph=False))
+    graph = list(eng.generate(prompt, max_tokens=12, use_graph=True))
+    assert len(eager) == 12 and eager == graph
+    # chunked prefill gives the same tokens
+    assert list(eng.generate(prompt, max_tokens=12, chunk=16)) == eager
+
+
+def test_decode_graph_state_and_launch_count(rib):
+    cfg = rib.Qwen3Config(num_layers=2, hidden_size=256, num_heads=2, num_kv_heads=1,
+                          intermediate_size=512, vocab_size=1000)
+    eng = rib.Engine(rib.random_weights(cfg, seed=24).to(DEV))
+    cache = eng.new_cache(64)
+    eng.prefill(torch.arange(10, dtype=torch.int32, device=DEV), cache, last=False)
+    ref_cache = eng.new_cache(64)
+    ref_cache.storage.copy_(cache.storage)
+    ref_cache.offset = cache.offset
+    g = eng.decode_graph(cache)
+    assert g.launches_per_step == 1 + 5 * cfg.num_layers + 2
+    g.set_state(7, cache.offset)
+    toks_g, tok = [], torch.tensor([7], dtype=torch.int32, device=DEV)
+    toks_e = []
+    for _ in range(4):
+        g.replay()
+        toks_g.append(int(g.tok.item()))
+        tok = eng.decode(tok, ref_cache)
+        toks_e.append(int(tok.item()))
+    assert toks_g == toks_e
+    assert int(g.pos.item()) == cache.offset == ref_cache.offset == 14
+    assert torch.equal(cache.storage[:, :, :, :14], ref_cache.storage[:, :, :, :14])

@@ -1,0 +1,140 @@
+"""CPU: host logic of the Qwen3 forward (config checks, weight layout, C-ABI
+argument checks of the model kernels) and self-consistency of the numpy
+model oracle.  No kernel is launched here."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT  # noqa: F401  (puts the repository on sys.path)
+
+FAKE = 0x10000        # 16-byte aligned dummy device address; never dereferenced
+MISALIGNED = 0x10008
+
+
+@pytest.fixture(scope="module")
+def mnp():
+    from oracle import model_np
+    return model_np
+
+
+def tiny_config(rib, layers=2):
+    return rib.Qwen3Config(num_layers=layers, hidden_size=256, num_heads=2, num_kv_heads=1,
+                           intermediate_size=512, vocab_size=1000)
+
+
+# ------------------------------------------------------------------ config / weights
+def test_config_preconditions(rib):
+    rib.QWEN3_0_6B.validate()
+    assert rib.QWEN3_0_6B.q_dim == 2048 and rib.QWEN3_0_6B.kv_dim == 1024
+    with pytest.raises(ValueError):
+        rib.Qwen3Config(num_heads=16, num_kv_heads=4).validate()   # GQA factor must be 2
+    with pytest.raises(ValueError):
+        rib.Qwen3Config(hidden_size=1000).validate()               # GEMV K % 256
+    with pytest.raises(ValueError):
+        rib.Qwen3Config(head_dim=64).validate()
+
+
+def test_random_weights_layout(rib):
+    cfg = tiny_config(rib)
+    w = rib.random_weights(cfg, seed=3)
+    l0 = w.layers[0]
+    assert tuple(l0["qkv"].shape) == (cfg.q_dim + 2 * cfg.kv_dim, cfg.hidden_size)
+    assert tuple(l0["o"].shape) == (cfg.hidden_size, cfg.q_dim)
+    assert tuple(l0["gu"].shape) == (2 * cfg.intermediate_size, cfg.hidden_size)
+    assert tuple(l0["down"].shape) == (cfg.hidden_size, cfg.intermediate_size)
+    assert tuple(w.embed.shape) == (cfg.vocab_size, cfg.hidden_size)
+    assert all(t.dtype == torch.bfloat16 for t in l0.values())
+    assert abs(float(l0["qkv"].float().std()) - 0.02) < 2e-3
+    w2 = rib.random_weights(cfg, seed=3)
+    assert torch.equal(w.layers[1]["down"], w2.layers[1]["down"])   # seeded
+
+
+def test_engine_requires_cuda_weights(rib):
+    w = rib.random_weights(tiny_config(rib), seed=0)
+    with pytest.raises(ValueError):
+        rib.Engine(w)
+
+
+# ------------------------------------------------------------------ C-ABI checks
+def test_model_entry_points_reject_bad_arguments(rib):
+    L = rib.load_library()
+    # gemv: K not a multiple of 256; residual epilogue without res; swiglu with odd N;
+    # misaligned x
+    assert L.rib_gemv(FAKE, 64, 100, FAKE, None, None, 0, 0, FAKE, None) == 1
+    assert L.rib_gemv(FAKE, 64, 256, FAKE, None, None, 1, 0, FAKE, None) == 1
+    assert L.rib_gemv(FAKE, 63, 256, FAKE, None, None, 2, 0, FAKE, None) == 1
+    assert L.rib_gemv(FAKE, 64, 256, FAKE, None, FAKE, 1, 1, FAKE, None) == 1
+    assert L.rib_gemv(FAKE, 64, 256, MISALIGNED, None, None, 0, 0, FAKE, None) == 3
+    assert L.rib_gemv(FAKE, 64, 256, FAKE, None, None, 7, 0, FAKE, None) == 1
+    # row kernels
+    assert L.rib_add_rms(FAKE, FAKE, FAKE, 0, 1024, FAKE, FAKE, None) == 1
+    assert L.rib_add_rms(FAKE, FAKE, FAKE, 4, 1020, FAKE, FAKE, None) == 1
+    assert L.rib_rms_norm(FAKE, MISALIGNED, 4, 1024, FAKE, None) == 3
+    assert L.rib_swiglu(FAKE, 4, 12, FAKE, None) == 1
+    assert L.rib_embed(FAKE, 100, 1024, FAKE, 0, FAKE, None) == 1
+    assert L.rib_embed(FAKE, 100, 1024, 0x10002, 3, FAKE, None) == 3
+    # argmax and the device-offset append
+    assert L.rib_argmax_workspace_bytes() >= 16
+    assert L.rib_argmax_f32(FAKE, 0, FAKE, FAKE, None) == 1
+    assert L.rib_argmax_f32(FAKE, 10, FAKE, 0x10004, None) == 3
+    assert L.rib_qk_norm_rope_append_dev(FAKE, 1, FAKE, FAKE, None, 16, 8, 1e6, 1, FAKE, FAKE, 256,
+                                         None) == 1
+    assert L.rib_qk_norm_rope_append_dev(FAKE, 1, FAKE, FAKE, 0x10002, 16, 8, 1e6, 1, FAKE, FAKE, 256,
+                                         None) == 3
+
+
+# ------------------------------------------------------------------ oracle
+def _u16(rng, shape, scale=1.0):
+    from oracle.reference_np import f32_to_bf16
+    return f32_to_bf16((rng.standard_normal(shape) * scale).astype(np.float32))
+
+
+def test_oracle_rms_norm_closed_form(mnp):
+    from oracle.reference_np import bf16_to_f32, f32_to_bf16
+    x = f32_to_bf16(np.full(256, 2.0, np.float32))
+    w = f32_to_bf16(np.full(256, 0.5, np.float32))
+    # mean(x^2) = 4, inv = 1/2 (eps negligible at BF16), x*inv = 1, w*1 = 0.5
+    np.testing.assert_array_equal(bf16_to_f32(mnp.rms_norm(x, w)), np.full(256, 0.5, np.float32))
+
+
+def test_oracle_gemv_epilogues_compose(mnp):
+    from oracle.reference_np import bf16_to_f32, f32_to_bf16
+    rng = np.random.default_rng(0)
+    W, x, nw, res = _u16(rng, (64, 256), 0.05), _u16(rng, 256), _u16(rng, 256, 0.1), _u16(rng, 64)
+    plain = mnp.gemv(W, x, nw=nw)
+    np.testing.assert_array_equal(plain, mnp.matmul(mnp.rms_norm(x, nw)[None], W)[0])
+    r = mnp.gemv(W, x, res=res)
+    np.testing.assert_array_equal(r, f32_to_bf16(bf16_to_f32(res) + bf16_to_f32(mnp.gemv(W, x))))
+    s = mnp.gemv(W, x, swiglu_epi=True)
+    np.testing.assert_array_equal(s, mnp.swiglu(mnp.gemv(W, x)))
+    lg = mnp.gemv(W, x, out_float=True)
+    assert lg.dtype == np.float32 and mnp.argmax(lg) == int(np.argmax(lg))
+
+
+def test_oracle_add_rms(mnp):
+    rng = np.random.default_rng(1)
+    a, b, w = _u16(rng, (3, 256)), _u16(rng, (3, 256)), _u16(rng, 256)
+    r, n = mnp.add_rms(a, b, w)
+    from oracle.reference_np import bf16_to_f32, f32_to_bf16
+    np.testing.assert_array_equal(r, f32_to_bf16(bf16_to_f32(a) + bf16_to_f32(b)))
+    np.testing.assert_array_equal(n, mnp.rms_norm(r, w))
+
+
+def test_oracle_decode_continues_prefill(rib, mnp):
+    """Prefill of n tokens then one decode step gives the logits of a prefill
+    of n+1 tokens: the cache, positions and causal structure agree."""
+    cfg = tiny_config(rib)
+    w = mnp.weights_to_numpy(rib.random_weights(cfg, seed=5))
+    toks = np.random.default_rng(2).integers(0, cfg.vocab_size, 19)
+    a = mnp.Qwen3Oracle(w, cfg, 64)
+    a.prefill(toks[:18])
+    la = a.decode(toks[18])
+    b = mnp.Qwen3Oracle(w, cfg, 64)
+    lb = b.prefill(toks)
+    assert a.offset == b.offset == 19
+    np.testing.assert_allclose(la, lb, atol=2e-2 * np.abs(lb).max())
+    assert np.abs(la - lb).mean() < 2e-3 * np.abs(lb).max()
