@@ -411,6 +411,9 @@ def run_ours(args):
     # ---- prefill (tcgen05 kernel), one GPU's view
     prefill = run_prefill(rib, device, args, pk) if not args.no_prefill else None
 
+    # ---- the full Qwen3-0.6B forward (one replica per GPU)
+    full_model = run_full_model(rib, rank, world, device, args) if not args.no_model else None
+
     device_status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
     if gather is not None:
         gather.close()
@@ -445,6 +448,7 @@ def run_ours(args):
         "per_layer_launches": {"value": per_layer_gbs, "unit": "GB/s", "ms_per_step": per_layer_ms,
                                "frac": per_layer_gbs / pk["hbm_gbs"]},
         "prefill": prefill,
+        "full_model": full_model,
         "ragged_batch": ragged,
         "e2e": e2e,
         "gpu_launches": args.steps,
@@ -650,6 +654,85 @@ def sm_clock_mhz(device):
         return None
 
 
+def run_full_model(rib, rank, world, device, args):
+    """Qwen3-0.6B forward with random N(0, 0.02) weights (28 layers, hidden
+    1024, 16/8 heads, FFN 3072, vocab 151936, tied embeddings, BF16): the
+    engine's CUDA-graph decode step at context 32768 (K/V seeded N(0, 1)), and
+    a 4096-token prompt + 128 generated tokens through Engine.generate (host
+    token ids in, host token ids out; wall clock).  Each GPU runs its own
+    replica; times are the max over ranks, tokens/s the sum over ranks.  Each
+    figure is reported against the full-model Level-A line (cold start)."""
+    rl = importlib.import_module("roofline-inference_b200.roofline_line")
+    cfg = rib.QWEN3_0_6B
+    eng = rib.Engine(rib.random_weights(cfg, seed=11 + rank, device=device))
+    out = {"model": "Qwen3-0.6B, random-init N(0, 0.02) weights, BF16", "replicas": world}
+
+    # decode step at context 32768
+    ctx, steps, warm = 32768, max(1, min(args.steps, 200)), max(3, min(args.warmup, 20))
+    cache = eng.new_cache(ctx + steps + warm + 8)
+    g = torch.Generator(device=device)
+    g.manual_seed(12 + rank)
+    for i in range(cfg.num_layers):
+        cache.storage[i, :, :, :ctx].normal_(generator=g)
+    cache.offset = ctx
+    dg = eng.decode_graph(cache)
+    dg.set_state(1, ctx)
+    for _ in range(warm):
+        dg.replay()
+    stream = torch.cuda.current_stream(device)
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        dg.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / steps, world, device)
+    line = rl.model_decode_line(cfg, ctx + warm)
+    out["decode_step"] = {
+        "context": f"{ctx + warm}..{ctx + warm + steps}", "steps": steps, "ms_per_token": ms,
+        "tokens_per_s": world * 1000.0 / ms, "launches_per_step": dg.launches_per_step,
+        "path": "one CUDA-graph replay per token (embedding, 28 x [norm+QKV GEMV, qk-norm+RoPE+KV "
+                "append, split-KV decode attention, O GEMV+residual, norm+gate/up GEMV+SwiGLU, "
+                "down GEMV+residual], final norm + LM-head GEMV, argmax)",
+        "reference_line_ms": line["time_s"] * 1e3, "reference_bottleneck": line["bottleneck"],
+        "fraction_of_line": line["time_s"] * 1e3 / ms}
+    del dg, cache
+    torch.cuda.empty_cache()
+
+    # a 4096-token prompt + 128 generated tokens
+    P, G = 4096, 128
+    prompt = torch.randint(0, cfg.vocab_size, (P,), generator=torch.Generator().manual_seed(13 + rank))
+    prompt = prompt.tolist()
+    list(eng.generate(prompt, max_tokens=G))          # warm-up: captures the session's graph
+    ttft, dec, tot = [], [], []
+    for _ in range(3):
+        barrier(world)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        it = eng.generate(prompt, max_tokens=G)
+        next(it)
+        t1 = time.perf_counter()
+        rest = list(it)
+        t2 = time.perf_counter()
+        if len(rest) != G - 1:
+            raise RuntimeError(f"generated {len(rest) + 1} tokens, expected {G}")
+        ttft.append(max_over_ranks(t1 - t0, world, device))
+        dec.append(max_over_ranks(t2 - t1, world, device))
+        tot.append(max_over_ranks(t2 - t0, world, device))
+    rline = rl.request_line(cfg, P, G)
+    t_ttft, t_dec, t_tot = statistics.median(ttft), statistics.median(dec), statistics.median(tot)
+    out["request"] = {
+        "prompt": P, "generated": G, "repeats": 3, "timing": "host wall clock, median",
+        "ttft_ms": t_ttft * 1e3, "decode_tokens_per_s": world * (G - 1) / t_dec,
+        "total_ms": t_tot * 1e3,
+        "reference_line": {"ttft_ms": rline["ttft_s"] * 1e3, "total_ms": rline["total_s"] * 1e3},
+        "fraction_ttft": rline["ttft_s"] / t_ttft, "fraction_total": rline["total_s"] / t_tot}
+    return out
+
+
 def run_case(case: str):
     """Bounded workloads for ncu captures: decode-small is the layer-batched
     decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
@@ -683,6 +766,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
     ap.add_argument("--case", choices=["decode-small", "prefill-small"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()

@@ -78,3 +78,55 @@ def prefill_attention_line(qL: int, kL: int | None = None, nq: int = 16, nkv: in
 def fraction(line: dict, measured_s: float) -> float:
     """Line time / measured time: 1.0 means the measurement sits on the bound."""
     return line["time_s"] / measured_s
+
+
+# ------------------------------------------------------------------ full model
+# Qwen3 forward lines, restating src/roofline/workload.py:decode/prefill and
+# bound.py:request_time for a dense GQA model with tied embeddings; cold start
+# (initial_resident_bytes = 0 in bound.py:96-116).
+
+def _params(cfg) -> dict:
+    d, q, kv, f = cfg.hidden_size, cfg.q_dim, cfg.kv_dim, cfg.intermediate_size
+    linear = d * q + 2 * d * kv + q * d + 3 * d * f                  # model.py layer_linear_params
+    norms = 2 * d + 2 * cfg.head_dim                                   # model.py layer_norm_params (qk_norm)
+    return {"linear": linear, "norms": norms,
+            "weights_read": (cfg.num_layers * (linear + norms) + d + cfg.vocab_size * d) * 2}
+
+
+def model_decode_line(cfg, context: int, batch: int = 1, spec: dict | None = None) -> dict:
+    """One decode step with `context` cached tokens (workload.py:decode)."""
+    spec = spec or load_spec()
+    P, L = _params(cfg), cfg.num_layers
+    keys = context + 1
+    flops = (2 * L * P["linear"] * batch + 2 * L * cfg.num_heads * cfg.head_dim * 2 * keys * batch
+             + 2 * cfg.vocab_size * cfg.hidden_size * batch)
+    vec = L * cfg.kv_dim * 2                                           # kv_bytes_per_token // 2
+    dram = P["weights_read"] + 2 * batch * 4 + batch * 2 * context * vec + batch * 2 * vec
+    return _line(flops, dram, L * cfg.num_heads * keys * batch, spec)
+
+
+def model_prefill_line(cfg, prompt_len: int, batch: int = 1, spec: dict | None = None) -> dict:
+    """Prefill of a prompt with logits for its last position only
+    (workload.py:prefill with prune_final=True)."""
+    spec = spec or load_spec()
+    P, L, p = _params(cfg), cfg.num_layers, prompt_len
+    pairs = p * (p + 1) // 2
+    d, q, f = cfg.hidden_size, cfg.q_dim, cfg.intermediate_size
+    dead = 2 * d * q + 3 * d * f
+    linear = 2 * L * P["linear"] * batch * p - 2 * dead * batch * (p - 1)
+    final_scores = cfg.num_heads * batch * p
+    attention = 4 * cfg.head_dim * (cfg.num_heads * pairs * batch * (L - 1) + final_scores)
+    flops = linear + attention + 2 * cfg.vocab_size * d * batch
+    dram = P["weights_read"] + (batch * p + batch) * 4 + batch * p * 2 * L * cfg.kv_dim * 2
+    exps = cfg.num_heads * pairs * batch * (L - 1) + final_scores
+    return _line(flops, dram, exps, spec)
+
+
+def request_line(cfg, prompt_len: int, gen: int, spec: dict | None = None) -> dict:
+    """T = TTFT(L) + sum_{i=1}^{gen-1} T_decode(L + i - 1) (bound.py:193-217)."""
+    spec = spec or load_spec()
+    ttft = model_prefill_line(cfg, prompt_len, spec=spec)["time_s"]
+    steps = [model_decode_line(cfg, prompt_len + i - 1, spec=spec)["time_s"] for i in range(1, gen)]
+    return {"ttft_s": ttft, "decode_s": sum(steps), "total_s": ttft + sum(steps),
+            "decode_first_s": steps[0] if steps else 0.0, "decode_last_s": steps[-1] if steps else 0.0,
+            "prompt_len": prompt_len, "gen": gen, "device": spec["name"]}

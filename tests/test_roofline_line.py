@@ -65,3 +65,38 @@ def test_lines_closed_form(rl):
     assert p["bottleneck"] == "compute"
     assert p["time_s"] == pytest.approx(4096 * 32768 * 32769 / spec["bf16"])
     assert rl.fraction(p, 2 * p["time_s"]) == pytest.approx(0.5)
+
+
+def test_model_lines_match_reference(rl, reference_roofline):
+    """Full-model lines equal the reference's own physical bound (cold start)
+    for Qwen3-0.6B on configs/b200.yaml."""
+    import importlib as _il
+    cfg = _il.import_module("roofline-inference_b200").QWEN3_0_6B
+    model = reference_roofline.load_model(REF_MODEL)
+    dev = reference_roofline.load_device(rl.SPEC)
+    for ctx in (512, 4096, 32768):
+        w = reference_roofline.decode(model, 1, ctx)
+        b = reference_roofline.physical_bound(w, dev, initial_resident_bytes=0)
+        line = rl.model_decode_line(cfg, ctx)
+        assert line["flops"] == w.total_flops
+        assert line["dram_bytes"] == pytest.approx(b.traffic["total"])
+        assert line["time_s"] == pytest.approx(b.time_s)
+    for p in (16, 1024, 4096):
+        w = reference_roofline.prefill(model, 1, p)
+        b = reference_roofline.physical_bound(w, dev, initial_resident_bytes=0)
+        line = rl.model_prefill_line(cfg, p)
+        assert line["flops"] == w.total_flops
+        assert line["dram_bytes"] == pytest.approx(b.traffic["total"])
+        assert line["time_s"] == pytest.approx(b.time_s)
+
+
+def test_request_line_closed_form(rl):
+    import importlib as _il
+    cfg = _il.import_module("roofline-inference_b200").QWEN3_0_6B
+    r = rl.request_line(cfg, 4096, 128)
+    assert r["ttft_s"] == pytest.approx(rl.model_prefill_line(cfg, 4096)["time_s"])
+    assert r["decode_first_s"] == pytest.approx(rl.model_decode_line(cfg, 4096)["time_s"])
+    assert r["total_s"] == pytest.approx(r["ttft_s"] + r["decode_s"])
+    d = rl.model_decode_line(cfg, 32768)
+    assert d["bottleneck"] == "dram_bandwidth"
+    assert 4.9e9 < d["dram_bytes"] < 5.0e9          # 1.19 GB weights + 3.76 GB K/V
