@@ -115,13 +115,24 @@ int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw,
  *   n      number of valid keys (offset + 1 in Engine.decode, engine.py:149)
  *   out    [nq, 128]             == [1, nq, 1, 128], o_proj input layout
  *   workspace / workspace_bytes  device scratch of at least
- *          rib_decode_workspace_bytes(1, n, nkv) bytes, no initialisation
- *          needed: each call first clears its counters with an enqueued
- *          memset on `stream`.  Calls that share a workspace must not
- *          overlap on the device.
+ *          rib_decode_workspace_bytes(1, n, nkv) bytes.  Its first 16 KiB
+ *          hold split counters that must be zero before the workspace's
+ *          first use (allocate it zero-filled or call
+ *          rib_decode_workspace_init once); every completed call leaves them
+ *          zero again, so calls of any shape can share one workspace and no
+ *          call enqueues a memset (except launches of more than 4095
+ *          sequence x KV-head units, which clear a larger region
+ *          themselves).  After a call whose launch reported RIB_ETIMEOUT
+ *          through rib_take_device_status, initialise it again.  Calls that
+ *          share a workspace must not overlap on the device.
  * Softmax and accumulation in FP32; output rounded to BF16 once.
  * ------------------------------------------------------------------------ */
 size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv);
+
+/* Zeroes the counter region of a decode workspace (an enqueued memset on
+ * `stream`); workspace_bytes >= 16384. */
+int rib_decode_workspace_init(void *workspace, size_t workspace_bytes,
+                              void *stream);
 
 int rib_decode_attention(const void *q, const void *cache, int cap, int n,
                          int nq, int nkv, float scale, void *out,
@@ -136,11 +147,12 @@ int rib_decode_attention(const void *q, const void *cache, int cap, int n,
  * host whose device memory is owned by another allocator or a hard memory
  * budget, a binding with no device allocator of its own).
  *   - Sizes whose scratch (rib_decode_workspace_bytes(1, n, nkv)) exceeds
- *     2 MiB are rejected with RIB_EINVAL (every n <= 911232 fits at 8 KV heads).
+ *     2 MiB are rejected with RIB_EINVAL (every n <= 909312 fits at 8 KV heads).
  *   - The first call on a device looks up the array's device address; make
  *     that first call before any stream capture.
- *   - Every call clears the array's counters on `stream` and then reuses it:
- *     calls that overlap on the GPU (other streams, other threads) race.
+ *   - The array starts zeroed and every call leaves its counters zero, so
+ *     calls need no memset; calls that overlap on the GPU (other streams,
+ *     other threads) race.
  * ------------------------------------------------------------------------ */
 int rib_decode_attention_noalloc(const void *q, const void *cache, int cap,
                                  int n, int nq, int nkv, float scale,

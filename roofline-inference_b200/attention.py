@@ -23,9 +23,10 @@ from ._tensors import HEAD_DIM, require_bf16_cuda, require_same_device, stream_h
 
 # --------------------------------------------------------------- workspace
 # Split-KV decode needs an FP32 scratch of partial results plus per-(sequence,
-# KV head) counters; the library clears the counters on the stream before
-# each launch, so calls of any shape can share one scratch.  One workspace
-# per (device, stream): calls on one stream never overlap.
+# KV head) counters in a fixed region at its start.  The counters must be zero
+# before first use (the scratch is allocated zero-filled) and every call leaves
+# them zero, so calls of any shape can share one scratch without a memset per
+# call.  One workspace per (device, stream): calls on one stream never overlap.
 _ws_lock = threading.Lock()
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
@@ -36,7 +37,7 @@ def decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
-            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
             _workspaces[key] = ws
         return ws
 

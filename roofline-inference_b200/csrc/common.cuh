@@ -45,6 +45,16 @@ __device__ __forceinline__ void record_timeout() {
   atomicExch(&g_device_status, RIB_ETIMEOUT);
 }
 
+// Programmatic dependent launch (kernels launched with the
+// programmatic-stream-serialization attribute): a kernel lets the next one in
+// its stream be scheduled as soon as every CTA has started, and waits for the
+// previous kernel's completion (and memory) before reading its results or
+// writing anything.  Without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

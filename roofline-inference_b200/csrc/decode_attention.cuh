@@ -153,6 +153,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
 
+  pdl_launch_dependents();
+  pdl_wait();
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int n = p.lens ? p.lens[b] : p.n_single;
   if (n < 1 || n > p.cap || n > p.max_n) {  // bad device-side length: record, write nothing

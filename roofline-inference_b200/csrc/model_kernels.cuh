@@ -82,13 +82,36 @@ struct GemvParams {
   int N, K, rows_out, epi, out_f32;
 };
 
-// C = K / 256 chunks of 8 elements per lane (0: runtime count).  R rows per warp.
-template <int R, int C>
+// C = K / 256 chunks of 8 elements per lane (0: runtime count); R output rows
+// per warp; SW: SwiGLU epilogue (each output row reads its gate and up rows).
+// The weight rows do not depend on the previous kernel, so with C known at
+// compile time they are loaded into registers before the dependent-launch
+// wait; x (and the residual) are read after it.
+template <int R, int C, bool SW>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ float xs[];  // [K]
   __shared__ float red[32];
+  pdl_launch_dependents();
+  constexpr int NR = SW ? 2 * R : R;  // weight rows per warp
   const int K = p.K;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row0 = (blockIdx.x * kGemvWarps + warp) * R;
+  const bool active = row0 < p.rows_out;
+  const int F = p.rows_out;  // up rows start at F in the SwiGLU case
+  const uint16_t *wrow[NR];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const int rr = r < R ? min(row0 + r, p.rows_out - 1) : min(row0 + r - R, p.rows_out - 1) + F;
+    wrow[r] = p.W + static_cast<size_t>(active ? rr : 0) * K;
+  }
+  uint4 wreg[NR][C > 0 ? C : 1];
+  if (C > 0 && active) {
+#pragma unroll
+    for (int c = 0; c < (C > 0 ? C : 1); ++c)
+#pragma unroll
+      for (int r = 0; r < NR; ++r) wreg[r][c] = ldg_stream(wrow[r] + (c * 32 + lane) * 8);
+  }
+  pdl_wait();
 
   // ---- x into shared memory (normalised when nw is given)
   float ss = 0.f;
@@ -113,39 +136,34 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     }
   }
   __syncthreads();
+  if (!active) return;
 
-  // ---- rows of this warp
-  const int row0 = (blockIdx.x * kGemvWarps + warp) * R;
-  if (row0 >= p.rows_out) return;
-  const bool swiglu = p.epi == kSwiGLU;
-  const int F = p.rows_out;  // up rows start at F in the SwiGLU case
-  const int nrow = swiglu ? 2 * R : R;
-  float acc[2 * R];
+  float acc[NR];
 #pragma unroll
-  for (int r = 0; r < 2 * R; ++r) acc[r] = 0.f;
-  const uint16_t *wrow[2 * R];
+  for (int r = 0; r < NR; ++r) acc[r] = 0.f;
+  if (C > 0) {
 #pragma unroll
-  for (int r = 0; r < 2 * R; ++r) {
-    const int rr = r < R ? min(row0 + r, p.rows_out - 1) : min(row0 + r - R, p.rows_out - 1) + F;
-    wrow[r] = p.W + static_cast<size_t>(r < nrow ? rr : row0) * K;
-  }
-  const int nchunks = C > 0 ? C : K / 256;
-#pragma unroll(C > 0 ? C : 1)
-  for (int c = 0; c < nchunks; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    const float4 xa = *reinterpret_cast<const float4 *>(xs + col);
-    const float4 xb = *reinterpret_cast<const float4 *>(xs + col + 4);
-    uint4 w[2 * R];
+    for (int c = 0; c < (C > 0 ? C : 1); ++c) {
+      const int col = (c * 32 + lane) * 8;
+      const float4 xa = *reinterpret_cast<const float4 *>(xs + col);
+      const float4 xb = *reinterpret_cast<const float4 *>(xs + col + 4);
 #pragma unroll
-    for (int r = 0; r < 2 * R; ++r)
-      if (r < nrow) w[r] = ldg_stream(wrow[r] + col);
+      for (int r = 0; r < NR; ++r) acc[r] = dot8(wreg[r][c], xa, xb, acc[r]);
+    }
+  } else {
+    for (int c = 0; c < K / 256; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      const float4 xa = *reinterpret_cast<const float4 *>(xs + col);
+      const float4 xb = *reinterpret_cast<const float4 *>(xs + col + 4);
+      uint4 w[NR];
 #pragma unroll
-    for (int r = 0; r < 2 * R; ++r)
-      if (r < nrow) acc[r] = dot8(w[r], xa, xb, acc[r]);
+      for (int r = 0; r < NR; ++r) w[r] = ldg_stream(wrow[r] + col);
+#pragma unroll
+      for (int r = 0; r < NR; ++r) acc[r] = dot8(w[r], xa, xb, acc[r]);
+    }
   }
 #pragma unroll
-  for (int r = 0; r < 2 * R; ++r)
-    if (r < nrow) acc[r] = warp_sum(acc[r]);
+  for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
   if (lane != 0) return;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -156,8 +174,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
       continue;
     }
     float v;
-    if (swiglu) {
-      const float g = round_bf16(acc[r]), u = round_bf16(acc[R + r]);
+    if (SW) {
+      const float g = round_bf16(acc[r]), u = round_bf16(acc[(SW ? R : 0) + r]);
       const float a = round_bf16(g * sigmoid_bf16(g));
       v = a * u;
     } else if (p.epi == kResidual) {
@@ -184,6 +202,8 @@ struct RowParams {
 __global__ void __launch_bounds__(256) add_rms_kernel(const __grid_constant__ RowParams p) {
   extern __shared__ float rs[];  // [W]
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const size_t base = static_cast<size_t>(blockIdx.x) * p.W;
   float ss = 0.f;
   for (int i = threadIdx.x * 8; i < p.W; i += blockDim.x * 8) {
@@ -229,6 +249,8 @@ __global__ void __launch_bounds__(256) add_rms_kernel(const __grid_constant__ Ro
 // ------------------------------------------------------------------ SwiGLU (prefill)
 // gu [rows][2F] (gate columns [0, F), up columns [F, 2F)) -> out [rows][F].
 __global__ void swiglu_kernel(const uint16_t *__restrict__ gu, int rows, int F, uint16_t *__restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const long long total = static_cast<long long>(rows) * (F / 8);
   for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < total;
        v += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -257,6 +279,8 @@ __global__ void swiglu_kernel(const uint16_t *__restrict__ gu, int rows, int F, 
 // records RIB_EINVAL in the device status word.
 __global__ void embed_kernel(const uint16_t *__restrict__ table, int vocab, int hidden,
                              const int32_t *__restrict__ tokens, uint16_t *__restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int i = blockIdx.x;
   const int tok = tokens[i];
   const bool ok = tok >= 0 && tok < vocab;
@@ -288,6 +312,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
                                                       int32_t *__restrict__ out) {
   __shared__ unsigned long long red[32];
   __shared__ bool last;
+  pdl_launch_dependents();
+  pdl_wait();
   unsigned long long best = 0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const unsigned long long k = argmax_key(x[i], i);

@@ -42,6 +42,8 @@ struct Params {
 
 __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constant__ Params p) {
   __shared__ float cos_t[64], sin_t[64];
+  pdl_launch_dependents();
+  pdl_wait();
   const int t = blockIdx.x;
   const int tid = threadIdx.x;
   int offset = p.offset, kv_row0 = p.kv_row0;

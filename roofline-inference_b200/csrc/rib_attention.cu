@@ -18,6 +18,10 @@
 #ifndef RIB_DECODE_MAX_CHUNK
 #define RIB_DECODE_MAX_CHUNK 4096
 #endif
+// Decode CTAs per SM that one wave of splits aims to fill (a build-time tuning constant).
+#ifndef RIB_DECODE_SLOTS_PER_SM
+#define RIB_DECODE_SLOTS_PER_SM 2
+#endif
 
 namespace {
 
@@ -66,8 +70,24 @@ bool set_smem_once(Kernel kernel, int bytes, bool *done_table) {
   return true;
 }
 
-int launch_status(const char *what) {
-  const cudaError_t e = cudaGetLastError();
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while the previous kernel in the stream is still running (it calls
+// pdl_wait() before touching that kernel's results, common.cuh).  Inside a
+// captured CUDA graph the same edge becomes a programmatic dependency.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char *what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
   return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda(what, e);
 }
 
@@ -124,8 +144,8 @@ int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offs
   for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
   const int items = nq + 2 * nkv;
   const int threads = ((items + 1) / 2) * 32;
-  rib::rope::qk_norm_rope_kernel<<<Lp, threads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status("qk_norm_rope_kernel launch");
+  return launch_pdl("qk_norm_rope_kernel launch", rib::rope::qk_norm_rope_kernel, dim3(Lp), dim3(threads), 0,
+                    static_cast<cudaStream_t>(stream), p);
 }
 
 // ------------------------------------------------------------------ decode
@@ -133,7 +153,16 @@ struct DecodeGeometry {
   int chunk;
   int max_splits;
   size_t counters_bytes, ml_bytes, o_bytes, total;
+  bool clear_counters;  // counters outside the fixed region: cleared before the launch
 };
+
+// Split counters live in a fixed region at the start of every workspace, so a
+// workspace shared by calls of different shapes never holds one call's
+// partials where another keeps counters.  The kernel leaves every counter it
+// used at zero, so once the region is zero (a zero-filled allocation, or
+// rib_decode_workspace_init) no call needs a memset before its launch.
+constexpr size_t kCounterRegionBytes = 16384;
+constexpr size_t kCounterRegionUnits = kCounterRegionBytes / sizeof(int) - 1;
 
 DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
   using namespace rib::decode;
@@ -144,7 +173,7 @@ DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
   // up to twice that whose CTA total fills whole waves (>= 97% of the last
   // wave's slots), so no nearly empty wave trails the launch; otherwise the
   // best wave fill in that range.
-  const long long slots = 2LL * sm_count();
+  const long long slots = static_cast<long long>(RIB_DECODE_SLOTS_PER_SM) * sm_count();
   const long long n_units = static_cast<long long>(batch) * nkv;
   const int lo = std::max(ceil_div(max_n, RIB_DECODE_MAX_CHUNK),
                           std::min(ceil_div(slots, n_units), ceil_div(max_n, TK)));
@@ -166,7 +195,8 @@ DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
   g.max_splits = ceil_div(max_n, best_chunk);
   const size_t units = static_cast<size_t>(batch) * nkv;
   // per-unit split counters, then one counter of units finalised (all-gather)
-  g.counters_bytes = (((units + 1) * sizeof(int) + 255) / 256) * 256;
+  g.clear_counters = units > kCounterRegionUnits;
+  g.counters_bytes = g.clear_counters ? (((units + 1) * sizeof(int) + 255) / 256) * 256 : kCounterRegionBytes;
   g.ml_bytes = ((units * g.max_splits * 2 * 2 * sizeof(float) + 255) / 256) * 256;
   g.o_bytes = units * g.max_splits * 2 * D * sizeof(float);
   g.total = g.counters_bytes + g.ml_bytes + g.o_bytes;
@@ -183,11 +213,13 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   if (!workspace || workspace_bytes < g.total) return RIB_EINVAL;
   if (!aligned16(workspace)) return RIB_EALIGN;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  // The split counters must start at zero.  A workspace shared with a call
-  // of another shape holds that call's FP32 partials where this call keeps
-  // counters, so they are cleared on the stream before every launch.
-  const cudaError_t ze = cudaMemsetAsync(ws, 0, g.counters_bytes, static_cast<cudaStream_t>(stream));
-  if (ze != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(decode counters)", ze);
+  // The split counters must start at zero.  In the fixed region they do (the
+  // workspace contract; the kernel resets what it uses); a launch with more
+  // units than the region holds clears its own, larger region first.
+  if (g.clear_counters) {
+    const cudaError_t ze = cudaMemsetAsync(ws, 0, g.counters_bytes, static_cast<cudaStream_t>(stream));
+    if (ze != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(decode counters)", ze);
+  }
   p.counters = reinterpret_cast<int *>(ws);
   p.done = p.counters + static_cast<size_t>(batch) * p.nkv;
   p.part_ml = reinterpret_cast<float *>(ws + g.counters_bytes);
@@ -199,8 +231,8 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   if (!set_smem_once(decode_kernel, smem, g_decode_smem_done))
     return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(decode smem)", 0);
   dim3 grid(g.max_splits, p.nkv, batch);
-  decode_kernel<<<grid, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status("decode_kernel launch");
+  return launch_pdl("decode_kernel launch", decode_kernel, grid, dim3(NTHREADS), smem,
+                    static_cast<cudaStream_t>(stream), p);
 }
 
 // ------------------------------------------------------------------ decode, no allocation
@@ -231,22 +263,27 @@ void *noalloc_scratch(int dev) {
 }
 
 // ------------------------------------------------------------------ model kernels
-template <int R, int C>
+template <int R, int C, bool SW>
 int gemv_launch_rc(const rib::model::GemvParams &p, cudaStream_t st) {
   const int rows_per_cta = rib::model::kGemvWarps * R;
   const int grid = ceil_div(p.rows_out, rows_per_cta);
-  rib::model::gemv_kernel<R, C><<<grid, rib::model::kGemvWarps * 32, p.K * sizeof(float), st>>>(p);
-  return launch_status("gemv_kernel launch");
+  return launch_pdl("gemv_kernel launch", rib::model::gemv_kernel<R, C, SW>, dim3(grid),
+                    dim3(rib::model::kGemvWarps * 32), p.K * sizeof(float), st, p);
+}
+
+template <int R, bool SW>
+int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
+  switch (p.K) {
+    case 1024: return gemv_launch_rc<R, 4, SW>(p, st);
+    case 2048: return gemv_launch_rc<R, 8, SW>(p, st);
+    case 3072: return gemv_launch_rc<R, 12, SW>(p, st);
+    default: return gemv_launch_rc<R, 0, SW>(p, st);
+  }
 }
 
 template <int R>
 int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
-  switch (p.K) {
-    case 1024: return gemv_launch_rc<R, 4>(p, st);
-    case 2048: return gemv_launch_rc<R, 8>(p, st);
-    case 3072: return gemv_launch_rc<R, 12>(p, st);
-    default: return gemv_launch_rc<R, 0>(p, st);
-  }
+  return p.epi == rib::model::kSwiGLU ? gemv_launch_r<R, true>(p, st) : gemv_launch_r<R, false>(p, st);
 }
 
 }  // namespace
@@ -302,6 +339,14 @@ int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw, const void *
 size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv) {
   if (batch < 1 || max_n < 1 || nkv < 1) return 0;
   return decode_geometry(batch, max_n, nkv).total;
+}
+
+int rib_decode_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
+  if (!workspace || workspace_bytes < kCounterRegionBytes) return RIB_EINVAL;
+  if (!aligned16(workspace)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const cudaError_t e = cudaMemsetAsync(workspace, 0, kCounterRegionBytes, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda("cudaMemsetAsync(decode workspace init)", e);
 }
 
 int rib_decode_attention(const void *q, const void *cache, int cap, int n, int nq, int nkv,
@@ -525,8 +570,8 @@ int rib_add_rms(const void *a, const void *b, const void *w, int rows, int W, vo
   rib::model::RowParams p = {static_cast<const uint16_t *>(a), static_cast<const uint16_t *>(b),
                              static_cast<const uint16_t *>(w), static_cast<uint16_t *>(residual),
                              static_cast<uint16_t *>(normalized), rows, W};
-  rib::model::add_rms_kernel<<<rows, 128, W * sizeof(float), static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status("add_rms_kernel launch");
+  return launch_pdl("add_rms_kernel launch", rib::model::add_rms_kernel, dim3(rows), dim3(128),
+                    W * sizeof(float), static_cast<cudaStream_t>(stream), p);
 }
 
 int rib_rms_norm(const void *x, const void *w, int rows, int W, void *out, void *stream) {
@@ -535,8 +580,8 @@ int rib_rms_norm(const void *x, const void *w, int rows, int W, void *out, void 
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
   rib::model::RowParams p = {static_cast<const uint16_t *>(x), nullptr, static_cast<const uint16_t *>(w),
                              nullptr, static_cast<uint16_t *>(out), rows, W};
-  rib::model::add_rms_kernel<<<rows, 128, W * sizeof(float), static_cast<cudaStream_t>(stream)>>>(p);
-  return launch_status("rms_norm launch");
+  return launch_pdl("rms_norm launch", rib::model::add_rms_kernel, dim3(rows), dim3(128),
+                    W * sizeof(float), static_cast<cudaStream_t>(stream), p);
 }
 
 int rib_swiglu(const void *gu, int rows, int F, void *out, void *stream) {
@@ -545,9 +590,9 @@ int rib_swiglu(const void *gu, int rows, int F, void *out, void *stream) {
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
   const long long vec = static_cast<long long>(rows) * (F / 8);
   const int grid = static_cast<int>(std::min<long long>(ceil_div(vec, 256), 16LL * sm_count()));
-  rib::model::swiglu_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t *>(gu), rows, F, static_cast<uint16_t *>(out));
-  return launch_status("swiglu_kernel launch");
+  return launch_pdl("swiglu_kernel launch", rib::model::swiglu_kernel, dim3(grid), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const uint16_t *>(gu), rows, F,
+                    static_cast<uint16_t *>(out));
 }
 
 int rib_embed(const void *table, int vocab, int hidden, const int32_t *tokens, int n, void *out,
@@ -555,9 +600,9 @@ int rib_embed(const void *table, int vocab, int hidden, const int32_t *tokens, i
   if (!table || !tokens || !out || vocab < 1 || hidden < 8 || hidden % 8 || n < 1) return RIB_EINVAL;
   if (!aligned16(table) || !aligned16(out) || (reinterpret_cast<uintptr_t>(tokens) & 3u)) return RIB_EALIGN;
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
-  rib::model::embed_kernel<<<n, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t *>(table), vocab, hidden, tokens, static_cast<uint16_t *>(out));
-  return launch_status("embed_kernel launch");
+  return launch_pdl("embed_kernel launch", rib::model::embed_kernel, dim3(n), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), static_cast<const uint16_t *>(table), vocab, hidden,
+                    tokens, static_cast<uint16_t *>(out));
 }
 
 size_t rib_argmax_workspace_bytes(void) { return 256; }
@@ -572,8 +617,8 @@ int rib_argmax_f32(const float *x, int n, int32_t *out, void *workspace, void *s
   cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(rib::model::ArgmaxWs), st);
   if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(argmax workspace)", e);
   const int grid = std::max(1, std::min(ceil_div(n, 1024 * 4), sm_count()));
-  rib::model::argmax_kernel<<<grid, 1024, 0, st>>>(x, n, static_cast<rib::model::ArgmaxWs *>(workspace), out);
-  return launch_status("argmax_kernel launch");
+  return launch_pdl("argmax_kernel launch", rib::model::argmax_kernel, dim3(grid), dim3(1024), 0, st, x, n,
+                    static_cast<rib::model::ArgmaxWs *>(workspace), out);
 }
 
 }  // extern "C"

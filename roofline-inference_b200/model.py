@@ -300,7 +300,7 @@ class DecodeGraph:
         L = _lib.load()
         self.max_n = cache.capacity
         ws_bytes = int(L.rib_decode_workspace_bytes(1, self.max_n, cfg.num_kv_heads))
-        self.ws = torch.empty(max(ws_bytes, 1 << 20), dtype=torch.uint8, device=dev)
+        self.ws = torch.zeros(max(ws_bytes, 1 << 20), dtype=torch.uint8, device=dev)  # counters zero
         self.argmax_ws = torch.empty(int(L.rib_argmax_workspace_bytes()), dtype=torch.uint8, device=dev)
         self.launches_per_step = 0
         self.stream = torch.cuda.current_stream(dev)

@@ -52,6 +52,13 @@ def test_workspace_bytes(rib):
     assert L.rib_decode_workspace_bytes(0, 10, 8) == 0
 
 
+def test_workspace_init_rejects_bad_arguments(rib):
+    L = rib.load_library()
+    assert L.rib_decode_workspace_init(None, 1 << 20, None) == 1
+    assert L.rib_decode_workspace_init(FAKE, 4096, None) == 1
+    assert L.rib_decode_workspace_init(MISALIGNED, 1 << 20, None) == 3
+
+
 def test_decode_rejects_bad_arguments(rib):
     L = rib.load_library()
     ws = L.rib_decode_workspace_bytes(1, 100, 8)

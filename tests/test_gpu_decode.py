@@ -107,9 +107,10 @@ def test_decode_ragged_batch(rib, wl, oracle, batch, lo, hi):
 
 
 def test_decode_workspace_shared_across_shapes(rib, wl, oracle):
-    """Calls of different shapes share one cached workspace; the partials of a
-    small call sit where a larger call keeps split counters, which the library
-    clears before every launch (a stale counter makes a unit merge early)."""
+    """Calls of different shapes share one cached workspace: the split
+    counters sit in a fixed region at its start, apart from every call's
+    partials, and each call leaves them zero (a stale counter makes a unit
+    merge early)."""
     for B, n in [(2, 4097), (28, 4160), (2, 4097), (28, 4097)]:
         cap = wl.round_cap(n)
         caches = wl.randn_bf16((B, 2, 8, cap, 128), seed=B + n, device="cuda")
@@ -125,3 +126,36 @@ def test_decode_device_status_clean(rib):
     from importlib import import_module
     lib = import_module("roofline-inference_b200._lib")
     assert lib.take_device_status() == 0
+
+
+def test_decode_leaves_counters_zero(rib, wl):
+    """After calls of several shapes the workspace's counter region is zero
+    again, so the next call needs no memset."""
+    att = __import__("importlib").import_module("roofline-inference_b200.attention")
+    for B, n in [(1, 513), (3, 40000), (28, 4097)]:
+        cap = wl.round_cap(n)
+        caches = wl.randn_bf16((B, 2, 8, cap, 128), seed=B + n, device="cuda")
+        q = wl.randn_bf16((B, 16, 128), seed=B * n, device="cuda")
+        rib.decode_attention_batched(q, caches, [n] * B, wl.SCALE)
+    torch.cuda.synchronize()
+    ws = att.decode_workspace(torch.device("cuda", torch.cuda.current_device()), 1)
+    assert not ws[:16384].any()
+
+
+def test_decode_workspace_init_repairs_garbage(rib, wl, oracle):
+    """A workspace full of garbage works after rib_decode_workspace_init."""
+    L = rib.load_library()
+    n, cap = 5000, wl.round_cap(5000)
+    cache = wl.randn_bf16((2, 8, cap, 128), seed=41, device="cuda")
+    q = wl.randn_bf16((16, 128), seed=42, device="cuda")
+    nbytes = L.rib_decode_workspace_bytes(1, n, 8)
+    ws = torch.full((nbytes,), 0x5A, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.rib_decode_workspace_init(ws.data_ptr(), nbytes, st) == 0
+    out = torch.empty((16, 128), dtype=torch.bfloat16, device="cuda")
+    assert L.rib_decode_attention(q.data_ptr(), cache.data_ptr(), cap, n, 16, 8, wl.SCALE, out.data_ptr(),
+                                  ws.data_ptr(), nbytes, st) == 0
+    torch.cuda.synchronize()
+    of, _ = oracle.decode_attention(u16(q), u16(cache), n, wl.SCALE)
+    _assert_parity(out, of)
+    assert not ws[:16384].any()
