@@ -405,6 +405,10 @@ def run_ours(args):
     # ---- end to end through the public API with host buffers
     e2e = run_e2e(rib, w, rank, world, device, args, gather, plan)
 
+    # ---- the sweep's other contexts (4096, 8192) and the ctx-512 layer latency
+    sweep = run_sweep_contexts(rib, rank, world, device, args, pk)
+    ctx512 = run_ctx512_latency(rib, device, args)
+
     # ---- batched ragged decode (64 sequences), sequence-sharded
     ragged = run_ragged(rib, rank, world, device, args, pk)
 
@@ -447,6 +451,8 @@ def run_ours(args):
         "nccl_allgather_baseline": nccl,
         "per_layer_launches": {"value": per_layer_gbs, "unit": "GB/s", "ms_per_step": per_layer_ms,
                                "frac": per_layer_gbs / pk["hbm_gbs"]},
+        "sweep_contexts": sweep,
+        "decode_ctx512": ctx512,
         "prefill": prefill,
         "full_model": full_model,
         "ragged_batch": ragged,
@@ -654,6 +660,102 @@ def sm_clock_mhz(device):
         return None
 
 
+def run_sweep_contexts(rib, rank, world, device, args, pk):
+    """The decode sweep at contexts 4096 and 8192 (28 layers, one layer-batched
+    launch per step, this rank's KV heads; no cross-GPU exchange): whole-job
+    GB/s = all ranks' K/V bytes / the max over ranks of the step time."""
+    out = {}
+    for ctx in (4096, 8192):
+        w = make_decode_workload(rank, world, device, ctx=ctx)
+        plan = DecodePlan(rib, w, device)
+        for _ in range(max(3, args.warmup)):
+            plan.launch()
+        stream = torch.cuda.current_stream(device)
+        barrier(world)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            plan.launch()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(a.elapsed_time(b) / args.steps, world, device)
+        gbs = N_LAYERS * 4096 * w["n"] / (ms * 1e-3) / 1e9
+        out[str(ctx)] = {"value": gbs, "unit": "GB/s", "ms_per_step": ms,
+                         "frac_of_hbm_peak_x_gpus": gbs / (pk["hbm_gbs"] * world),
+                         "kv_bytes_per_step": N_LAYERS * 4096 * w["n"]}
+        del plan, w
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_ctx512_latency(rib, device, args):
+    """Single-layer decode at context 512 (the reference's CPU-runnable
+    configuration): the fused norm + RoPE + append of the new token at
+    position 512, then attention over 513 keys.  Device time per layer from a
+    CUDA graph of 28 such layers (distinct caches), and host-to-host time of
+    one eager layer through the public API (with a synchronise)."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    L = rib.load_library()
+    layers, pos = N_LAYERS, 512
+    cache = rib.Cache(layers, 8, 128, pos + 1, device=device)
+    cache.storage[:, :, :, :pos].copy_(wl.randn_bf16(tuple(cache.storage[:, :, :, :pos].shape), seed=5,
+                                                     device=device))
+    st = wl.decode_step(pos, seed=1, device=device)
+    posd = torch.tensor([pos], dtype=torch.int32, device=device)
+    nk = torch.tensor([pos + 1], dtype=torch.int32, device=device)
+    ptrs = torch.tensor([cache.kv[i].data_ptr() for i in range(layers)], dtype=torch.int64, device=device)
+    q = torch.empty((16, 1, 128), dtype=torch.bfloat16, device=device)
+    out = torch.empty((1, 16, 128), dtype=torch.bfloat16, device=device)
+    ws = torch.zeros(int(L.rib_decode_workspace_bytes(1, cache.capacity, 8)), dtype=torch.uint8,
+                     device=device)
+
+    def layer(i):
+        rib.qk_norm_rope_append_at(st.qkv, st.qw, st.kw, posd, 16, 8, 1e6, cache.kv[i], out=q)
+        rc = L.rib_decode_attention_batched(q.data_ptr(), ptrs.data_ptr() + 8 * i, nk.data_ptr(), 1,
+                                            cache.capacity, cache.capacity, 16, 8, wl.SCALE,
+                                            out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                            torch.cuda.current_stream(device).cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"decode launch failed: status {rc}")
+
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        layer(0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        for i in range(layers):
+            layer(i)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 50))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    b.synchronize()
+    dev_us = a.elapsed_time(b) * 1000 / (reps * layers)
+    # eager, host to host: one layer through the public API per call
+    for _ in range(3):
+        layer(0)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        layer(0)
+        torch.cuda.synchronize()
+    host_us = (time.perf_counter() - t0) * 1e6 / reps
+    del g
+    bytes_layer = 4096 * 512 + 3 * 4096 + 16384
+    return {"us_per_layer_device": dev_us, "us_per_layer_host_sync": host_us, "layers": layers,
+            "bytes_per_layer": bytes_layer,
+            "path": "qk_norm_rope_append_at + decode_attention_batched (batch 1) per layer; device time "
+                    "from a CUDA graph of 28 layers, host time from eager calls with a synchronise"}
+
+
 def run_full_model(rib, rank, world, device, args):
     """Qwen3-0.6B forward with random N(0, 0.02) weights (28 layers, hidden
     1024, 16/8 heads, FFN 3072, vocab 151936, tied embeddings, BF16): the
@@ -737,7 +839,9 @@ def run_case(case: str):
     """Bounded workloads for ncu captures: decode-small is the layer-batched
     decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
     prefill-small is causal prefill at L = 16384 (128 MB of Q/K/V, above L2;
-    3 launches)."""
+    3 launches); model-decode is the Qwen3-0.6B decode step at context 4096
+    (1.19 GB of weights and 0.47 GB of K/V, above L2): the graph's eager
+    warm-up step and 3 replays of 143 launches each."""
     rib = load_rib()
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
@@ -747,6 +851,19 @@ def run_case(case: str):
         plan = DecodePlan(rib, w, device)
         for _ in range(3):
             plan.launch()
+    elif case == "model-decode":
+        eng = rib.Engine(rib.random_weights(rib.QWEN3_0_6B, seed=11, device=device))
+        ctx = 4096
+        cache = eng.new_cache(ctx + 64)
+        g = torch.Generator(device=device)
+        g.manual_seed(12)
+        for i in range(rib.QWEN3_0_6B.num_layers):
+            cache.storage[i, :, :, :ctx].normal_(generator=g)
+        cache.offset = ctx
+        dg = eng.decode_graph(cache)
+        dg.set_state(1, ctx)
+        for _ in range(3):
+            dg.replay()
     else:
         L = 16384
         Q = wl.randn_bf16((16, L, 128), seed=71, device=device)
@@ -767,7 +884,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "prefill-small"], default=None,
+    ap.add_argument("--case", choices=["decode-small", "prefill-small", "model-decode"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()
     if args.case:
