@@ -771,7 +771,7 @@ def run_full_model(rib, rank, world, device, args):
 
     # decode step at context 32768
     ctx, steps, warm = 32768, max(1, min(args.steps, 200)), max(3, min(args.warmup, 20))
-    cache = eng.new_cache(ctx + steps + warm + 8)
+    cache = eng.new_cache(ctx + 2 * (steps + warm) + 8)
     g = torch.Generator(device=device)
     g.manual_seed(12 + rank)
     for i in range(cfg.num_layers):
@@ -792,7 +792,27 @@ def run_full_model(rib, rank, world, device, args):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(a.elapsed_time(b) / steps, world, device)
+    # the same step as one persistent cooperative launch per token
+    cache.offset = ctx + warm + steps
+    pers = eng.persistent_decode(cache)
+    pers.set_state(1, cache.offset)
+    for _ in range(warm):
+        pers.replay()
+    barrier(world)
+    torch.cuda.synchronize()
+    a.record(stream)
+    for _ in range(steps):
+        pers.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    pms = max_over_ranks(a.elapsed_time(b) / steps, world, device)
     line = rl.model_decode_line(cfg, ctx + warm)
+    out["decode_step_persistent"] = {
+        "ms_per_token": pms, "tokens_per_s": world * 1000.0 / pms, "launches_per_step": 1,
+        "path": "rib_qwen3_decode_step: one cooperative launch per token, 169 grid barriers",
+        "fraction_of_line": line["time_s"] * 1e3 / pms}
+    del pers
     out["decode_step"] = {
         "context": f"{ctx + warm}..{ctx + warm + steps}", "steps": steps, "ms_per_token": ms,
         "tokens_per_s": world * 1000.0 / ms, "launches_per_step": dg.launches_per_step,

@@ -307,6 +307,58 @@ size_t rib_argmax_workspace_bytes(void);
 int rib_argmax_f32(const float *x, int n, int32_t *out, void *workspace,
                    void *stream);
 
+/* ------------------------------------------------------------------------ *
+ * Whole decode step of a dense Qwen3 model in one cooperative launch: the
+ * per-token loop of Engine.decode (agent-test/v2/engine.py:145-163) with the
+ * same kernels' arithmetic, but one persistent kernel instead of one launch
+ * per operation (no counterpart in the reference, which launches 7 kernels
+ * per layer).
+ *   model      weights in the engine layout (engine.py:80-88); every
+ *              pointer 16-byte aligned.  head_dim 128, num_heads ==
+ *              2 * num_kv_heads, hidden / intermediate / num_heads*128
+ *              multiples of 256, num_heads + 2*num_kv_heads <= 64,
+ *              num_layers <= 64.
+ *   cache_ptrs device array [num_layers] of layer caches [2, nkv, cap, 128]
+ *   token, pos, nkeys   device int32 scalars: the token to decode, its
+ *              position (the cache offset) and pos + 1.  The step writes the
+ *              next greedy token into *token and advances *pos and *nkeys, so
+ *              calling it again decodes the following token.
+ *   logits     [vocab] FP32 logits of the step, or NULL
+ *   workspace  rib_qwen3_step_workspace_bytes(model, cap) bytes, 256-byte
+ *              aligned, zero-filled before first use (or
+ *              rib_qwen3_step_workspace_init); steps leave it ready for the
+ *              next one.  After a failed step (rib_take_device_status != 0)
+ *              initialise it again.
+ * ------------------------------------------------------------------------ */
+#define RIB_QWEN3_MAX_LAYERS 64
+typedef struct rib_qwen3_layer {
+  const void *qkv;        /* [(nq + 2 nkv) * 128, hidden]  q_proj; k_proj; v_proj */
+  const void *o;          /* [hidden, nq * 128] */
+  const void *gu;         /* [2 * intermediate, hidden]     gate_proj; up_proj */
+  const void *down;       /* [hidden, intermediate] */
+  const void *in_norm;    /* [hidden] */
+  const void *post_norm;  /* [hidden] */
+  const void *q_norm;     /* [128] */
+  const void *k_norm;     /* [128] */
+} rib_qwen3_layer;
+
+typedef struct rib_qwen3_model {
+  int num_layers, hidden, num_heads, num_kv_heads, intermediate, vocab;
+  double rope_theta;
+  const void *embed;      /* [vocab, hidden], also the LM head (tied) */
+  const void *final_norm; /* [hidden] */
+  rib_qwen3_layer layers[RIB_QWEN3_MAX_LAYERS];
+} rib_qwen3_model;
+
+size_t rib_qwen3_step_workspace_bytes(const rib_qwen3_model *model, int cap);
+int rib_qwen3_step_workspace_init(void *workspace, size_t workspace_bytes,
+                                  void *stream);
+int rib_qwen3_decode_step(const rib_qwen3_model *model,
+                          const uint64_t *cache_ptrs, int cap, int32_t *token,
+                          int32_t *pos, int32_t *nkeys, float *logits,
+                          void *workspace, size_t workspace_bytes,
+                          void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -115,6 +115,9 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_embed": ([vp, i, i, vp, i, vp, vp], i),
         "rib_argmax_workspace_bytes": ([], sz),
         "rib_argmax_f32": ([vp, i, vp, vp, vp], i),
+        "rib_qwen3_step_workspace_bytes": ([vp, i], sz),
+        "rib_qwen3_step_workspace_init": ([vp, sz, vp], i),
+        "rib_qwen3_decode_step": ([vp, vp, i, vp, vp, vp, vp, vp, sz, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -149,13 +149,11 @@ __device__ __forceinline__ void unpack8(const uint4 &r, float *f) {
   f[6] = bf16lo(r.w); f[7] = bf16hi(r.w);
 }
 
-__global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_constant__ Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
-
-  pdl_launch_dependents();
-  pdl_wait();
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+// One CTA's work unit: split `split` of KV head h of sequence b.  Used by
+// decode_kernel (one unit per CTA) and by the persistent decode-step kernel
+// (decode_step.cuh), which calls it with the unit it owns in that phase.
+// All NTHREADS threads enter; returns are CTA-uniform.
+__device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, int h, int b) {
   const int n = p.lens ? p.lens[b] : p.n_single;
   if (n < 1 || n > p.cap || n > p.max_n) {  // bad device-side length: record, write nothing
     if (threadIdx.x == 0 && split == 0) atomicExch(&g_device_status, RIB_EINVAL);
@@ -215,8 +213,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
       const uint16_t *qb = p.q + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const uint4 r0 = *reinterpret_cast<const uint4 *>(qb + hh * D + 8 * j);
-        const uint4 r1 = *reinterpret_cast<const uint4 *>(qb + hh * D + 64 + 8 * j);
+        // L2-coherent loads: in the persistent decode step another CTA wrote q
+        // earlier in the same kernel (a line left in this SM's L1 could be stale).
+        const uint4 r0 = __ldcg(reinterpret_cast<const uint4 *>(qb + hh * D + 8 * j));
+        const uint4 r1 = __ldcg(reinterpret_cast<const uint4 *>(qb + hh * D + 64 + 8 * j));
         unpack8(r0, &qa[hh][0]);
         unpack8(r1, &qa[hh][8]);
 #pragma unroll
@@ -447,6 +447,14 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
   if (tid == 0) p.counters[unit] = 0;  // leave the workspace ready for the next call
   __syncthreads();
   finalize_unit(p, b, h, tid, res, s.is_last);
+}
+
+__global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  pdl_launch_dependents();
+  pdl_wait();
+  decode_cta(p, s, blockIdx.x, blockIdx.y, blockIdx.z);
 }
 
 }  // namespace decode

@@ -40,6 +40,68 @@ struct Params {
   double inv_freq[64];  // base^(-d/64), FP64
 };
 
+// cos/sin of the 64 RoPE angles at position `pos`: theta_d = pos * inv_freq[d],
+// reduced to [-pi, pi] in FP64, then full-range sincosf.  Threads 0..63 write.
+__device__ __forceinline__ void rope_angles(int pos, const double *inv_freq, float *cos_t, float *sin_t,
+                                            int tid) {
+  if (tid < 64) {
+    const double two_pi = 6.283185307179586476925286766559;
+    const double th = static_cast<double>(pos) * inv_freq[tid];
+    const double r = th - rint(th * (1.0 / two_pi)) * two_pi;
+    float s, c;
+    sincosf(static_cast<float>(r), &s, &c);
+    cos_t[tid] = c;
+    sin_t[tid] = s;
+  }
+}
+
+// Per-head RMSNorm + RoPE of one head of 128 dims held by a half-warp: lane j
+// (j = lane & 15) passes dims [8j, 8j+8) as `raw` and gets them back normed
+// and rotated.  `w` is the head's norm weight (qw or kw).
+__device__ __forceinline__ uint4 norm_rope8(const uint4 raw, const uint16_t *w, int j, unsigned half_mask,
+                                            const float *cos_t, const float *sin_t) {
+  float x[8];
+  x[0] = bf16lo(raw.x); x[1] = bf16hi(raw.x);
+  x[2] = bf16lo(raw.y); x[3] = bf16hi(raw.y);
+  x[4] = bf16lo(raw.z); x[5] = bf16hi(raw.z);
+  x[6] = bf16lo(raw.w); x[7] = bf16hi(raw.w);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o, 16);
+  const float inv = 1.0f / sqrtf(ss / 128.0f + 1e-6f);
+
+  const uint4 wraw = *reinterpret_cast<const uint4 *>(w + 8 * j);
+  float wf[8];
+  wf[0] = bf16lo(wraw.x); wf[1] = bf16hi(wraw.x);
+  wf[2] = bf16lo(wraw.y); wf[3] = bf16hi(wraw.y);
+  wf[4] = bf16lo(wraw.z); wf[5] = bf16hi(wraw.z);
+  wf[6] = bf16lo(wraw.w); wf[7] = bf16hi(wraw.w);
+
+  float nv[8], pv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) nv[i] = round_bf16(wf[i] * round_bf16(x[i] * inv));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(half_mask, nv[i], 8, 16);
+
+  const bool first_half = j < 8;
+  const int a0 = 8 * (j & 7);
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float c = cos_t[a0 + i], s = sin_t[a0 + i];
+    // first half: x1 = nv, x2 = pv ; second half: x1 = pv, x2 = nv
+    o[i] = first_half ? fmaf(nv[i], c, -pv[i] * s) : fmaf(pv[i], s, nv[i] * c);
+  }
+  uint4 out;
+  out.x = pack_bf16x2(o[0], o[1]);
+  out.y = pack_bf16x2(o[2], o[3]);
+  out.z = pack_bf16x2(o[4], o[5]);
+  out.w = pack_bf16x2(o[6], o[7]);
+  return out;
+}
+
 __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constant__ Params p) {
   __shared__ float cos_t[64], sin_t[64];
   pdl_launch_dependents();
@@ -55,15 +117,7 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
       return;
     }
   }
-  if (tid < 64) {
-    const double two_pi = 6.283185307179586476925286766559;
-    const double th = static_cast<double>(offset + t) * p.inv_freq[tid];
-    const double r = th - rint(th * (1.0 / two_pi)) * two_pi;
-    float s, c;
-    sincosf(static_cast<float>(r), &s, &c);
-    cos_t[tid] = c;
-    sin_t[tid] = s;
-  }
+  rope_angles(offset + t, p.inv_freq, cos_t, sin_t, tid);
   __syncthreads();
 
   const int items = p.nq + 2 * p.nkv;
@@ -91,45 +145,7 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
     return;
   }
 
-  float x[8];
-  x[0] = bf16lo(raw.x); x[1] = bf16hi(raw.x);
-  x[2] = bf16lo(raw.y); x[3] = bf16hi(raw.y);
-  x[4] = bf16lo(raw.z); x[5] = bf16hi(raw.z);
-  x[6] = bf16lo(raw.w); x[7] = bf16hi(raw.w);
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
-#pragma unroll
-  for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o, 16);
-  const float inv = 1.0f / sqrtf(ss / 128.0f + 1e-6f);
-
-  const uint4 wraw = *reinterpret_cast<const uint4 *>((item < p.nq ? p.qw : p.kw) + 8 * j);
-  float w[8];
-  w[0] = bf16lo(wraw.x); w[1] = bf16hi(wraw.x);
-  w[2] = bf16lo(wraw.y); w[3] = bf16hi(wraw.y);
-  w[4] = bf16lo(wraw.z); w[5] = bf16hi(wraw.z);
-  w[6] = bf16lo(wraw.w); w[7] = bf16hi(wraw.w);
-
-  float nv[8], pv[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) nv[i] = round_bf16(w[i] * round_bf16(x[i] * inv));
-#pragma unroll
-  for (int i = 0; i < 8; ++i) pv[i] = __shfl_xor_sync(half_mask, nv[i], 8, 16);
-
-  const bool first_half = j < 8;
-  const int a0 = 8 * (j & 7);
-  float o[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float c = cos_t[a0 + i], s = sin_t[a0 + i];
-    // first half: x1 = nv, x2 = pv ; second half: x1 = pv, x2 = nv
-    o[i] = first_half ? fmaf(nv[i], c, -pv[i] * s) : fmaf(pv[i], s, nv[i] * c);
-  }
-  uint4 out;
-  out.x = pack_bf16x2(o[0], o[1]);
-  out.y = pack_bf16x2(o[2], o[3]);
-  out.z = pack_bf16x2(o[4], o[5]);
-  out.w = pack_bf16x2(o[6], o[7]);
+  const uint4 out = norm_rope8(raw, item < p.nq ? p.qw : p.kw, j, half_mask, cos_t, sin_t);
   uint16_t *dst;
   if (item < p.nq) {
     dst = p.q_out + (static_cast<size_t>(item) * p.Lp + t) * D + 8 * j;

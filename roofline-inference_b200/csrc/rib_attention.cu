@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "decode_attention.cuh"
+#include "decode_step.cuh"
 #include "prefill_attention.cuh"
 #include "model_kernels.cuh"
 #include "qk_norm_rope.cuh"
@@ -284,6 +285,79 @@ int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
 template <int R>
 int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
   return p.epi == rib::model::kSwiGLU ? gemv_launch_r<R, true>(p, st) : gemv_launch_r<R, false>(p, st);
+}
+
+// ------------------------------------------------------------------ persistent decode step
+inline size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+
+struct StepLayout {
+  DecodeGeometry g;
+  size_t sync_off, ml_off, po_off, h_off[3], qkv_off, q_off, ao_off, a_off, total;
+};
+
+StepLayout step_layout(const rib_qwen3_model *m, int cap) {
+  StepLayout l;
+  l.g = decode_geometry(1, cap, m->num_kv_heads);
+  size_t off = kCounterRegionBytes;  // decode split counters (fixed region)
+  l.sync_off = off;
+  off += round256(sizeof(rib::step::Sync));
+  l.ml_off = off;
+  off += round256(l.g.ml_bytes);
+  l.po_off = off;
+  off += round256(l.g.o_bytes);
+  for (int i = 0; i < 3; ++i) {
+    l.h_off[i] = off;
+    off += round256(static_cast<size_t>(m->hidden) * 2);
+  }
+  l.qkv_off = off;
+  off += round256(static_cast<size_t>(m->num_heads + 2 * m->num_kv_heads) * 128 * 2);
+  l.q_off = off;
+  off += round256(static_cast<size_t>(m->num_heads) * 128 * 2);
+  l.ao_off = off;
+  off += round256(static_cast<size_t>(m->num_heads) * 128 * 2);
+  l.a_off = off;
+  off += round256(static_cast<size_t>(m->intermediate) * 2);
+  l.total = off;
+  return l;
+}
+
+bool step_model_ok(const rib_qwen3_model *m) {
+  if (!m || m->num_layers < 1 || m->num_layers > RIB_QWEN3_MAX_LAYERS || m->num_kv_heads < 1 ||
+      m->num_heads != 2 * m->num_kv_heads || m->num_heads + 2 * m->num_kv_heads > rib::rope::kMaxItems ||
+      m->hidden < 256 || m->hidden % 256 || m->hidden > rib::model::kMaxK || m->intermediate < 256 ||
+      m->intermediate % 256 || m->intermediate > rib::model::kMaxK || (m->num_heads * 128) % 256 ||
+      m->num_heads * 128 > rib::model::kMaxK || m->vocab < 1 || !(m->rope_theta > 0.0))
+    return false;
+  return m->embed && m->final_norm;
+}
+
+bool g_step_smem_done[2][kMaxDevices];
+
+template <int CH, int CQ, int CI, int MQ, int MO, int MG, int MD>
+int step_launch(const rib::step::Params &p, int which, cudaStream_t st) {
+  auto kernel = rib::step::decode_step_kernel<CH, CQ, CI, MQ, MO, MG, MD>;
+  const int smem = static_cast<int>(sizeof(rib::decode::Smem)) + 128;
+  if (!set_smem_once(kernel, smem, g_step_smem_done[which]))
+    return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(decode step smem)", 0);
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, rib::step::NT, smem);
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaOccupancyMaxActiveBlocksPerMultiprocessor(decode step)", e);
+  if (per_sm < 1) return rib::host_fail(RIB_ECUDA, "decode step kernel does not fit on an SM", per_sm);
+  per_sm = std::min(per_sm, RIB_DECODE_SLOTS_PER_SM);
+  if (per_sm * sm_count() > rib::step::kMaxCtas)
+    return rib::host_fail(RIB_ECUDA, "decode step grid exceeds the barrier slots", per_sm * sm_count());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(per_sm * sm_count());
+  cfg.blockDim = dim3(rib::step::NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier relies on it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, p);
+  return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda("decode_step_kernel launch", e);
 }
 
 }  // namespace
@@ -619,6 +693,97 @@ int rib_argmax_f32(const float *x, int n, int32_t *out, void *workspace, void *s
   const int grid = std::max(1, std::min(ceil_div(n, 1024 * 4), sm_count()));
   return launch_pdl("argmax_kernel launch", rib::model::argmax_kernel, dim3(grid), dim3(1024), 0, st, x, n,
                     static_cast<rib::model::ArgmaxWs *>(workspace), out);
+}
+
+
+// ------------------------------------------------------------------ persistent decode step
+size_t rib_qwen3_step_workspace_bytes(const rib_qwen3_model *model, int cap) {
+  if (!step_model_ok(model) || cap < 1) return 0;
+  return step_layout(model, cap).total;
+}
+
+int rib_qwen3_step_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
+  const size_t head = kCounterRegionBytes + round256(sizeof(rib::step::Sync));
+  if (!workspace || workspace_bytes < head) return RIB_EINVAL;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255u) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const cudaError_t e = cudaMemsetAsync(workspace, 0, head, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda("cudaMemsetAsync(decode step workspace init)", e);
+}
+
+int rib_qwen3_decode_step(const rib_qwen3_model *m, const uint64_t *cache_ptrs, int cap, int32_t *token,
+                          int32_t *pos, int32_t *nkeys, float *logits, void *workspace, size_t workspace_bytes,
+                          void *stream) {
+  if (!step_model_ok(m) || !cache_ptrs || !token || !pos || !nkeys || !workspace || cap < 1) return RIB_EINVAL;
+  if (m->num_kv_heads > static_cast<int>(kCounterRegionUnits)) return RIB_EINVAL;
+  const StepLayout lay = step_layout(m, cap);
+  if (workspace_bytes < lay.total) return RIB_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) || (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) ||
+      (reinterpret_cast<uintptr_t>(token) & 3u) || (reinterpret_cast<uintptr_t>(pos) & 3u) ||
+      (reinterpret_cast<uintptr_t>(nkeys) & 3u) || (logits && (reinterpret_cast<uintptr_t>(logits) & 3u)) ||
+      !aligned16(m->embed) || !aligned16(m->final_norm))
+    return RIB_EALIGN;
+  rib::step::Params p;
+  p.L = m->num_layers;
+  p.hidden = m->hidden;
+  p.nq = m->num_heads;
+  p.nkv = m->num_kv_heads;
+  p.inter = m->intermediate;
+  p.vocab = m->vocab;
+  p.cap = cap;
+  p.embed = static_cast<const uint16_t *>(m->embed);
+  p.final_norm = static_cast<const uint16_t *>(m->final_norm);
+  for (int l = 0; l < m->num_layers; ++l) {
+    const rib_qwen3_layer &w = m->layers[l];
+    const void *ptrs[8] = {w.qkv, w.o, w.gu, w.down, w.in_norm, w.post_norm, w.q_norm, w.k_norm};
+    for (const void *q : ptrs) {
+      if (!q) return RIB_EINVAL;
+      if (!aligned16(q)) return RIB_EALIGN;
+    }
+    p.layer[l] = {static_cast<const uint16_t *>(w.qkv), static_cast<const uint16_t *>(w.o),
+                  static_cast<const uint16_t *>(w.gu), static_cast<const uint16_t *>(w.down),
+                  static_cast<const uint16_t *>(w.in_norm), static_cast<const uint16_t *>(w.post_norm),
+                  static_cast<const uint16_t *>(w.q_norm), static_cast<const uint16_t *>(w.k_norm)};
+  }
+  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(m->rope_theta, -static_cast<double>(d) / 64.0);
+  p.cache_ptrs = cache_ptrs;
+  p.tok = token;
+  p.pos = pos;
+  p.nkeys = nkeys;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  for (int i = 0; i < 3; ++i) p.h[i] = reinterpret_cast<uint16_t *>(ws + lay.h_off[i]);
+  p.qkv = reinterpret_cast<uint16_t *>(ws + lay.qkv_off);
+  p.q = reinterpret_cast<uint16_t *>(ws + lay.q_off);
+  p.o = reinterpret_cast<uint16_t *>(ws + lay.ao_off);
+  p.a = reinterpret_cast<uint16_t *>(ws + lay.a_off);
+  p.logits = logits;
+  p.sync = reinterpret_cast<rib::step::Sync *>(ws + lay.sync_off);
+  rib::decode::Params &dp = p.dp;
+  dp = rib::decode::Params{};
+  dp.q = p.q;
+  dp.cache_ptrs = cache_ptrs;
+  dp.cache = nullptr;
+  dp.lens = nkeys;
+  dp.n_single = 0;
+  dp.max_n = cap;
+  dp.cap = cap;
+  dp.nq = m->num_heads;
+  dp.nkv = m->num_kv_heads;
+  dp.chunk = lay.g.chunk;
+  dp.max_splits = lay.g.max_splits;
+  dp.qscale = (1.0f / std::sqrt(128.0f)) * 1.4426950408889634f;
+  dp.out = p.o;
+  dp.part_ml = reinterpret_cast<float *>(ws + lay.ml_off);
+  dp.part_o = reinterpret_cast<float *>(ws + lay.po_off);
+  dp.counters = reinterpret_cast<int *>(ws);
+  dp.world = 0;
+  dp.done = dp.counters + m->num_kv_heads;
+  dp.total_units = m->num_kv_heads;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (m->hidden == 1024 && m->num_heads * 128 == 2048 && m->intermediate == 3072)
+    return step_launch<4, 8, 12, 4, 1, 3, 1>(p, 0, st);  // Qwen3-0.6B widths
+  return step_launch<0, 0, 0, 0, 0, 0, 0>(p, 1, st);
 }
 
 }  // extern "C"

@@ -21,6 +21,7 @@ and the logits cover the final row only.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 from collections.abc import Iterator
 from dataclasses import dataclass
@@ -210,27 +211,38 @@ class Engine:
     def decode_graph(self, cache: Cache) -> "DecodeGraph":
         return DecodeGraph(self, cache)
 
-    def session(self, capacity: int) -> tuple[Cache, "DecodeGraph"]:
-        """A cache of at least `capacity` positions with its captured decode
-        graph, reused across requests (capacity rounded up to 1024): rows
-        past the offset are never read, so a request only resets the offset.
-        One request at a time per session."""
+    def persistent_decode(self, cache: Cache) -> "PersistentDecode":
+        return PersistentDecode(self, cache)
+
+    def session(self, capacity: int, mode: str = "graph"):
+        """A cache of at least `capacity` positions with its decode-step runner
+        (mode "graph": the captured CUDA graph, "persistent": the one-launch
+        step kernel), reused across requests (capacity rounded up to 1024):
+        rows past the offset are never read, so a request only resets the
+        offset.  One request at a time per session."""
+        if mode not in ("persistent", "graph"):
+            raise ValueError(f"unknown decode mode {mode!r}")
         bucket = (capacity + 1023) // 1024 * 1024
-        sess = self._sessions.get(bucket)
+        key = (bucket, mode)
+        sess = self._sessions.get(key)
         if sess is None:
             cache = self.new_cache(bucket)
-            sess = (cache, DecodeGraph(self, cache))
-            self._sessions[bucket] = sess
+            runner = PersistentDecode(self, cache) if mode == "persistent" else DecodeGraph(self, cache)
+            sess = (cache, runner)
+            self._sessions[key] = sess
         sess[0].offset = 0
         return sess
 
     # ---------------- generation ----------------
     def generate(self, prompt: list[int], *, max_tokens: int = 65, chunk: int = 4096, eos_ids=(),
-                 use_graph: bool = True) -> Iterator[int]:
+                 use_graph: bool = True, mode: str = "graph") -> Iterator[int]:
         """Greedy generation (engine.py:165-192): chunked prefill, the first
         token, then decode steps with one step of lookahead (step t+1 is
         enqueued before token t is read on the host).  With use_graph the
-        steps replay the session's captured CUDA graph."""
+        steps run on the session's runner: `mode` "graph" (a captured CUDA
+        graph of the multi-kernel step, the faster on B200) or "persistent"
+        (one cooperative launch per token); without it, eager multi-kernel
+        steps."""
         if not prompt or max_tokens < 0 or chunk < 1:
             raise ValueError("Nonempty prompt, nonnegative max_tokens, positive chunk required")
         if min(prompt) < 0 or max(prompt) >= self.cfg.vocab_size:
@@ -240,7 +252,7 @@ class Engine:
         eos_ids = set(eos_ids)
         need = len(prompt) + max_tokens + 1
         if use_graph:
-            cache, graph = self.session(need)
+            cache, graph = self.session(need, mode)
         else:
             cache, graph = self.new_cache(need), None
         tokens = torch.tensor(prompt, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
@@ -386,3 +398,72 @@ class DecodeGraph:
             yield token
             if token in eos_ids or not more:
                 break
+
+
+class _Qwen3Layer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("qkv", "o", "gu", "down", "in_norm", "post_norm", "q_norm", "k_norm")]
+
+
+class _Qwen3Model(ctypes.Structure):
+    """rib_qwen3_model (include/rib_attention.h)."""
+    _fields_ = [("num_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("num_heads", ctypes.c_int),
+                ("num_kv_heads", ctypes.c_int), ("intermediate", ctypes.c_int), ("vocab", ctypes.c_int),
+                ("rope_theta", ctypes.c_double), ("embed", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+                ("layers", _Qwen3Layer * 64)]
+
+
+class PersistentDecode:
+    """The decode step as one cooperative launch (rib_qwen3_decode_step): the
+    same state and interface as DecodeGraph (token, position and key count on
+    the device, advanced by the step itself), but the whole token runs in one
+    persistent kernel with grid barriers between its phases."""
+
+    def __init__(self, engine: Engine, cache: Cache):
+        cfg, dev = engine.cfg, engine.device
+        if cfg.num_layers > 64:
+            raise ValueError("the persistent decode step takes at most 64 layers")
+        self.e, self.cache, self.device = engine, cache, dev
+        m = _Qwen3Model()
+        m.num_layers, m.hidden, m.num_heads = cfg.num_layers, cfg.hidden_size, cfg.num_heads
+        m.num_kv_heads, m.intermediate, m.vocab = cfg.num_kv_heads, cfg.intermediate_size, cfg.vocab_size
+        m.rope_theta = float(cfg.rope_theta)
+        m.embed, m.final_norm = engine.embed.data_ptr(), engine.final_norm.data_ptr()
+        for i, w in enumerate(engine.layers):
+            for k in ("qkv", "o", "gu", "down", "in_norm", "post_norm", "q_norm", "k_norm"):
+                setattr(m.layers[i], k, w[k].data_ptr())
+        self._model = m
+        L = _lib.load()
+        nbytes = int(L.rib_qwen3_step_workspace_bytes(ctypes.byref(m), cache.capacity))
+        if nbytes == 0:
+            raise ValueError("model shape not supported by the persistent decode step")
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)   # zero-filled: ready
+        self.ptrs = torch.tensor([cache.kv[i].data_ptr() for i in range(cfg.num_layers)], dtype=torch.int64,
+                                 device=dev)
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.nkeys = torch.ones(1, dtype=torch.int32, device=dev)
+        self.logits = torch.empty(cfg.vocab_size, dtype=torch.float32, device=dev)
+        self.launches_per_step = 1
+
+    def set_state(self, token, pos: int) -> None:
+        if isinstance(token, torch.Tensor):
+            self.tok.copy_(token.reshape(-1)[:1])
+        else:
+            self.tok.fill_(int(token))
+        self.pos.fill_(int(pos))
+        self.nkeys.fill_(int(pos) + 1)
+
+    def replay(self, logits: bool = False) -> None:
+        """One decode step (see DecodeGraph.replay); with `logits` the FP32
+        logits land in self.logits."""
+        if self.cache.offset + 1 > self.cache.capacity:
+            raise ValueError("KV capacity exceeded")
+        st = _lib.load().rib_qwen3_decode_step(
+            ctypes.byref(self._model), self.ptrs.data_ptr(), self.cache.capacity, self.tok.data_ptr(),
+            self.pos.data_ptr(), self.nkeys.data_ptr(), self.logits.data_ptr() if logits else None,
+            self.ws.data_ptr(), self.ws.numel(), stream_handle(self.device))
+        _lib.check(st, "qwen3_decode_step")
+        self.cache.offset += 1
+
+    run = DecodeGraph.run

@@ -233,3 +233,48 @@ def test_decode_graph_state_and_launch_count(rib):
     assert toks_g == toks_e
     assert int(g.pos.item()) == cache.offset == ref_cache.offset == 14
     assert torch.equal(cache.storage[:, :, :, :14], ref_cache.storage[:, :, :, :14])
+
+
+# ------------------------------------------------------------------ persistent decode step
+def _persistent_vs_graph(rib, cfg, seed, n_prompt=37, steps=6):
+    eng = rib.Engine(rib.random_weights(cfg, seed=seed).to(DEV))
+    cap = n_prompt + steps + 16
+    ca, cb = eng.new_cache(cap), eng.new_cache(cap)
+    toks = torch.tensor(np.random.default_rng(seed).integers(0, cfg.vocab_size, n_prompt).astype(np.int32),
+                        device=DEV)
+    first = rib.argmax(eng.prefill(toks, ca, last=True).reshape(-1))
+    cb.storage.copy_(ca.storage)
+    cb.offset = ca.offset
+    g, pd = eng.decode_graph(ca), eng.persistent_decode(cb)
+    g.set_state(first, ca.offset)
+    pd.set_state(first, cb.offset)
+    tg, tp, errs = [], [], []
+    for _ in range(steps):
+        g.replay()
+        pd.replay(logits=True)
+        tg.append(int(g.tok.item()))
+        tp.append(int(pd.tok.item()))
+        scale = g.logits.abs().max().item()
+        errs.append((pd.logits - g.logits).abs().max().item() / scale)
+    assert rib._lib.take_device_status() == 0
+    assert tp == tg, (tp, tg)
+    assert max(errs) <= 1e-2, errs
+    assert int(pd.pos.item()) == cb.offset == ca.offset == n_prompt + steps
+    assert torch.equal(ca.storage[:, :, :, :cb.offset], cb.storage[:, :, :, :cb.offset])
+    return eng
+
+
+def test_persistent_step_tiny_config(rib):
+    """The generic instantiation (runtime K loops, no prefetch)."""
+    cfg = rib.Qwen3Config(num_layers=3, hidden_size=256, num_heads=2, num_kv_heads=1,
+                          intermediate_size=512, vocab_size=1000)
+    _persistent_vs_graph(rib, cfg, seed=31)
+
+
+def test_persistent_step_qwen3_widths(rib):
+    """The Qwen3-0.6B instantiation (prefetched weight rows), 2 layers."""
+    eng = _persistent_vs_graph(rib, rib.Qwen3Config(num_layers=2), seed=32)
+    prompt = list(np.random.default_rng(33).integers(0, 151936, 70))
+    a = list(eng.generate(prompt, max_tokens=10, mode="persistent"))
+    b = list(eng.generate(prompt, max_tokens=10, mode="graph"))
+    assert a == b and len(a) == 10
