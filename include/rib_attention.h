@@ -222,6 +222,22 @@ int rib_decode_attention_gather(const void *q, const uint64_t *cache_ptrs,
                                 unsigned long long epoch, void *workspace,
                                 size_t workspace_bytes, void *stream);
 
+/* The same with the epoch kept on the device, for CUDA-graph replay: the call
+ * uses *epoch_dev + 1 (an 8-byte-aligned counter in device memory, zero on
+ * every rank before the first call) and stores it back, so every replay
+ * gets the next epoch.  The output region alternates with the epoch as
+ * above; after every rank's outputs have arrived, the kernel also copies
+ * them into out_copy [batch, world * nq, 128], a fixed address that the
+ * captured consumer can read.  Every rank makes the same sequence of calls
+ * with its own counter. */
+int rib_decode_attention_gather_dev(const void *q, const uint64_t *cache_ptrs,
+                                    const int32_t *lens, int batch, int max_n,
+                                    int cap, int nq, int nkv, float scale,
+                                    const rib_peer_gather *g,
+                                    unsigned long long *epoch_dev,
+                                    void *out_copy, void *workspace,
+                                    size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------ *
  * Causal GQA prefill attention (tcgen05 / TMEM flash attention).
  * Replaces attention(Q, K, V, qL, kL, scale, ...) (agent-test/v2/attention.py

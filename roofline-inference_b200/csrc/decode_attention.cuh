@@ -83,6 +83,13 @@ struct Params {
   unsigned long long epoch;               // > 0, increases by one per call
   int *done;                              // units finalised in this call
   int total_units;
+  // Device-side epoch (CUDA-graph replay): when set, the call's epoch is
+  // *epoch_dev + 1, gout[] are region bases (region = epoch & 1, region_elems
+  // elements each), the last unit stores the epoch back and copies this
+  // rank's gathered region into gcopy.
+  unsigned long long *epoch_dev;
+  size_t region_elems;
+  uint16_t *gcopy;
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned long long *addr, unsigned long long v) {
@@ -110,12 +117,16 @@ __device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int
     }
     return;
   }
+  // this call's epoch and output region (both fixed on the host, or the
+  // region chosen by the epoch read from the device)
+  const unsigned long long epoch = p.epoch_dev ? __ldcg(p.epoch_dev) + 1 : p.epoch;
+  const size_t region = p.epoch_dev ? (epoch & 1ull) * p.region_elems : 0;
   if (tid < D) {
     const size_t row = static_cast<size_t>(b) * p.nq_total + p.rank * p.nq + 2 * h;
     for (int r = 0; r < p.world; ++r) {
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh)
-        p.gout[r][(row + hh) * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(res[hh]));
+        p.gout[r][region + (row + hh) * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(res[hh]));
     }
     __threadfence_system();
   }
@@ -125,12 +136,12 @@ __device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int
   if (!flag) return;
   // last unit of this rank: signal every peer, then wait for every peer
   __threadfence_system();
-  if (tid < p.world) st_release_sys(p.gsig[tid] + p.rank, p.epoch);
+  if (tid < p.world) st_release_sys(p.gsig[tid] + p.rank, epoch);
   if (tid < p.world) {
     const unsigned long long *slot = p.gsig[p.rank] + tid;
-    if (ld_acquire_sys(slot) < p.epoch) {
+    if (ld_acquire_sys(slot) < epoch) {
       const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(slot) < p.epoch) {
+      while (ld_acquire_sys(slot) < epoch) {
         if (global_timer_ns() - t0 > kWaitLimitNs) {
           record_timeout();
           break;
@@ -139,6 +150,14 @@ __device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int
     }
   }
   __syncthreads();
+  if (p.epoch_dev) {
+    // every rank's outputs are in this rank's region: copy them to the fixed buffer
+    const size_t n16 = static_cast<size_t>(p.total_units / p.nkv) * p.nq_total * D / 8;
+    const uint4 *src = reinterpret_cast<const uint4 *>(p.gout[p.rank] + region);
+    for (size_t i = tid; i < n16; i += NTHREADS) reinterpret_cast<uint4 *>(p.gcopy)[i] = __ldcg(src + i);
+    __syncthreads();
+    if (tid == 0) *p.epoch_dev = epoch;
+  }
   if (tid == 0) *p.done = 0;  // ready for the next call
 }
 

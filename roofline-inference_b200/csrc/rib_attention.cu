@@ -561,6 +561,46 @@ int rib_decode_attention_gather(const void *q, const uint64_t *cache_ptrs, const
   return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
 }
 
+int rib_decode_attention_gather_dev(const void *q, const uint64_t *cache_ptrs, const int32_t *lens,
+                                    int batch, int max_n, int cap, int nq, int nkv, float scale,
+                                    const rib_peer_gather *g, unsigned long long *epoch_dev,
+                                    void *out_copy, void *workspace, size_t workspace_bytes, void *stream) {
+  if (!q || !cache_ptrs || !lens || !g || !epoch_dev || !out_copy) return RIB_EINVAL;
+  if (batch < 1 || nkv < 1 || nq != 2 * nkv || max_n < 1 || cap < 1 || !(scale > 0.f))
+    return RIB_EINVAL;
+  if (g->world < 1 || g->world > RIB_MAX_PEERS || g->rank < 0 || g->rank >= g->world) return RIB_EINVAL;
+  const size_t elems = static_cast<size_t>(batch) * g->world * nq * 128;
+  if (g->region_bytes < elems * 2 || (g->region_bytes & 15u)) return RIB_EINVAL;
+  if (max_n > cap) return RIB_ECAPACITY;
+  if (!aligned16(q) || !aligned16(out_copy) || (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) ||
+      (reinterpret_cast<uintptr_t>(lens) & 3u) || (reinterpret_cast<uintptr_t>(epoch_dev) & 7u))
+    return RIB_EALIGN;
+  rib::decode::Params p = {};
+  for (int r = 0; r < g->world; ++r) {
+    if (!g->out[r] || !g->sig[r] || (g->out[r] & 15u) || (g->sig[r] & 7u)) return RIB_EALIGN;
+    p.gout[r] = reinterpret_cast<uint16_t *>(g->out[r]);
+    p.gsig[r] = reinterpret_cast<unsigned long long *>(g->sig[r]);
+  }
+  p.q = static_cast<const uint16_t *>(q);
+  p.cache = nullptr;
+  p.cache_ptrs = cache_ptrs;
+  p.lens = lens;
+  p.cap = cap;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = nullptr;
+  p.world = g->world;
+  p.rank = g->rank;
+  p.nq_total = g->world * nq;
+  p.epoch = 0;
+  p.epoch_dev = epoch_dev;
+  p.region_elems = g->region_bytes / 2;
+  p.gcopy = static_cast<uint16_t *>(out_copy);
+  p.total_units = batch * nkv;
+  return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
+}
+
 int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs, const int32_t *lens,
                                  int batch, int max_n, int cap, int nq, int nkv, float scale,
                                  void *out, void *workspace, size_t workspace_bytes, void *stream) {

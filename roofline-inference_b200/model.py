@@ -121,8 +121,25 @@ def _linear(x, W):
     return torch.matmul(x, W.t())
 
 
+def _shard_qkv_rows(W: torch.Tensor, h0: int, h1: int, nq: int, nkv: int) -> torch.Tensor:
+    """Rows of a [(nq + 2 nkv) * 128, hidden] QKV weight for KV heads [h0, h1):
+    their query heads, K heads and V heads, in the fused kernel's order."""
+    x = W.reshape(nq + 2 * nkv, HEAD_DIM, W.shape[1])
+    return torch.cat([x[2 * h0:2 * h1], x[nq + h0:nq + h1], x[nq + nkv + h0:nq + nkv + h1]]) \
+        .reshape(-1, W.shape[1]).contiguous()
+
+
 class Engine:
-    def __init__(self, weights: Qwen3Weights):
+    """The Qwen3 forward on one GPU, or KV-head sharded over the ranks of a
+    torch.distributed group (shard=True): rank r owns KV heads
+    sharding.head_range(r, world) -- their rows of each QKV projection, their
+    K/V cache and their attention -- and every rank receives every head's
+    attention output (decode: the decode kernel's own NVLink stores; prefill:
+    an NCCL all-gather), then runs the rest of the layer on the full hidden
+    state, so all ranks hold the same activations and tokens.  Every rank
+    makes the same calls in the same order."""
+
+    def __init__(self, weights: Qwen3Weights, *, shard: bool = False, group=None):
         cfg = weights.config
         cfg.validate()
         if not weights.embed.is_cuda:
@@ -131,16 +148,67 @@ class Engine:
         self.cfg = cfg
         self.w = weights
         self.device = weights.embed.device
-        self.n_heads, self.n_kv = cfg.num_heads, cfg.num_kv_heads
+        self.n_heads = cfg.num_heads              # all query heads (the O projection's input)
         self.scale = HEAD_DIM ** -0.5
         self.base = cfg.rope_theta
-        self.layers = weights.layers
         self.embed = weights.embed
         self.final_norm = weights.final_norm
-        self._sessions: dict[int, tuple[Cache, DecodeGraph]] = {}
+        self.group = group
+        self.world, self.rank = 1, 0
+        self.gather = None
+        if shard:
+            import torch.distributed as dist
+            from .nvlink_gather import NVLinkGather
+            from .sharding import head_range
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+            h0, h1 = head_range(self.rank, self.world, cfg.num_kv_heads)
+        else:
+            h0, h1 = 0, cfg.num_kv_heads
+        self.n_kv = h1 - h0                       # KV heads of this rank
+        self.nq_local = 2 * self.n_kv             # query heads of this rank
+        if self.world > 1:
+            self.layers = [dict(l, qkv=_shard_qkv_rows(l["qkv"], h0, h1, cfg.num_heads, cfg.num_kv_heads))
+                           for l in weights.layers]
+            self.gather = NVLinkGather(1, self.nq_local, self.device, group)
+            self.epoch_dev = torch.zeros(1, dtype=torch.int64, device=self.device)
+        else:
+            self.layers = weights.layers
+        self._sessions: dict = {}
 
     def new_cache(self, capacity: int) -> Cache:
         return Cache(self.cfg.num_layers, self.n_kv, HEAD_DIM, capacity, device=self.device)
+
+    def close(self) -> None:
+        """Collective when sharded: releases the NVLink gather buffers."""
+        self._sessions.clear()
+        if self.gather is not None:
+            self.gather.close()
+            self.gather = None
+
+    def _attend_one(self, q, cache_layer, n: int, out=None):
+        """Decode attention of one query row over n keys: [1, nq_local, 128] in,
+        [1, n_heads, 128] out (all ranks' heads when sharded)."""
+        if self.world == 1:
+            return decode_attention(q, cache_layer, n, self.scale).reshape(1, self.n_heads, HEAD_DIM)
+        from .attention import decode_workspace
+        L = _lib.load()
+        ws = decode_workspace(self.device, int(L.rib_decode_workspace_bytes(1, n, self.n_kv)))
+        ptrs = torch.tensor([cache_layer.data_ptr()], dtype=torch.int64, device=self.device)
+        lens = torch.tensor([n], dtype=torch.int32, device=self.device)
+        out = torch.empty((1, self.n_heads, HEAD_DIM), dtype=torch.bfloat16, device=self.device) \
+            if out is None else out
+        return self.gather.decode_into(q.reshape(1, self.nq_local, HEAD_DIM).contiguous(), ptrs, lens, n,
+                                       cache_layer.shape[2], self.scale, ws, self.epoch_dev, out)
+
+    def _gather_rows(self, o_local):
+        """[n, nq_local * 128] per rank -> [n, n_heads * 128] (NCCL all-gather)."""
+        if self.world == 1:
+            return o_local
+        import torch.distributed as dist
+        n = o_local.shape[0]
+        buf = torch.empty((self.world, n, o_local.shape[1]), dtype=o_local.dtype, device=o_local.device)
+        dist.all_gather_into_tensor(buf, o_local.contiguous(), group=self.group)
+        return buf.permute(1, 0, 2).reshape(n, -1)
 
     # ---------------- prefill (M >= 1) ----------------
     def prefill(self, tokens, cache: Cache, *, last: bool, all_logits: bool = False):
@@ -158,19 +226,19 @@ class Engine:
         h = embedding(self.embed, tokens)                                   # [n, hidden]
         x = rms_norm(h, self.layers[0]["in_norm"])
         for i, w in enumerate(self.layers):
-            q = qk_norm_rope_append(_linear(x, w["qkv"]), w["q_norm"], w["k_norm"], off, self.n_heads,
-                                    self.n_kv, self.base, cache.kv[i], Lp)    # [nq, Lp, 128]
+            q = qk_norm_rope_append(_linear(x, w["qkv"]), w["q_norm"], w["k_norm"], off, self.nq_local,
+                                    self.n_kv, self.base, cache.kv[i], Lp)    # [nq_local, Lp, 128]
             final = i == nl - 1
             if final and not last:
                 break        # last layer's K/V written; its outputs are dead for a middle chunk
             if final and not all_logits:
                 # Only the final row feeds the logits: attention/MLP for one row (engine.py:118-121).
                 qrow = q[:, n - 1, :].contiguous()
-                o = decode_attention(qrow, cache.kv[i], off + n, self.scale).reshape(1, -1)
+                o = self._attend_one(qrow, cache.kv[i], off + n).reshape(1, -1)
                 h = h[n - 1:]
             else:
                 kvl = cache.kv[i]
-                o = attention(q, kvl[0], kvl[1], n, off + n, self.scale)     # [n, H*128]
+                o = self._gather_rows(attention(q, kvl[0], kvl[1], n, off + n, self.scale))  # [n, H*128]
             h, x = add_rms(h, _linear(o, w["o"]), w["post_norm"])
             r = _linear(swiglu(_linear(x, w["gu"])), w["down"])
             if final:
@@ -196,9 +264,9 @@ class Engine:
         h = embedding(self.embed, token.reshape(-1)).reshape(-1)
         for i, w in enumerate(self.layers):
             qkv = gemv(w["qkv"], h, nw=w["in_norm"])
-            q = qk_norm_rope_append(qkv, w["q_norm"], w["k_norm"], pos, self.n_heads, self.n_kv,
+            q = qk_norm_rope_append(qkv, w["q_norm"], w["k_norm"], pos, self.nq_local, self.n_kv,
                                     self.base, cache.kv[i])
-            o = decode_attention(q, cache.kv[i], n, self.scale)
+            o = self._attend_one(q, cache.kv[i], n)
             h = gemv(w["o"], o.reshape(-1), res=h)
             a = gemv(w["gu"], h, nw=w["post_norm"], swiglu=True)
             h = gemv(w["down"], a, res=h)
@@ -300,18 +368,18 @@ class DecodeGraph:
         self.nkeys = torch.ones(1, dtype=torch.int32, device=dev)
         self.ptrs = torch.tensor([cache.kv[i].data_ptr() for i in range(cfg.num_layers)],
                                  dtype=torch.int64, device=dev)
-        d, qkvw = cfg.hidden_size, cfg.q_dim + 2 * cfg.kv_dim
+        d, qkvw = cfg.hidden_size, (engine.nq_local + 2 * engine.n_kv) * HEAD_DIM
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.h = [torch.empty(d, **bf), torch.empty(d, **bf), torch.empty(d, **bf)]
         self.x = torch.empty((1, d), **bf)
         self.qkv = torch.empty(qkvw, **bf)
-        self.q = torch.empty((self.e.n_heads, 1, HEAD_DIM), **bf)
+        self.q = torch.empty((self.e.nq_local, 1, HEAD_DIM), **bf)
         self.o = torch.empty((1, self.e.n_heads, HEAD_DIM), **bf)
         self.a = torch.empty(cfg.intermediate_size, **bf)
         self.logits = torch.empty(cfg.vocab_size, dtype=torch.float32, device=dev)
         L = _lib.load()
         self.max_n = cache.capacity
-        ws_bytes = int(L.rib_decode_workspace_bytes(1, self.max_n, cfg.num_kv_heads))
+        ws_bytes = int(L.rib_decode_workspace_bytes(1, self.max_n, engine.n_kv))
         self.ws = torch.zeros(max(ws_bytes, 1 << 20), dtype=torch.uint8, device=dev)  # counters zero
         self.argmax_ws = torch.empty(int(L.rib_argmax_workspace_bytes()), dtype=torch.uint8, device=dev)
         self.launches_per_step = 0
@@ -343,13 +411,17 @@ class DecodeGraph:
         launches += 1
         for i, w in enumerate(e.layers):
             gemv(w["qkv"], h, nw=w["in_norm"], out=self.qkv)
-            qk_norm_rope_append_at(self.qkv, w["q_norm"], w["k_norm"], self.pos, e.n_heads, e.n_kv, e.base,
+            qk_norm_rope_append_at(self.qkv, w["q_norm"], w["k_norm"], self.pos, e.nq_local, e.n_kv, e.base,
                                    self.cache.kv[i], out=self.q)
-            rc = L.rib_decode_attention_batched(self.q.data_ptr(), self.ptrs.data_ptr() + 8 * i,
-                                                self.nkeys.data_ptr(), 1, self.max_n, self.cache.capacity,
-                                                e.n_heads, e.n_kv, float(e.scale), self.o.data_ptr(),
-                                                self.ws.data_ptr(), self.ws.numel(), st)
-            _lib.check(rc, "decode_attention_batched")
+            if e.world > 1:   # this rank's heads, every rank's outputs into self.o over NVLink
+                e.gather.decode_into(self.q.view(1, e.nq_local, HEAD_DIM), self.ptrs[i:i + 1], self.nkeys,
+                                     self.max_n, self.cache.capacity, e.scale, self.ws, e.epoch_dev, self.o)
+            else:
+                rc = L.rib_decode_attention_batched(self.q.data_ptr(), self.ptrs.data_ptr() + 8 * i,
+                                                    self.nkeys.data_ptr(), 1, self.max_n, self.cache.capacity,
+                                                    e.nq_local, e.n_kv, float(e.scale), self.o.data_ptr(),
+                                                    self.ws.data_ptr(), self.ws.numel(), st)
+                _lib.check(rc, "decode_attention_batched")
             h1 = gemv(w["o"], self.o.view(-1), res=h, out=self.h[1])
             gemv(w["gu"], h1, nw=w["post_norm"], swiglu=True, out=self.a)
             h = gemv(w["down"], self.a, res=h1, out=self.h[2 if h is not self.h[2] else 0])
@@ -423,6 +495,8 @@ class PersistentDecode:
         cfg, dev = engine.cfg, engine.device
         if cfg.num_layers > 64:
             raise ValueError("the persistent decode step takes at most 64 layers")
+        if engine.world > 1:
+            raise ValueError("the persistent decode step runs on one GPU (use mode='graph' when sharded)")
         self.e, self.cache, self.device = engine, cache, dev
         m = _Qwen3Model()
         m.num_layers, m.hidden, m.num_heads = cfg.num_layers, cfg.hidden_size, cfg.num_heads

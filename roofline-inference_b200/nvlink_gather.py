@@ -56,6 +56,9 @@ def _bind(L: ctypes.CDLL) -> None:
                                               ctypes.POINTER(_PeerGatherStruct),
                                               ctypes.c_ulonglong, vp, sz, vp]
     L.rib_decode_attention_gather.restype = i
+    L.rib_decode_attention_gather_dev.argtypes = [vp, vp, vp, i, i, i, i, i, ctypes.c_float,
+                                                  ctypes.POINTER(_PeerGatherStruct), vp, vp, vp, sz, vp]
+    L.rib_decode_attention_gather_dev.restype = i
 
 
 class NVLinkGather:
@@ -132,6 +135,29 @@ class NVLinkGather:
             workspace.data_ptr(), workspace.numel(), stream_handle(self.device))
         _lib.check(st, "decode_attention_gather")
         return self.output()
+
+    def decode_into(self, q, cache_ptrs, lens, max_n: int, cap: int, scale: float, workspace: torch.Tensor,
+                    epoch_dev: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """decode() with the epoch in `epoch_dev` (int64 CUDA tensor of one
+        element, zero on every rank before the first call) and the gathered
+        outputs copied into `out` [batch, world*nq_local, 128]: every argument
+        is a fixed device address, so the call can be captured in a CUDA graph
+        and replayed."""
+        require_bf16_cuda("q", q)
+        require_bf16_cuda("out", out)
+        if self.closed:
+            raise RuntimeError("NVLinkGather is closed")
+        if out.numel() != self.batch * self.nq_total * 128:
+            raise ValueError("out must hold [batch, world * nq_local, 128]")
+        if epoch_dev.dtype != torch.int64 or epoch_dev.numel() != 1 or not epoch_dev.is_cuda:
+            raise ValueError("epoch_dev must be a one-element int64 CUDA tensor")
+        nkv = self.nq_local // 2
+        st = self.L.rib_decode_attention_gather_dev(
+            q.data_ptr(), cache_ptrs.data_ptr(), lens.data_ptr(), self.batch, int(max_n), int(cap),
+            self.nq_local, nkv, float(scale), ctypes.byref(self.g), epoch_dev.data_ptr(), out.data_ptr(),
+            workspace.data_ptr(), workspace.numel(), stream_handle(self.device))
+        _lib.check(st, "decode_attention_gather_dev")
+        return out
 
     def close(self) -> None:
         """Collective: unmap the peers' buffers and free this rank's."""

@@ -94,3 +94,61 @@ def test_decode_nvlink_gather_two_gpus():
     for r, v in res.items():
         assert not isinstance(v, str), f"rank {r}: {v}"
         assert v[1] == 0, f"rank {r}: device status {v[1]}"
+
+
+# ------------------------------------------------------------------ sharded Qwen3 forward
+def _engine_worker(rank, world, port, q_out):
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                             timeout=datetime.timedelta(seconds=60))
+        rib = importlib.import_module("roofline-inference_b200")
+        cfg = rib.Qwen3Config(num_layers=2, hidden_size=256, num_heads=4, num_kv_heads=2,
+                              intermediate_size=512, vocab_size=1000)
+        w = rib.random_weights(cfg, seed=61).to(dev)           # identical on every rank
+        prompt = [int(t) for t in np.random.default_rng(62).integers(0, cfg.vocab_size, 45)]
+        eng = rib.Engine(w, shard=True)
+        assert eng.n_kv == 1 and eng.nq_local == 2
+        graph = list(eng.generate(prompt, max_tokens=10))                 # CUDA-graph steps
+        eager = list(eng.generate(prompt, max_tokens=10, use_graph=False))
+        # prefill logits of the sharded forward against the single-GPU forward
+        toks = torch.tensor(prompt, dtype=torch.int32, device=dev)
+        ls = eng.prefill(toks, eng.new_cache(64), last=True).reshape(-1)
+        ref = rib.Engine(w)                                     # no collective calls
+        lr = ref.prefill(toks, ref.new_cache(64), last=True).reshape(-1)
+        rel = float((ls - lr).abs().max() / lr.abs().max())
+        single = list(ref.generate(prompt, max_tokens=10))
+        status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
+        eng.close()
+        torch.distributed.destroy_process_group()
+        q_out.put((rank, (graph, eager, single, rel, status)))
+    except Exception as e:  # report to the parent
+        q_out.put((rank, repr(e)))
+
+
+def test_sharded_engine_two_gpus():
+    """KV-head sharded Qwen3 forward on 2 GPUs: both ranks generate the same
+    tokens as the single-GPU engine (graph and eager decode), and the sharded
+    prefill's logits match the single-GPU ones."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_engine_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert not isinstance(v, str), f"rank {r}: {v}"
+        graph, eager, single, rel, status = v
+        assert status == 0, f"rank {r}: device status {status}"
+        assert rel <= 1e-2, f"rank {r}: prefill logits differ by {rel}"
+        assert graph == eager == single, (r, graph, eager, single)
+    assert res[0][0] == res[1][0]
