@@ -761,19 +761,24 @@ def run_full_model(rib, rank, world, device, args):
     1024, 16/8 heads, FFN 3072, vocab 151936, tied embeddings, BF16): the
     engine's CUDA-graph decode step at context 32768 (K/V seeded N(0, 1)), and
     a 4096-token prompt + 128 generated tokens through Engine.generate (host
-    token ids in, host token ids out; wall clock).  Each GPU runs its own
-    replica; times are the max over ranks, tokens/s the sum over ranks.  Each
-    figure is reported against the full-model Level-A line (cold start)."""
+    token ids in, host token ids out; wall clock).  At N > 1 one sequence runs
+    KV-head sharded over all ranks (Engine(shard=True): each rank owns 8/N KV
+    heads, the decode kernel gathers every head's output over NVLink, the
+    rest of the layer runs on every rank); times are the max over ranks.
+    Each figure is reported against the full-model Level-A line (cold start)."""
     rl = importlib.import_module("roofline-inference_b200.roofline_line")
     cfg = rib.QWEN3_0_6B
-    eng = rib.Engine(rib.random_weights(cfg, seed=11 + rank, device=device))
-    out = {"model": "Qwen3-0.6B, random-init N(0, 0.02) weights, BF16", "replicas": world}
+    # the same seed on every rank: identical weights, as a sharded engine needs
+    eng = rib.Engine(rib.random_weights(cfg, seed=11, device=device), shard=world > 1)
+    out = {"model": "Qwen3-0.6B, random-init N(0, 0.02) weights, BF16",
+           "parallelism": f"kv-head shard x{world}" if world > 1 else "1 GPU",
+           "kv_heads_per_rank": eng.n_kv}
 
     # decode step at context 32768
     ctx, steps, warm = 32768, max(1, min(args.steps, 200)), max(3, min(args.warmup, 20))
     cache = eng.new_cache(ctx + 2 * (steps + warm) + 8)
     g = torch.Generator(device=device)
-    g.manual_seed(12 + rank)
+    g.manual_seed(12 + rank)     # this rank's KV heads
     for i in range(cfg.num_layers):
         cache.storage[i, :, :, :ctx].normal_(generator=g)
     cache.offset = ctx
@@ -792,41 +797,40 @@ def run_full_model(rib, rank, world, device, args):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(a.elapsed_time(b) / steps, world, device)
-    # the same step as one persistent cooperative launch per token
-    cache.offset = ctx + warm + steps
-    pers = eng.persistent_decode(cache)
-    pers.set_state(1, cache.offset)
-    for _ in range(warm):
-        pers.replay()
-    barrier(world)
-    torch.cuda.synchronize()
-    a.record(stream)
-    for _ in range(steps):
-        pers.replay()
-    b.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    pms = max_over_ranks(a.elapsed_time(b) / steps, world, device)
     line = rl.model_decode_line(cfg, ctx + warm)
-    out["decode_step_persistent"] = {
-        "ms_per_token": pms, "tokens_per_s": world * 1000.0 / pms, "launches_per_step": 1,
-        "path": "rib_qwen3_decode_step: one cooperative launch per token, 169 grid barriers",
-        "fraction_of_line": line["time_s"] * 1e3 / pms}
-    del pers
+    if world == 1:  # the same step as one persistent cooperative launch per token
+        cache.offset = ctx + warm + steps
+        pers = eng.persistent_decode(cache)
+        pers.set_state(1, cache.offset)
+        for _ in range(warm):
+            pers.replay()
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(steps):
+            pers.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        pms = a.elapsed_time(b) / steps
+        out["decode_step_persistent"] = {
+            "ms_per_token": pms, "tokens_per_s": 1000.0 / pms, "launches_per_step": 1,
+            "path": "rib_qwen3_decode_step: one cooperative launch per token, 169 grid barriers",
+            "fraction_of_line": line["time_s"] * 1e3 / pms}
+        del pers
     out["decode_step"] = {
         "context": f"{ctx + warm}..{ctx + warm + steps}", "steps": steps, "ms_per_token": ms,
-        "tokens_per_s": world * 1000.0 / ms, "launches_per_step": dg.launches_per_step,
+        "tokens_per_s": 1000.0 / ms, "launches_per_step": dg.launches_per_step,
         "path": "one CUDA-graph replay per token (embedding, 28 x [norm+QKV GEMV, qk-norm+RoPE+KV "
                 "append, split-KV decode attention, O GEMV+residual, norm+gate/up GEMV+SwiGLU, "
                 "down GEMV+residual], final norm + LM-head GEMV, argmax)",
         "reference_line_ms": line["time_s"] * 1e3, "reference_bottleneck": line["bottleneck"],
+        "reference_line_scope": "one GPU (the whole model's bytes over one GPU's bandwidth)",
         "fraction_of_line": line["time_s"] * 1e3 / ms}
     del dg, cache
     torch.cuda.empty_cache()
 
     # a 4096-token prompt + 128 generated tokens
     P, G = 4096, 128
-    prompt = torch.randint(0, cfg.vocab_size, (P,), generator=torch.Generator().manual_seed(13 + rank))
+    prompt = torch.randint(0, cfg.vocab_size, (P,), generator=torch.Generator().manual_seed(13))
     prompt = prompt.tolist()
     list(eng.generate(prompt, max_tokens=G))          # warm-up: captures the session's graph
     ttft, dec, tot = [], [], []
@@ -848,10 +852,11 @@ def run_full_model(rib, rank, world, device, args):
     t_ttft, t_dec, t_tot = statistics.median(ttft), statistics.median(dec), statistics.median(tot)
     out["request"] = {
         "prompt": P, "generated": G, "repeats": 3, "timing": "host wall clock, median",
-        "ttft_ms": t_ttft * 1e3, "decode_tokens_per_s": world * (G - 1) / t_dec,
+        "ttft_ms": t_ttft * 1e3, "decode_tokens_per_s": (G - 1) / t_dec,
         "total_ms": t_tot * 1e3,
         "reference_line": {"ttft_ms": rline["ttft_s"] * 1e3, "total_ms": rline["total_s"] * 1e3},
         "fraction_ttft": rline["ttft_s"] / t_ttft, "fraction_total": rline["total_s"] / t_tot}
+    eng.close()  # collective when sharded
     return out
 
 
