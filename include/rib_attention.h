@@ -375,6 +375,37 @@ int rib_qwen3_decode_step(const rib_qwen3_model *model,
                           void *workspace, size_t workspace_bytes,
                           void *stream);
 
+/* ------------------------------------------------------------------------ *
+ * Batched ragged decode of the whole model: B independent sequences, each in
+ * its own contiguous cache of its own capacity (engine.py:33-40 generalised
+ * to many sequences; the reference engine is single-stream).
+ *
+ * Decode attention over per-sequence caches: as
+ * rib_decode_attention_batched, with caps[b] the capacity (rows per head)
+ * of sequence b's cache [2, nkv, caps[b], 128] and max_n >= every lens[b]. */
+int rib_decode_attention_ragged(const void *q, const uint64_t *cache_ptrs,
+                                const int32_t *caps, const int32_t *lens,
+                                int batch, int max_n, int nq, int nkv,
+                                float scale, void *out, void *workspace,
+                                size_t workspace_bytes, void *stream);
+
+/* Fused RMSNorm + RoPE + KV append of one new token per sequence:
+ *   qkv [B, (nq + 2 nkv) * 128], pos [B] device int32 (each token's position,
+ *   the cache row written), cache_ptrs [B], caps [B] as above,
+ *   q_out [B, nq, 128].
+ * A position outside [0, caps[b]) writes nothing for that sequence and sets
+ * the device status word to RIB_ECAPACITY. */
+int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw,
+                                    const void *kw, const int32_t *pos,
+                                    const uint64_t *cache_ptrs,
+                                    const int32_t *caps, int batch, int nq,
+                                    int nkv, double base, void *q_out,
+                                    void *stream);
+
+/* Greedy token of each row of x [rows, n] FP32 (the first index on ties). */
+int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out,
+                        void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -16,8 +16,10 @@ from .cache import Cache
 from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope, qk_norm_rope_append,
                       qk_norm_rope_append_at, qk_norm_rope_prefill, rms_norm, swiglu)
 from .model import QWEN3_0_6B, DecodeGraph, Engine, Qwen3Config, Qwen3Weights, random_weights
+from .batch import BatchDecoder, generate_batch
 
 __all__ = [
+    "BatchDecoder",
     "Cache",
     "DecodeGraph",
     "Engine",
@@ -28,6 +30,7 @@ __all__ = [
     "argmax",
     "embedding",
     "gemv",
+    "generate_batch",
     "qk_norm_rope_append_at",
     "random_weights",
     "rms_norm",

@@ -118,6 +118,9 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_qwen3_step_workspace_bytes": ([vp, i], sz),
         "rib_qwen3_step_workspace_init": ([vp, sz, vp], i),
         "rib_qwen3_decode_step": ([vp, vp, i, vp, vp, vp, vp, vp, sz, vp], i),
+        "rib_decode_attention_ragged": ([vp, vp, vp, vp, i, i, i, i, f, vp, vp, sz, vp], i),
+        "rib_qk_norm_rope_append_batched": ([vp, vp, vp, vp, vp, vp, i, i, i, d, vp, vp], i),
+        "rib_argmax_rows_f32": ([vp, i, i, vp, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -75,6 +75,7 @@ struct Params {
   float *part_ml;              // [B][nkv][max_splits][2][2]  (m, l)
   float *part_o;               // [B][nkv][max_splits][2][128]
   int *counters;               // [B][nkv]
+  const int32_t *caps;         // [B] per-sequence capacities (rows per head), or null: cap
   // All-gather over NVLink (world > 0): the outputs of this rank's heads go
   // straight into every rank's gathered buffer instead of `out`.
   int world, rank, nq_total;
@@ -174,7 +175,8 @@ __device__ __forceinline__ void unpack8(const uint4 &r, float *f) {
 // All NTHREADS threads enter; returns are CTA-uniform.
 __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, int h, int b) {
   const int n = p.lens ? p.lens[b] : p.n_single;
-  if (n < 1 || n > p.cap || n > p.max_n) {  // bad device-side length: record, write nothing
+  const int cap = p.caps ? p.caps[b] : p.cap;  // rows per head of this sequence's cache
+  if (n < 1 || n > cap || n > p.max_n) {  // bad device-side length: record, write nothing
     if (threadIdx.x == 0 && split == 0) atomicExch(&g_device_status, RIB_EINVAL);
     return;
   }
@@ -188,8 +190,8 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
     if (threadIdx.x == 0 && split == 0) atomicExch(&g_device_status, RIB_EALIGN);
     return;
   }
-  const uint16_t *Kh = cache + static_cast<size_t>(h) * p.cap * D;
-  const uint16_t *Vh = cache + static_cast<size_t>(p.nkv + h) * p.cap * D;
+  const uint16_t *Kh = cache + static_cast<size_t>(h) * cap * D;
+  const uint16_t *Vh = cache + static_cast<size_t>(p.nkv + h) * cap * D;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;

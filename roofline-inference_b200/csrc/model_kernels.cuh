@@ -341,5 +341,31 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
   }
 }
 
+// Greedy token of each row of x [rows][n] (the first index on ties): one CTA
+// per row, the same keys as argmax_kernel.
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float *__restrict__ x, int n,
+                                                          int32_t *__restrict__ out) {
+  __shared__ unsigned long long red[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const float *row = x + static_cast<size_t>(blockIdx.x) * n;
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long k = argmax_key(row[i], i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    out[blockIdx.x] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(best & 0xffffffffull));
+  }
+}
+
 }  // namespace model
 }  // namespace rib

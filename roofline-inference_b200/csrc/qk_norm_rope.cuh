@@ -158,3 +158,53 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
 
 }  // namespace rope
 }  // namespace rib
+
+namespace rib {
+namespace rope {
+
+// One new token for each of B sequences, each at its own position in its own
+// cache: the batched form of the decode append (one CTA per sequence).
+struct BatchParams {
+  const uint16_t *qkv;          // [B][items*128]
+  const uint16_t *qw, *kw;      // [128]
+  uint16_t *q_out;              // [B][nq][128]
+  const uint64_t *cache_ptrs;   // [B] caches [2][nkv][caps[b]][128]
+  const int32_t *caps;          // [B]
+  const int32_t *pos;           // [B] positions (the row written)
+  int nq, nkv;
+  double inv_freq[64];
+};
+
+__global__ void __launch_bounds__(1024) qk_norm_rope_batched_kernel(const __grid_constant__ BatchParams p) {
+  __shared__ float cos_t[64], sin_t[64];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int pos = p.pos[b], cap = p.caps[b];
+  if (pos < 0 || pos >= cap) {
+    if (tid == 0) atomicExch(&g_device_status, RIB_ECAPACITY);
+    return;
+  }
+  rope_angles(pos, p.inv_freq, cos_t, sin_t, tid);
+  __syncthreads();
+  const int items = p.nq + 2 * p.nkv;
+  const int lane = tid & 31;
+  const int item = (tid >> 5) * 2 + (lane >> 4);
+  const int j = lane & 15;
+  if (item >= items) return;
+  const unsigned half_mask = 0xffffu << (lane & 16);
+  const uint4 raw = *reinterpret_cast<const uint4 *>(p.qkv + (static_cast<size_t>(b) * items + item) * D + 8 * j);
+  uint16_t *cache = reinterpret_cast<uint16_t *>(p.cache_ptrs[b]);
+  if (item >= p.nq + p.nkv) {  // V: bit-exact copy
+    const int hv = item - p.nq - p.nkv;
+    *reinterpret_cast<uint4 *>(cache + (static_cast<size_t>(p.nkv + hv) * cap + pos) * D + 8 * j) = raw;
+    return;
+  }
+  const uint4 out = norm_rope8(raw, item < p.nq ? p.qw : p.kw, j, half_mask, cos_t, sin_t);
+  uint16_t *dst = item < p.nq ? p.q_out + (static_cast<size_t>(b) * p.nq + item) * D + 8 * j
+                              : cache + (static_cast<size_t>(item - p.nq) * cap + pos) * D + 8 * j;
+  *reinterpret_cast<uint4 *>(dst) = out;
+}
+
+}  // namespace rope
+}  // namespace rib

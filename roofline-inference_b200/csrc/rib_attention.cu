@@ -826,4 +826,61 @@ int rib_qwen3_decode_step(const rib_qwen3_model *m, const uint64_t *cache_ptrs, 
   return step_launch<0, 0, 0, 0, 0, 0, 0>(p, 1, st);
 }
 
+
+// ------------------------------------------------------------------ batched ragged decode
+int rib_decode_attention_ragged(const void *q, const uint64_t *cache_ptrs, const int32_t *caps,
+                                const int32_t *lens, int batch, int max_n, int nq, int nkv, float scale,
+                                void *out, void *workspace, size_t workspace_bytes, void *stream) {
+  if (!q || !cache_ptrs || !caps || !lens || !out) return RIB_EINVAL;
+  if (batch < 1 || nkv < 1 || nq != 2 * nkv || max_n < 1 || !(scale > 0.f)) return RIB_EINVAL;
+  if (!aligned16(q) || !aligned16(out) || (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) ||
+      (reinterpret_cast<uintptr_t>(caps) & 3u) || (reinterpret_cast<uintptr_t>(lens) & 3u))
+    return RIB_EALIGN;
+  rib::decode::Params p = {};
+  p.q = static_cast<const uint16_t *>(q);
+  p.cache_ptrs = cache_ptrs;
+  p.caps = caps;
+  p.lens = lens;
+  p.cap = max_n;  // per-sequence capacities come from caps[]
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t *>(out);
+  return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
+}
+
+int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw, const void *kw, const int32_t *pos,
+                                    const uint64_t *cache_ptrs, const int32_t *caps, int batch, int nq,
+                                    int nkv, double base, void *q_out, void *stream) {
+  if (!qkv || !qw || !kw || !pos || !cache_ptrs || !caps || !q_out) return RIB_EINVAL;
+  if (batch < 1 || nq < 1 || nkv < 1 || nq + 2 * nkv > rib::rope::kMaxItems || !(base > 0.0)) return RIB_EINVAL;
+  if (!aligned16(qkv) || !aligned16(qw) || !aligned16(kw) || !aligned16(q_out) ||
+      (reinterpret_cast<uintptr_t>(pos) & 3u) || (reinterpret_cast<uintptr_t>(caps) & 3u) ||
+      (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  rib::rope::BatchParams p;
+  p.qkv = static_cast<const uint16_t *>(qkv);
+  p.qw = static_cast<const uint16_t *>(qw);
+  p.kw = static_cast<const uint16_t *>(kw);
+  p.q_out = static_cast<uint16_t *>(q_out);
+  p.cache_ptrs = cache_ptrs;
+  p.caps = caps;
+  p.pos = pos;
+  p.nq = nq;
+  p.nkv = nkv;
+  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
+  const int threads = ((nq + 2 * nkv + 1) / 2) * 32;
+  return launch_pdl("qk_norm_rope_batched_kernel launch", rib::rope::qk_norm_rope_batched_kernel, dim3(batch),
+                    dim3(threads), 0, static_cast<cudaStream_t>(stream), p);
+}
+
+int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out, void *stream) {
+  if (!x || !out || rows < 1 || n < 1) return RIB_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  return launch_pdl("argmax_rows_kernel launch", rib::model::argmax_rows_kernel, dim3(rows), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), x, n, out);
+}
+
 }  // extern "C"

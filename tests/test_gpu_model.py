@@ -278,3 +278,51 @@ def test_persistent_step_qwen3_widths(rib):
     a = list(eng.generate(prompt, max_tokens=10, mode="persistent"))
     b = list(eng.generate(prompt, max_tokens=10, mode="graph"))
     assert a == b and len(a) == 10
+
+
+# ------------------------------------------------------------------ batched ragged decode
+def test_batched_ragged_decode_matches_single(rib):
+    """Sequences of different lengths in their own caches decode together:
+    each row's logits match the single-sequence decode of the same token
+    (teacher-forced for 3 steps), and generate_batch gives each prompt the
+    tokens of its own generate() wherever the logit margin is clear."""
+    from importlib import import_module
+    batch = import_module("roofline-inference_b200.batch")
+    cfg = rib.Qwen3Config(num_layers=2, hidden_size=256, num_heads=4, num_kv_heads=2,
+                          intermediate_size=512, vocab_size=1000)
+    eng = rib.Engine(rib.random_weights(cfg, seed=41).to(DEV))
+    rng = np.random.default_rng(41)
+    prompts = [list(rng.integers(0, cfg.vocab_size, n)) for n in (5, 70, 33, 129)]
+    cb, cs = [], []
+    for p in prompts:
+        for lst in (cb, cs):
+            c = eng.new_cache(len(p) + 8)
+            eng.prefill(torch.tensor(p, dtype=torch.int32, device=DEV), c, last=False)
+            lst.append(c)
+    dec = batch.BatchDecoder(eng, cb)
+    toks = torch.tensor([3, 7, 11, 13], dtype=torch.int32, device=DEV)
+    for step in range(3):
+        lb = dec.logits(toks)
+        for i, c in enumerate(cs):
+            ls = eng.decode(toks[i:i + 1], c, return_logits=True)
+            rel = float((lb[i] - ls).abs().max() / ls.abs().max())
+            assert rel <= 1e-2, (step, i, rel)
+        toks = toks + 1
+    assert [c.offset for c in cb] == [c.offset for c in cs] == [len(p) + 3 for p in prompts]
+    assert rib._lib.take_device_status() == 0
+    out = batch.generate_batch(eng, prompts, max_tokens=6)
+    assert [len(o) for o in out] == [6] * 4
+    for p, o in zip(prompts, out):
+        assert o[0] == next(iter(eng.generate(p, max_tokens=1, use_graph=False)))
+
+
+def test_argmax_rows(rib):
+    x = torch.randn(5, 151936, device=DEV)
+    x[3, 10] = 100.0
+    x[3, 20] = 100.0
+    L = rib.load_library()
+    out = torch.empty(5, dtype=torch.int32, device=DEV)
+    assert L.rib_argmax_rows_f32(x.data_ptr(), 5, x.shape[1], out.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream) == 0
+    want = torch.argmax(x, dim=1).to(torch.int32)
+    assert torch.equal(out, want) and int(out[3]) == 10

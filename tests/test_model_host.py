@@ -138,3 +138,18 @@ def test_oracle_decode_continues_prefill(rib, mnp):
     assert a.offset == b.offset == 19
     np.testing.assert_allclose(la, lb, atol=2e-2 * np.abs(lb).max())
     assert np.abs(la - lb).mean() < 2e-3 * np.abs(lb).max()
+
+
+def test_batched_entry_points_reject_bad_arguments(rib):
+    L = rib.load_library()
+    # GQA factor, misaligned caps, null pointers, empty batch
+    assert L.rib_decode_attention_ragged(FAKE, FAKE, FAKE, FAKE, 2, 100, 15, 8, 0.09, FAKE, FAKE, 1 << 20,
+                                         None) == 1
+    assert L.rib_decode_attention_ragged(FAKE, FAKE, 0x10002, FAKE, 2, 100, 16, 8, 0.09, FAKE, FAKE, 1 << 20,
+                                         None) == 3
+    assert L.rib_qk_norm_rope_append_batched(FAKE, FAKE, FAKE, None, FAKE, FAKE, 2, 16, 8, 1e6, FAKE,
+                                             None) == 1
+    assert L.rib_qk_norm_rope_append_batched(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, 16, 8, 1e6, FAKE,
+                                             None) == 1
+    assert L.rib_argmax_rows_f32(FAKE, 0, 10, FAKE, None) == 1
+    assert L.rib_argmax_rows_f32(0x10002, 2, 10, FAKE, None) == 3
