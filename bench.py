@@ -856,8 +856,56 @@ def run_full_model(rib, rank, world, device, args):
         "total_ms": t_tot * 1e3,
         "reference_line": {"ttft_ms": rline["ttft_s"] * 1e3, "total_ms": rline["total_s"] * 1e3},
         "fraction_ttft": rline["ttft_s"] / t_ttft, "fraction_total": rline["total_s"] / t_tot}
+    if world == 1:
+        out["batched_decode"] = run_model_batch(rib, eng, device, args)
     eng.close()  # collective when sharded
     return out
+
+
+def run_model_batch(rib, eng, device, args):
+    """Batched ragged decode of the whole model on one GPU: 64 independent
+    sequences with contexts drawn U[512, 4096] (seeded), each in its own cache
+    (K/V copied from a seeded N(0, 1) block), one token each per step through
+    BatchDecoder (GEMM projections over the 64 rows, batched append, ragged
+    split-KV attention, row argmax).  Tokens/s and the step against the
+    batched Level-A line (weights read once per step, every sequence's K/V)."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    rl = importlib.import_module("roofline-inference_b200.roofline_line")
+    batch_mod = importlib.import_module("roofline-inference_b200.batch")
+    cfg = eng.cfg
+    ctxs = wl.ragged_lengths(64, 512, 4096, seed=0)
+    steps, warm = max(1, min(args.steps, 20)), 3
+    src = wl.randn_bf16((2, cfg.num_kv_heads, max(ctxs), 128), seed=14, device=device)
+    caches = []
+    for c in ctxs:
+        cache = eng.new_cache(c + steps + warm + 2)
+        cache.storage[:, :, :, :c].copy_(src[None, :, :, :c].expand(cfg.num_layers, -1, -1, -1, -1))
+        cache.offset = c
+        caches.append(cache)
+    dec = batch_mod.BatchDecoder(eng, caches)
+    tok = torch.arange(64, dtype=torch.int32, device=device)
+    for _ in range(warm):
+        tok = dec.step(tok)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        tok = dec.step(tok)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    line = rl.model_batch_decode_line(cfg, [c + warm for c in ctxs])
+    res = {"sequences": 64, "contexts": "U[512, 4096], seed 0", "steps": steps, "ms_per_step": ms,
+           "tokens_per_s": 64 * 1000.0 / ms, "kv_bytes_per_step": sum(ctxs) * cfg.num_layers * 4096,
+           "reference_line_ms": line["time_s"] * 1e3, "reference_bottleneck": line["bottleneck"],
+           "fraction_of_line": line["time_s"] * 1e3 / ms,
+           "path": "BatchDecoder.step: cuBLAS GEMMs for the projections, rib_qk_norm_rope_append_batched, "
+                   "rib_decode_attention_ragged, add_rms/SwiGLU kernels, FP32-output LM-head GEMM, "
+                   "rib_argmax_rows_f32"}
+    del dec, caches, src
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_case(case: str):

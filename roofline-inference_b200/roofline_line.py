@@ -130,3 +130,14 @@ def request_line(cfg, prompt_len: int, gen: int, spec: dict | None = None) -> di
     return {"ttft_s": ttft, "decode_s": sum(steps), "total_s": ttft + sum(steps),
             "decode_first_s": steps[0] if steps else 0.0, "decode_last_s": steps[-1] if steps else 0.0,
             "prompt_len": prompt_len, "gen": gen, "device": spec["name"]}
+
+
+def model_batch_decode_line(cfg, contexts: list[int], spec: dict | None = None) -> dict:
+    """One decode step of len(contexts) independent sequences: every weight is
+    read once for the whole batch (workload.py:decode with batch > 1 reads
+    _weights_read_bytes once), each sequence reads its own cached K/V."""
+    spec = spec or load_spec()
+    lines = [model_decode_line(cfg, c, spec=spec) for c in contexts]
+    w = _params(cfg)["weights_read"]
+    dram = w + sum(l["dram_bytes"] - w for l in lines)
+    return _line(sum(l["flops"] for l in lines), dram, sum(l["exps"] for l in lines), spec)

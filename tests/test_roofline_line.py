@@ -100,3 +100,17 @@ def test_request_line_closed_form(rl):
     d = rl.model_decode_line(cfg, 32768)
     assert d["bottleneck"] == "dram_bandwidth"
     assert 4.9e9 < d["dram_bytes"] < 5.0e9          # 1.19 GB weights + 3.76 GB K/V
+
+
+def test_batch_decode_line_matches_reference(rl, reference_roofline):
+    """Equal contexts: the batched line is the reference's decode(model, B, ctx)."""
+    import importlib as _il
+    cfg = _il.import_module("roofline-inference_b200").QWEN3_0_6B
+    model = reference_roofline.load_model(REF_MODEL)
+    dev = reference_roofline.load_device(rl.SPEC)
+    w = reference_roofline.decode(model, 8, 4096)
+    b = reference_roofline.physical_bound(w, dev, initial_resident_bytes=0)
+    line = rl.model_batch_decode_line(cfg, [4096] * 8)
+    assert line["flops"] == w.total_flops
+    assert line["dram_bytes"] == pytest.approx(b.traffic["total"])
+    assert line["time_s"] == pytest.approx(b.time_s)
