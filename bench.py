@@ -858,6 +858,7 @@ def run_full_model(rib, rank, world, device, args):
         "fraction_ttft": rline["ttft_s"] / t_ttft, "fraction_total": rline["total_s"] / t_tot}
     if world == 1:
         out["batched_decode"] = run_model_batch(rib, eng, device, args)
+        out["serving"] = run_serving(rib, eng, device)
     eng.close()  # collective when sharded
     return out
 
@@ -869,20 +870,10 @@ def run_model_batch(rib, eng, device, args):
     BatchDecoder (GEMM projections over the 64 rows, batched append, ragged
     split-KV attention, row argmax).  Tokens/s and the step against the
     batched Level-A line (weights read once per step, every sequence's K/V)."""
-    wl = importlib.import_module("roofline-inference_b200.workloads")
     rl = importlib.import_module("roofline-inference_b200.roofline_line")
-    batch_mod = importlib.import_module("roofline-inference_b200.batch")
     cfg = eng.cfg
-    ctxs = wl.ragged_lengths(64, 512, 4096, seed=0)
     steps, warm = max(1, min(args.steps, 20)), 3
-    src = wl.randn_bf16((2, cfg.num_kv_heads, max(ctxs), 128), seed=14, device=device)
-    caches = []
-    for c in ctxs:
-        cache = eng.new_cache(c + steps + warm + 2)
-        cache.storage[:, :, :, :c].copy_(src[None, :, :, :c].expand(cfg.num_layers, -1, -1, -1, -1))
-        cache.offset = c
-        caches.append(cache)
-    dec = batch_mod.BatchDecoder(eng, caches)
+    ctxs, dec = batch_workload(eng, device, steps + warm + 2)
     tok = torch.arange(64, dtype=torch.int32, device=device)
     for _ in range(warm):
         tok = dec.step(tok)
@@ -900,12 +891,62 @@ def run_model_batch(rib, eng, device, args):
            "tokens_per_s": 64 * 1000.0 / ms, "kv_bytes_per_step": sum(ctxs) * cfg.num_layers * 4096,
            "reference_line_ms": line["time_s"] * 1e3, "reference_bottleneck": line["bottleneck"],
            "fraction_of_line": line["time_s"] * 1e3 / ms,
-           "path": "BatchDecoder.step: cuBLAS GEMMs for the projections, rib_qk_norm_rope_append_batched, "
+           "launches_per_step": dec.launches_per_step,
+           "path": "BatchDecoder.step replayed from one CUDA graph: cuBLAS GEMMs for the projections, rib_qk_norm_rope_append_batched, "
                    "rib_decode_attention_ragged, add_rms/SwiGLU kernels, FP32-output LM-head GEMM, "
                    "rib_argmax_rows_f32"}
-    del dec, caches, src
+    del dec
     torch.cuda.empty_cache()
     return res
+
+
+def run_serving(rib, eng, device):
+    """Continuous batching: 128 requests (prompts U[128, 2048] tokens, outputs
+    U[32, 256] tokens, seeded), all submitted at once, served by the
+    Scheduler with 64 decode slots, 4096-token prefill chunks and a KV arena
+    for 64 requests of the largest size.  Host wall clock around run()."""
+    g = torch.Generator().manual_seed(21)
+    n = 128
+    plens = torch.randint(128, 2049, (n,), generator=g).tolist()
+    outs = torch.randint(32, 257, (n,), generator=g).tolist()
+    prompts = [torch.randint(0, eng.cfg.vocab_size, (k,), generator=g).tolist() for k in plens]
+    s = rib.Scheduler(eng, pool_rows=64 * 2560, slots=64, max_len=2560, chunk=4096)
+    for p, m in zip(prompts, outs):
+        s.submit(p, m)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    res = s.run()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    gen = sum(len(v) for v in res.values())
+    out = {"requests": n, "prompt_tokens": sum(plens), "generated_tokens": gen, "wall_s": wall,
+           "output_tokens_per_s": gen / wall, "total_tokens_per_s": (gen + sum(plens)) / wall,
+           "scheduler_steps": s.steps, "decode_steps": s.decode_steps,
+           "mean_active_slots": (gen - n) / max(1, s.decode_steps),
+           "config": "prompts U[128, 2048], outputs U[32, 256], seed 21; 64 slots, chunk 4096, "
+                     "arena 64 x 2560 rows",
+           "timing": "host wall clock around Scheduler.run (graph capture included)"}
+    del s
+    torch.cuda.empty_cache()
+    return out
+
+
+def batch_workload(eng, device, extra: int):
+    """64 sequences with contexts U[512, 4096] (seed 0), each in its own cache
+    with room for `extra` more tokens, K/V copied from a seeded N(0, 1) block;
+    returns the contexts and a captured BatchDecoder over the caches."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    batch_mod = importlib.import_module("roofline-inference_b200.batch")
+    cfg = eng.cfg
+    ctxs = wl.ragged_lengths(64, 512, 4096, seed=0)
+    src = wl.randn_bf16((2, cfg.num_kv_heads, max(ctxs), 128), seed=14, device=device)
+    caches = []
+    for c in ctxs:
+        cache = eng.new_cache(c + extra)
+        cache.storage[:, :, :, :c].copy_(src[None, :, :, :c].expand(cfg.num_layers, -1, -1, -1, -1))
+        cache.offset = c
+        caches.append(cache)
+    return ctxs, batch_mod.BatchDecoder(eng, caches).capture()
 
 
 def run_case(case: str):
@@ -914,7 +955,9 @@ def run_case(case: str):
     prefill-small is causal prefill at L = 16384 (128 MB of Q/K/V, above L2;
     3 launches); model-decode is the Qwen3-0.6B decode step at context 4096
     (1.19 GB of weights and 0.47 GB of K/V, above L2): the graph's eager
-    warm-up step and 3 replays of 143 launches each."""
+    warm-up step and 3 replays of 143 launches each; model-batch is the
+    64-sequence ragged batched decode step (contexts U[512, 4096], 17.9 GB
+    of K/V): the capture's eager warm-up step and 3 graph replays."""
     rib = load_rib()
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
@@ -937,6 +980,12 @@ def run_case(case: str):
         dg.set_state(1, ctx)
         for _ in range(3):
             dg.replay()
+    elif case == "model-batch":
+        eng = rib.Engine(rib.random_weights(rib.QWEN3_0_6B, seed=11, device=device))
+        _, dec = batch_workload(eng, device, 8)
+        tok = torch.arange(64, dtype=torch.int32, device=device)
+        for _ in range(3):
+            tok = dec.step(tok)
     else:
         L = 16384
         Q = wl.randn_bf16((16, L, 128), seed=71, device=device)
@@ -957,7 +1006,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "prefill-small", "model-decode"], default=None,
+    ap.add_argument("--case", choices=["decode-small", "prefill-small", "model-decode", "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()
     if args.case:

@@ -16,16 +16,23 @@ from .cache import Cache
 from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope, qk_norm_rope_append,
                       qk_norm_rope_append_at, qk_norm_rope_prefill, rms_norm, swiglu)
 from .model import QWEN3_0_6B, DecodeGraph, Engine, Qwen3Config, Qwen3Weights, random_weights
-from .batch import BatchDecoder, generate_batch
+from .batch import BatchDecoder, SlotDecoder, generate_batch
+from .pool import KVPool, PoolFull
+from .scheduler import Request, Scheduler
 
 __all__ = [
     "BatchDecoder",
     "Cache",
     "DecodeGraph",
     "Engine",
+    "KVPool",
+    "PoolFull",
     "QWEN3_0_6B",
     "Qwen3Config",
     "Qwen3Weights",
+    "Request",
+    "Scheduler",
+    "SlotDecoder",
     "add_rms",
     "argmax",
     "embedding",

@@ -30,6 +30,21 @@ class Cache:
         self.n_kv = n_kv
         self.head_dim = head_dim
 
+    @classmethod
+    def over(cls, storage: torch.Tensor) -> "Cache":
+        """A cache over existing storage [n_layers, 2, n_kv, cap, head_dim]
+        (e.g. rows of a KVPool arena); cap must be a multiple of 256."""
+        if storage.dim() != 5 or storage.shape[1] != 2 or storage.shape[3] % 256 or not storage.is_contiguous():
+            raise ValueError("storage must be contiguous [n_layers, 2, n_kv, cap % 256 == 0, head_dim]")
+        c = cls.__new__(cls)
+        c.storage = storage
+        c.kv = [storage[i] for i in range(storage.shape[0])]
+        c.offset = 0
+        c.capacity = int(storage.shape[3])
+        c.n_kv = int(storage.shape[2])
+        c.head_dim = int(storage.shape[4])
+        return c
+
     def update(self, i: int, kv: torch.Tensor) -> torch.Tensor:
         """Write kv [2, n_kv, n, d] at [offset, offset+n) (engine.py:42-48)."""
         a, b = self.offset, self.offset + kv.shape[2]

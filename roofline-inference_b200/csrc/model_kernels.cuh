@@ -342,16 +342,46 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 }
 
 // Greedy token of each row of x [rows][n] (the first index on ties): one CTA
-// per row, the same keys as argmax_kernel.
-__global__ void __launch_bounds__(256) argmax_rows_kernel(const float *__restrict__ x, int n,
-                                                          int32_t *__restrict__ out) {
-  __shared__ unsigned long long red[8];
+// of 1024 threads per row, the same keys as argmax_kernel.  The row body is
+// read as 16-byte vectors, four per thread in flight (64 KB per CTA), with a
+// scalar head up to the first 16-byte boundary and a scalar tail.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float *__restrict__ x, int n,
+                                                           int32_t *__restrict__ out) {
+  __shared__ unsigned long long red[32];
   pdl_launch_dependents();
   pdl_wait();
   const float *row = x + static_cast<size_t>(blockIdx.x) * n;
+  const int t = threadIdx.x, nt = blockDim.x;
   unsigned long long best = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const unsigned long long k = argmax_key(row[i], i);
+  const int mis = static_cast<int>((reinterpret_cast<uintptr_t>(row) >> 2) & 3u);
+  const int head = min(n, (4 - mis) & 3);
+  if (t < head) best = argmax_key(__ldcs(row + t), t);
+  const int nv = (n - head) >> 2;
+  const float4 *v = reinterpret_cast<const float4 *>(row + head);
+  for (int j = t; j < nv; j += 4 * nt) {
+    float4 a[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (j + u * nt < nv) a[u] = __ldcs(v + j + u * nt);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int jj = j + u * nt;
+      if (jj < nv) {
+        const int i = head + 4 * jj;
+        unsigned long long k = argmax_key(a[u].x, i);
+        best = k > best ? k : best;
+        k = argmax_key(a[u].y, i + 1);
+        best = k > best ? k : best;
+        k = argmax_key(a[u].z, i + 2);
+        best = k > best ? k : best;
+        k = argmax_key(a[u].w, i + 3);
+        best = k > best ? k : best;
+      }
+    }
+  }
+  const int tail0 = head + 4 * nv;
+  if (tail0 + t < n) {
+    const unsigned long long k = argmax_key(__ldcs(row + tail0 + t), tail0 + t);
     best = k > best ? k : best;
   }
 #pragma unroll
@@ -359,10 +389,10 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float *__restric
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
     best = other > best ? other : best;
   }
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  if ((t & 31) == 0) red[t >> 5] = best;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+  if (t == 0) {
+    for (int w = 1; w < (nt >> 5); ++w) best = red[w] > best ? red[w] : best;
     out[blockIdx.x] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(best & 0xffffffffull));
   }
 }

@@ -879,7 +879,7 @@ int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out, void *str
   if (!x || !out || rows < 1 || n < 1) return RIB_EINVAL;
   if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u)) return RIB_EALIGN;
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
-  return launch_pdl("argmax_rows_kernel launch", rib::model::argmax_rows_kernel, dim3(rows), dim3(256), 0,
+  return launch_pdl("argmax_rows_kernel launch", rib::model::argmax_rows_kernel, dim3(rows), dim3(1024), 0,
                     static_cast<cudaStream_t>(stream), x, n, out);
 }
 

@@ -316,6 +316,39 @@ def test_batched_ragged_decode_matches_single(rib):
         assert o[0] == next(iter(eng.generate(p, max_tokens=1, use_graph=False)))
 
 
+def test_batched_decode_graph_matches_eager(rib):
+    """The CUDA-graph replay of the batched step gives the eager step's logits
+    and tokens, advances every cache, and leaves the device status clean."""
+    from importlib import import_module
+    batch = import_module("roofline-inference_b200.batch")
+    cfg = rib.Qwen3Config(num_layers=3, hidden_size=256, num_heads=4, num_kv_heads=2,
+                          intermediate_size=512, vocab_size=1000)
+    eng = rib.Engine(rib.random_weights(cfg, seed=43).to(DEV))
+    rng = np.random.default_rng(43)
+    prompts = [list(rng.integers(0, cfg.vocab_size, n)) for n in (9, 300, 41)]
+    ce, cg = [], []
+    for p in prompts:
+        for lst in (ce, cg):
+            c = eng.new_cache(len(p) + 6)
+            eng.prefill(torch.tensor(p, dtype=torch.int32, device=DEV), c, last=False)
+            lst.append(c)
+    de = batch.BatchDecoder(eng, ce)
+    dg = batch.BatchDecoder(eng, cg).capture()
+    assert [c.offset for c in cg] == [len(p) for p in prompts]     # capture does not advance
+    toks = torch.tensor([5, 6, 7], dtype=torch.int32, device=DEV)
+    for step in range(4):
+        le = de.logits(toks)
+        tg = dg.step(toks)
+        rel = float((le - dg.graph_logits).abs().max() / le.abs().max())
+        assert rel <= 1e-3, (step, rel)
+        agree = tg.cpu() == torch.argmax(le, dim=1).to(torch.int32).cpu()
+        top2 = torch.topk(le, 2, dim=1).values
+        assert bool(torch.all(agree | ((top2[:, 0] - top2[:, 1]) < 1e-2).cpu())), step
+        toks = (toks * 3 + 1) % cfg.vocab_size
+    assert [c.offset for c in cg] == [c.offset for c in ce] == [len(p) + 4 for p in prompts]
+    assert rib._lib.take_device_status() == 0
+
+
 def test_argmax_rows(rib):
     x = torch.randn(5, 151936, device=DEV)
     x[3, 10] = 100.0
@@ -326,3 +359,55 @@ def test_argmax_rows(rib):
                                  torch.cuda.current_stream().cuda_stream) == 0
     want = torch.argmax(x, dim=1).to(torch.int32)
     assert torch.equal(out, want) and int(out[3]) == 10
+
+
+@pytest.mark.parametrize("rows,n", [(3, 1001), (7, 5), (2, 1), (4, 4099)])
+def test_argmax_rows_ragged_alignment(rib, rows, n):
+    """Rows whose starts fall off the 16-byte grid (n not a multiple of 4):
+    the scalar head, vector body and scalar tail cover every element, and a
+    tie inside the head keeps the first index."""
+    g = torch.Generator(device=DEV).manual_seed(n)
+    x = torch.randn(rows, n, device=DEV, generator=g)
+    if n > 3:
+        x[rows - 1, 1] = 50.0
+        x[rows - 1, n - 1] = 50.0           # tie with a tail element: the first index wins
+        x[0, n - 1] = 60.0                  # maximum in the tail
+    L = rib.load_library()
+    out = torch.empty(rows, dtype=torch.int32, device=DEV)
+    assert L.rib_argmax_rows_f32(x.data_ptr(), rows, n, out.data_ptr(),
+                                 torch.cuda.current_stream().cuda_stream) == 0
+    assert torch.equal(out, torch.argmax(x, dim=1).to(torch.int32))
+
+
+# ------------------------------------------------------------------ continuous batching
+def test_scheduler_greedy_consistent(rib):
+    """Requests served by the continuous-batching scheduler (fewer slots than
+    requests, a pool that holds only some of them at once, chunked prefill,
+    the step replayed from a CUDA graph while members join and leave) each get
+    a greedy continuation: every token is the argmax, up to a near-tie margin,
+    of the single-sequence engine's logits at its position given the same
+    prefix, and the count and stopping rule are those of generate()."""
+    from importlib import import_module
+    sched = import_module("roofline-inference_b200.scheduler")
+    cfg = rib.Qwen3Config(num_layers=2, hidden_size=256, num_heads=4, num_kv_heads=2,
+                          intermediate_size=512, vocab_size=1000)
+    eng = rib.Engine(rib.random_weights(cfg, seed=47).to(DEV))
+    rng = np.random.default_rng(47)
+    lens, mts = (5, 300, 40, 129, 700, 17), (6, 4, 9, 1, 5, 12)
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab_size, n)] for n in lens]
+    s = sched.Scheduler(eng, pool_rows=4 * 256 + 1024, slots=2, max_len=1024, chunk=256)
+    ids = [s.submit(p, m) for p, m in zip(prompts, mts)]
+    out = s.run()
+    assert s.decode_steps > 0 and s.dec.graph is not None
+    assert s.pool.free_pages == s.pool.pages
+    for rid, p, m in zip(ids, prompts, mts):
+        o = out[rid]
+        assert len(o) == m, (rid, o)
+        full = p + o[:-1]
+        c = eng.new_cache(len(full) + 1)
+        lg = eng.prefill(torch.tensor(full, dtype=torch.int32, device=DEV), c, last=True, all_logits=True)[0]
+        for j, t in enumerate(o):
+            row = lg[len(p) - 1 + j]
+            margin = float(row.max() - row[t])
+            assert margin <= 1e-2 * float(row.abs().max()), (rid, j, margin)
+    assert rib._lib.take_device_status() == 0
