@@ -417,6 +417,8 @@ def run_ours(args):
 
     # ---- the full Qwen3-0.6B forward (one replica per GPU)
     full_model = run_full_model(rib, rank, world, device, args) if not args.no_model else None
+    if full_model is not None and world > 1:   # the same sequence with the projections split too
+        full_model["tensor_parallel"] = run_full_model(rib, rank, world, device, args, tp=True)
 
     device_status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
     if gather is not None:
@@ -756,7 +758,7 @@ def run_ctx512_latency(rib, device, args):
                     "from a CUDA graph of 28 layers, host time from eager calls with a synchronise"}
 
 
-def run_full_model(rib, rank, world, device, args):
+def run_full_model(rib, rank, world, device, args, tp: bool = False):
     """Qwen3-0.6B forward with random N(0, 0.02) weights (28 layers, hidden
     1024, 16/8 heads, FFN 3072, vocab 151936, tied embeddings, BF16): the
     engine's CUDA-graph decode step at context 32768 (K/V seeded N(0, 1)), and
@@ -765,13 +767,16 @@ def run_full_model(rib, rank, world, device, args):
     KV-head sharded over all ranks (Engine(shard=True): each rank owns 8/N KV
     heads, the decode kernel gathers every head's output over NVLink, the
     rest of the layer runs on every rank); times are the max over ranks.
+    With tp the projections are split too (Engine(tp=True): O / down partial
+    sums and the argmax keys exchanged over NVLink inside the GEMV kernels).
     Each figure is reported against the full-model Level-A line (cold start)."""
     rl = importlib.import_module("roofline-inference_b200.roofline_line")
     cfg = rib.QWEN3_0_6B
     # the same seed on every rank: identical weights, as a sharded engine needs
-    eng = rib.Engine(rib.random_weights(cfg, seed=11, device=device), shard=world > 1)
+    eng = rib.Engine(rib.random_weights(cfg, seed=11, device=device), shard=world > 1, tp=tp and world > 1)
     out = {"model": "Qwen3-0.6B, random-init N(0, 0.02) weights, BF16",
-           "parallelism": f"kv-head shard x{world}" if world > 1 else "1 GPU",
+           "parallelism": (f"tensor parallel x{world}" if tp else f"kv-head shard x{world}") if world > 1
+           else "1 GPU",
            "kv_heads_per_rank": eng.n_kv}
 
     # decode step at context 32768
@@ -856,7 +861,7 @@ def run_full_model(rib, rank, world, device, args):
         "total_ms": t_tot * 1e3,
         "reference_line": {"ttft_ms": rline["ttft_s"] * 1e3, "total_ms": rline["total_s"] * 1e3},
         "fraction_ttft": rline["ttft_s"] / t_ttft, "fraction_total": rline["total_s"] / t_tot}
-    if world == 1:
+    if world == 1 and not tp:
         out["batched_decode"] = run_model_batch(rib, eng, device, args)
         out["serving"] = run_serving(rib, eng, device)
     eng.close()  # collective when sharded

@@ -279,7 +279,7 @@ int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw,
 /* Batch-1 GEMV with fused input RMSNorm and epilogue.  Replaces
  * gemv(W, x, nw=, res=, swiglu=, out_float=) (agent-test/v2/kernels.py
  * :103-113, Metal source :19-97).
- *   W    [N, K] BF16 row-major, K a multiple of 256, K <= 8192
+ *   W    [N, K] BF16 row-major, K a multiple of 8, K <= 8192
  *   x    [K] BF16
  *   nw   [K] RMSNorm weight or NULL; with it the kernel uses
  *        bf16(nw * bf16(x / sqrt(mean(x^2) + 1e-6))) in place of x
@@ -405,6 +405,58 @@ int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw,
 /* Greedy token of each row of x [rows, n] FP32 (the first index on ties). */
 int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out,
                         void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * Tensor parallelism of the decode projections over the GPUs of one node
+ * (no counterpart in the single-GPU reference; it splits the GEMVs of
+ * Engine.decode, agent-test/v2/engine.py:150-162, over ranks).
+ *
+ * Rank r holds its KV heads' rows of the QKV projection, the matching
+ * columns of the O projection, a slice of the gate and up rows, the matching
+ * columns of the down projection and a slice of the LM-head rows.  The O and
+ * down GEMVs then give FP32 partial sums of the full hidden vector, which
+ * every rank stores straight into every rank's exchange buffer over NVLink
+ * (RIB_EPI_PEER_PARTIAL) and flags with the exchange's epoch; the next GEMV
+ * waits (bounded) for all ranks' flags and reads its input as
+ * bf16(residual + bf16(sum of the partials in rank order)), the rounding of
+ * RIB_EPI_RESIDUAL, so every rank computes identical activations.
+ *
+ * Exchange buffer of one rank (rib_tp_buffer_bytes(world, slot) bytes,
+ * zeroed, shared through rib_peer_buffer_alloc / _open):
+ *   [2 regions][world][slot] FP32 partials, then (at a 256-byte boundary)
+ *   [world] u64 epoch flags.  Exchange number e uses region e & 1.
+ * epoch: device u64 counting this rank's exchanges (zero on every rank
+ * before the first); done: device u32 arrival counter (zero; every call
+ * leaves it zero).  All ranks make the same exchanges in the same order. */
+#define RIB_TP_MAX_RANKS 8
+#define RIB_EPI_PEER_PARTIAL 3 /* FP32 W x -> slot `rank` of every rank's buffer */
+
+typedef struct rib_tp_exchange {
+  int world, rank;
+  uint64_t buf[RIB_TP_MAX_RANKS]; /* per rank: its exchange buffer (peer mapping) */
+  uint64_t epoch;                  /* device address, u64                         */
+  uint64_t done;                   /* device address, u32                         */
+  int slot;                        /* floats per rank slot (>= every N exchanged) */
+} rib_tp_exchange;
+
+size_t rib_tp_buffer_bytes(int world, int slot);
+
+/* rib_gemv with the exchange (ex may be NULL when neither is used):
+ *   in_sum   x is the residual stream; the input is
+ *            bf16(x + bf16(sum of the last exchange's partials)), K <= slot,
+ *            and x_out [K] receives it (the next residual).
+ *   epi      RIB_EPI_NONE, RIB_EPI_SWIGLU or RIB_EPI_PEER_PARTIAL (N <= slot;
+ *            y unused).  out_f32 with RIB_EPI_NONE only. */
+int rib_gemv_tp(const void *W, int N, int K, const void *x, const void *nw,
+                int epi, int out_f32, void *y, const rib_tp_exchange *ex,
+                int in_sum, void *x_out, void *stream);
+
+/* Greedy token over the ranks' logit slices: x [n] FP32 holds logits
+ * [index_offset, index_offset + n) of the vocabulary; every rank gets the
+ * global argmax (the first index on ties) in out[0].  One exchange. */
+int rib_argmax_f32_tp(const float *x, int n, int index_offset, int32_t *out,
+                      void *workspace, const rib_tp_exchange *ex,
+                      void *stream);
 
 #ifdef __cplusplus
 }

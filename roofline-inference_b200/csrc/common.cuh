@@ -45,6 +45,17 @@ __device__ __forceinline__ void record_timeout() {
   atomicExch(&g_device_status, RIB_ETIMEOUT);
 }
 
+// System-scope release store / acquire load of a u64 flag (peer GPUs write
+// and poll flags in each other's memory over NVLink).
+__device__ __forceinline__ void st_release_sys(unsigned long long *addr, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *addr) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 // Programmatic dependent launch (kernels launched with the
 // programmatic-stream-serialization attribute): a kernel lets the next one in
 // its stream be scheduled as soon as every CTA has started, and waits for the

@@ -93,14 +93,6 @@ struct Params {
   uint16_t *gcopy;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *addr, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *addr) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
-  return v;
-}
 
 // Final outputs of one (sequence, KV head) unit: res[hh] is dim `tid` of
 // query head 2h + hh.  Without gather they go to `out`.  With gather every

@@ -27,9 +27,49 @@ constexpr float kEps = 1e-6f;
 constexpr int kGemvWarps = 8;
 constexpr int kMaxK = 8192;
 
-enum Epilogue { kNone = 0, kResidual = 1, kSwiGLU = 2 };
+enum Epilogue { kNone = 0, kResidual = 1, kSwiGLU = 2, kPeerPartial = 3 };
 
 __device__ __forceinline__ void record_status(int status) { atomicExch(&g_device_status, status); }
+
+// ------------------------------------------------------------------ tensor-parallel exchange
+// rib_tp_exchange on the device.  Rank q's buffer: [2 regions][world][slot]
+// FP32 partials, then [world] u64 epoch flags at byte offset flag_off.
+struct TpEx {
+  int world, rank, slot;
+  float *buf[RIB_TP_MAX_RANKS];
+  size_t flag_off;
+  unsigned long long *epoch;  // this rank's exchange counter
+  unsigned int *done;         // arrival counter of the producing kernel's warps
+};
+
+__device__ __forceinline__ unsigned long long *tp_flags(const TpEx &ex, int q) {
+  return reinterpret_cast<unsigned long long *>(reinterpret_cast<char *>(ex.buf[q]) + ex.flag_off);
+}
+
+// Slot of `rank`'s partials for exchange e, in rank q's buffer.
+__device__ __forceinline__ float *tp_slot(const TpEx &ex, int q, unsigned long long e, int rank) {
+  return ex.buf[q] + (static_cast<size_t>(e & 1ull) * ex.world + rank) * ex.slot;
+}
+
+// Every thread of the CTA returns once all ranks' flags in this rank's buffer
+// reached e (thread t < world polls rank t's flag), or after kWaitLimitNs
+// with RIB_ETIMEOUT recorded.
+__device__ __forceinline__ void tp_wait_all(const TpEx &ex, unsigned long long e) {
+  if (static_cast<int>(threadIdx.x) < ex.world) {
+    const unsigned long long *f = tp_flags(ex, ex.rank) + threadIdx.x;
+    if (ld_acquire_sys(f) < e) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) < e) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_timeout();
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+}
 
 // 16-byte streaming load that does not allocate in L1 (weights are read once).
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
@@ -80,6 +120,13 @@ struct GemvParams {
   const uint16_t *res;  // [rows_out] residual, epilogue kResidual
   void *y;              // [rows_out] BF16, or FP32 when out_f32
   int N, K, rows_out, epi, out_f32;
+  // Tensor parallelism: with in_sum, x is the residual stream and the input
+  // is bf16(x + bf16(sum of the last exchange's partials in rank order)),
+  // written to x_out by CTA 0; epi kPeerPartial stores the FP32 rows into
+  // every rank's exchange buffer and publishes the exchange.
+  int in_sum;
+  uint16_t *x_out;
+  TpEx ex;
 };
 
 // C = K / 256 chunks of 8 elements per lane (0: runtime count); R output rows
@@ -87,7 +134,9 @@ struct GemvParams {
 // The weight rows do not depend on the previous kernel, so with C known at
 // compile time they are loaded into registers before the dependent-launch
 // wait; x (and the residual) are read after it.
-template <int R, int C, bool SW>
+// TP: the tensor-parallel forms (in_sum input, kPeerPartial epilogue) are
+// compiled in; without it those fields are ignored.
+template <int R, int C, bool SW, bool TP>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ float xs[];  // [K]
   __shared__ float red[32];
@@ -114,11 +163,43 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   pdl_wait();
 
   // ---- x into shared memory (normalised when nw is given)
+  const float *part = nullptr;
+  if (TP && p.in_sum) {
+    const unsigned long long e = __ldcg(p.ex.epoch);  // the exchange the previous kernel published
+    tp_wait_all(p.ex, e);
+    part = tp_slot(p.ex, p.ex.rank, e, 0);
+  }
   float ss = 0.f;
   for (int i = tid * 8; i < K; i += blockDim.x * 8) {
     const uint4 v = *reinterpret_cast<const uint4 *>(p.x + i);
     float f[8] = {bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y),
                   bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w)};
+    if (TP && part) {
+      float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < p.ex.world; ++r) {
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(r) * p.ex.slot + i));
+        const float4 b =
+            __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(r) * p.ex.slot + i + 4));
+        sum[0] += a.x;
+        sum[1] += a.y;
+        sum[2] += a.z;
+        sum[3] += a.w;
+        sum[4] += b.x;
+        sum[5] += b.y;
+        sum[6] += b.z;
+        sum[7] += b.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = round_bf16(f[e] + round_bf16(sum[e]));
+      if (blockIdx.x == 0) {
+        uint4 o;
+        o.x = pack_bf16x2(f[0], f[1]);
+        o.y = pack_bf16x2(f[2], f[3]);
+        o.z = pack_bf16x2(f[4], f[5]);
+        o.w = pack_bf16x2(f[6], f[7]);
+        *reinterpret_cast<uint4 *>(p.x_out + i) = o;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       xs[i + e] = f[e];
@@ -161,10 +242,37 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
 #pragma unroll
       for (int r = 0; r < NR; ++r) acc[r] = dot8(w[r], xa, xb, acc[r]);
     }
+    const int col = (K / 256) * 256 + lane * 8;  // K % 256 != 0: a partial chunk of K % 256 columns
+    if (col < K) {
+      const float4 xa = *reinterpret_cast<const float4 *>(xs + col);
+      const float4 xb = *reinterpret_cast<const float4 *>(xs + col + 4);
+#pragma unroll
+      for (int r = 0; r < NR; ++r) acc[r] = dot8(ldg_stream(wrow[r] + col), xa, xb, acc[r]);
+    }
   }
 #pragma unroll
   for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
   if (lane != 0) return;
+  if (TP && !SW && p.epi == kPeerPartial) {
+    // Rows into slot `rank` of every rank's buffer; the last warp to finish
+    // (of ceil(rows_out / R)) publishes the exchange's epoch to every rank.
+    const unsigned long long e = __ldcg(p.ex.epoch) + 1;
+    for (int q = 0; q < p.ex.world; ++q) {
+      float *dst = tp_slot(p.ex, q, e, p.ex.rank);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (row0 + r < p.rows_out) dst[row0 + r] = acc[r];
+    }
+    __threadfence_system();
+    const unsigned int warps = static_cast<unsigned int>((p.rows_out + R - 1) / R);
+    if (atomicAdd(p.ex.done, 1u) == warps - 1) {
+      __threadfence_system();
+      for (int q = 0; q < p.ex.world; ++q) st_release_sys(tp_flags(p.ex, q) + p.ex.rank, e);
+      *p.ex.epoch = e;
+      atomicExch(p.ex.done, 0u);
+    }
+    return;
+  }
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int row = row0 + r;
@@ -339,6 +447,66 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
     const unsigned long long b = atomicAdd(&ws->best, 0ull);
     out[0] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(b & 0xffffffffull));
   }
+}
+
+// Greedy token over the ranks' logit slices (tensor-parallel LM head): x
+// holds logits [offset, offset + n); keys carry the global index.  The last
+// CTA publishes this rank's best key to every rank (one exchange), waits
+// (bounded) for every rank's key and writes the largest key's index.
+__global__ void __launch_bounds__(1024) argmax_tp_kernel(const float *__restrict__ x, int n, int offset,
+                                                         ArgmaxWs *ws, int32_t *__restrict__ out,
+                                                         const __grid_constant__ TpEx ex) {
+  __shared__ unsigned long long red[32];
+  __shared__ bool last;
+  pdl_launch_dependents();
+  pdl_wait();
+  unsigned long long best = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long k = argmax_key(x[i], i + offset);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    atomicMax(&ws->best, best);
+    __threadfence();
+    last = atomicAdd(&ws->done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  const unsigned long long mine = atomicAdd(&ws->best, 0ull);
+  const unsigned long long e = __ldcg(ex.epoch) + 1;
+  for (int q = 0; q < ex.world; ++q)
+    *reinterpret_cast<unsigned long long *>(tp_slot(ex, q, e, ex.rank)) = mine;
+  __threadfence_system();
+  for (int q = 0; q < ex.world; ++q) st_release_sys(tp_flags(ex, q) + ex.rank, e);
+  unsigned long long g = 0;
+  for (int r = 0; r < ex.world; ++r) {
+    const unsigned long long *f = tp_flags(ex, ex.rank) + r;
+    if (ld_acquire_sys(f) < e) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) < e) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_timeout();
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    const unsigned long long k =
+        __ldcg(reinterpret_cast<const unsigned long long *>(tp_slot(ex, ex.rank, e, r)));
+    g = k > g ? k : g;
+  }
+  out[0] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(g & 0xffffffffull));
+  *ex.epoch = e;
 }
 
 // Greedy token of each row of x [rows][n] (the first index on ties): one CTA

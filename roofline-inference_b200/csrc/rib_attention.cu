@@ -264,27 +264,36 @@ void *noalloc_scratch(int dev) {
 }
 
 // ------------------------------------------------------------------ model kernels
-template <int R, int C, bool SW>
+template <int R, int C, bool SW, bool TP>
 int gemv_launch_rc(const rib::model::GemvParams &p, cudaStream_t st) {
   const int rows_per_cta = rib::model::kGemvWarps * R;
   const int grid = ceil_div(p.rows_out, rows_per_cta);
-  return launch_pdl("gemv_kernel launch", rib::model::gemv_kernel<R, C, SW>, dim3(grid),
+  return launch_pdl("gemv_kernel launch", rib::model::gemv_kernel<R, C, SW, TP>, dim3(grid),
                     dim3(rib::model::kGemvWarps * 32), p.K * sizeof(float), st, p);
 }
 
-template <int R, bool SW>
+// Compile-time chunk counts for the K of Qwen3 projections, whole and split
+// over 2, 4 or 8 ranks; other K take the runtime loop.
+template <int R, bool SW, bool TP>
 int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
   switch (p.K) {
-    case 1024: return gemv_launch_rc<R, 4, SW>(p, st);
-    case 2048: return gemv_launch_rc<R, 8, SW>(p, st);
-    case 3072: return gemv_launch_rc<R, 12, SW>(p, st);
-    default: return gemv_launch_rc<R, 0, SW>(p, st);
+    case 256: return gemv_launch_rc<R, 1, SW, TP>(p, st);
+    case 512: return gemv_launch_rc<R, 2, SW, TP>(p, st);
+    case 768: return gemv_launch_rc<R, 3, SW, TP>(p, st);
+    case 1024: return gemv_launch_rc<R, 4, SW, TP>(p, st);
+    case 1536: return gemv_launch_rc<R, 6, SW, TP>(p, st);
+    case 2048: return gemv_launch_rc<R, 8, SW, TP>(p, st);
+    case 3072: return gemv_launch_rc<R, 12, SW, TP>(p, st);
+    default: return gemv_launch_rc<R, 0, SW, TP>(p, st);
   }
 }
 
 template <int R>
 int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
-  return p.epi == rib::model::kSwiGLU ? gemv_launch_r<R, true>(p, st) : gemv_launch_r<R, false>(p, st);
+  const bool tp = p.in_sum || p.epi == rib::model::kPeerPartial;
+  if (p.epi == rib::model::kSwiGLU)
+    return tp ? gemv_launch_r<R, true, true>(p, st) : gemv_launch_r<R, true, false>(p, st);
+  return tp ? gemv_launch_r<R, false, true>(p, st) : gemv_launch_r<R, false, false>(p, st);
 }
 
 // ------------------------------------------------------------------ persistent decode step
@@ -641,10 +650,21 @@ int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw, const vo
   return rope_launch(qkv, L, qw, kw, 0, nq, nkv, base, Lp, q_out, cache, cap, 0, stream, offset_dev);
 }
 
+// Rows per warp: one while that still gives at least 4 CTAs per SM, more for
+// tall matrices (the LM head) so that each CTA's x load and norm are
+// amortised over more weight bytes.
+static int gemv_dispatch(const rib::model::GemvParams &p, cudaStream_t st) {
+  using rib::model::kGemvWarps;
+  const int target_ctas = 4 * sm_count();
+  if (p.rows_out >= target_ctas * kGemvWarps * 4) return gemv_launch_r<4>(p, st);
+  if (p.rows_out >= target_ctas * kGemvWarps * 2) return gemv_launch_r<2>(p, st);
+  return gemv_launch_r<1>(p, st);
+}
+
 int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const void *res, int epi,
              int out_f32, void *y, void *stream) {
   using namespace rib::model;
-  if (!W || !x || !y || N < 1 || K < 256 || K % 256 || K > kMaxK) return RIB_EINVAL;
+  if (!W || !x || !y || N < 1 || K < 8 || K % 8 || K > kMaxK) return RIB_EINVAL;
   if (epi != kNone && epi != kResidual && epi != kSwiGLU) return RIB_EINVAL;
   if ((epi == kResidual) != (res != nullptr)) return RIB_EINVAL;
   if (epi == kSwiGLU && (N % 2 || out_f32)) return RIB_EINVAL;
@@ -653,7 +673,7 @@ int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const v
       (res && (reinterpret_cast<uintptr_t>(res) & 1u)))
     return RIB_EALIGN;
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
-  GemvParams p;
+  GemvParams p = {};
   p.W = static_cast<const uint16_t *>(W);
   p.x = static_cast<const uint16_t *>(x);
   p.nw = static_cast<const uint16_t *>(nw);
@@ -664,14 +684,84 @@ int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const v
   p.rows_out = epi == kSwiGLU ? N / 2 : N;
   p.epi = epi;
   p.out_f32 = out_f32 ? 1 : 0;
-  // Rows per warp: one while that still gives at least 4 CTAs per SM, more
-  // for tall matrices (the LM head) so that each CTA's x load and norm are
-  // amortised over more weight bytes.
-  const int target_ctas = 4 * sm_count();
+  return gemv_dispatch(p, static_cast<cudaStream_t>(stream));
+}
+
+size_t rib_tp_buffer_bytes(int world, int slot) {
+  if (world < 1 || world > RIB_TP_MAX_RANKS || slot < 4 || slot % 4) return 0;
+  return round256(2 * static_cast<size_t>(world) * slot * sizeof(float)) +
+         round256(static_cast<size_t>(world) * sizeof(unsigned long long));
+}
+
+// Checks a rib_tp_exchange and converts it to the device form.
+static int tp_ex_from(const rib_tp_exchange *ex, rib::model::TpEx &d) {
+  if (!ex || ex->world < 1 || ex->world > RIB_TP_MAX_RANKS || ex->rank < 0 || ex->rank >= ex->world ||
+      ex->slot < 4 || ex->slot % 4 || !ex->epoch || !ex->done)
+    return RIB_EINVAL;
+  if ((ex->epoch & 7u) || (ex->done & 3u)) return RIB_EALIGN;
+  d = {};
+  d.world = ex->world;
+  d.rank = ex->rank;
+  d.slot = ex->slot;
+  for (int q = 0; q < ex->world; ++q) {
+    if (!ex->buf[q]) return RIB_EINVAL;
+    if (ex->buf[q] & 255u) return RIB_EALIGN;
+    d.buf[q] = reinterpret_cast<float *>(ex->buf[q]);
+  }
+  d.flag_off = round256(2 * static_cast<size_t>(ex->world) * ex->slot * sizeof(float));
+  d.epoch = reinterpret_cast<unsigned long long *>(ex->epoch);
+  d.done = reinterpret_cast<unsigned int *>(ex->done);
+  return RIB_OK;
+}
+
+int rib_gemv_tp(const void *W, int N, int K, const void *x, const void *nw, int epi, int out_f32, void *y,
+                const rib_tp_exchange *ex, int in_sum, void *x_out, void *stream) {
+  using namespace rib::model;
+  if (!W || !x || N < 1 || K < 8 || K % 8 || K > kMaxK) return RIB_EINVAL;
+  if (epi != kNone && epi != kSwiGLU && epi != kPeerPartial) return RIB_EINVAL;
+  if (epi != kPeerPartial && !y) return RIB_EINVAL;
+  if (out_f32 && epi != kNone) return RIB_EINVAL;
+  if (epi == kSwiGLU && N % 2) return RIB_EINVAL;
+  GemvParams p = {};
+  if (epi == kPeerPartial || in_sum) {
+    const int st = tp_ex_from(ex, p.ex);
+    if (st != RIB_OK) return st;
+    if ((epi == kPeerPartial && N > ex->slot) || (in_sum && (K > ex->slot || !x_out))) return RIB_EINVAL;
+  }
+  if (!aligned16(W) || !aligned16(x) || (nw && !aligned16(nw)) || (y && !aligned16(y)) ||
+      (in_sum && !aligned16(x_out)))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  p.W = static_cast<const uint16_t *>(W);
+  p.x = static_cast<const uint16_t *>(x);
+  p.nw = static_cast<const uint16_t *>(nw);
+  p.y = y;
+  p.N = N;
+  p.K = K;
+  p.rows_out = epi == kSwiGLU ? N / 2 : N;
+  p.epi = epi;
+  p.out_f32 = out_f32 ? 1 : 0;
+  p.in_sum = in_sum ? 1 : 0;
+  p.x_out = static_cast<uint16_t *>(x_out);
+  return gemv_dispatch(p, static_cast<cudaStream_t>(stream));
+}
+
+int rib_argmax_f32_tp(const float *x, int n, int index_offset, int32_t *out, void *workspace,
+                      const rib_tp_exchange *ex, void *stream) {
+  if (!x || !out || !workspace || n < 1 || index_offset < 0) return RIB_EINVAL;
+  rib::model::TpEx d;
+  const int s = tp_ex_from(ex, d);
+  if (s != RIB_OK) return s;
+  if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15u))
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (p.rows_out >= target_ctas * kGemvWarps * 4) return gemv_launch_r<4>(p, st);
-  if (p.rows_out >= target_ctas * kGemvWarps * 2) return gemv_launch_r<2>(p, st);
-  return gemv_launch_r<1>(p, st);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(rib::model::ArgmaxWs), st);
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemsetAsync(argmax workspace)", e);
+  const int grid = std::max(1, std::min(ceil_div(n, 1024 * 4), sm_count()));
+  return launch_pdl("argmax_tp_kernel launch", rib::model::argmax_tp_kernel, dim3(grid), dim3(1024), 0, st, x,
+                    n, index_offset, static_cast<rib::model::ArgmaxWs *>(workspace), out, d);
 }
 
 int rib_add_rms(const void *a, const void *b, const void *w, int rows, int W, void *residual,

@@ -152,7 +152,7 @@ def _out_or_new(out, shape, dtype, device, name):
 def gemv(W, x, *, nw=None, res=None, swiglu=False, out_float=False, cfg=None, out=None):
     """y = epi(W @ pre(x)) for one token (agent-test/v2/kernels.py:103-113).
 
-    W [N, K] BF16 (K a multiple of 256); x [K]; nw: fuse the input RMSNorm
+    W [N, K] BF16 (K a multiple of 8); x [K]; nw: fuse the input RMSNorm
     (eps 1e-6) with this weight; res: y = bf16(res + bf16(W x)); swiglu: W is
     [gate; up] and y[N/2] = bf16(bf16(g * bf16(sigmoid(g))) * u); out_float:
     FP32 output (the logits).  `cfg` (Metal launch tuning) is accepted and
@@ -166,8 +166,8 @@ def gemv(W, x, *, nw=None, res=None, swiglu=False, out_float=False, cfg=None, ou
     N, K = W.shape
     if x.numel() != K:
         raise ValueError(f"x holds {x.numel()} elements, W has K = {K}")
-    if K % 256:
-        raise ValueError(f"K ({K}) must be a multiple of 256")
+    if K % 8:
+        raise ValueError(f"K ({K}) must be a multiple of 8")
     if nw is not None:
         require_bf16_cuda("nw", nw)
         require_same_device(W, nw)

@@ -137,9 +137,16 @@ class Engine:
     attention output (decode: the decode kernel's own NVLink stores; prefill:
     an NCCL all-gather), then runs the rest of the layer on the full hidden
     state, so all ranks hold the same activations and tokens.  Every rank
-    makes the same calls in the same order."""
+    makes the same calls in the same order.
 
-    def __init__(self, weights: Qwen3Weights, *, shard: bool = False, group=None):
+    tp=True (implies shard) also splits the projections (tensor
+    parallelism, tp.py): each rank keeps the O columns of its heads, a slice
+    of the gate/up rows and down columns and a slice of the LM-head rows;
+    attention outputs stay local, and the O / down partial sums and the argmax
+    keys are exchanged over NVLink inside the GEMV and argmax kernels (prefill:
+    NCCL all-reduce of FP32 partials)."""
+
+    def __init__(self, weights: Qwen3Weights, *, shard: bool = False, tp: bool = False, group=None):
         cfg = weights.config
         cfg.validate()
         if not weights.embed.is_cuda:
@@ -156,7 +163,9 @@ class Engine:
         self.group = group
         self.world, self.rank = 1, 0
         self.gather = None
-        if shard:
+        self.tp = bool(tp)
+        self.tpx = None
+        if shard or tp:
             import torch.distributed as dist
             from .nvlink_gather import NVLinkGather
             from .sharding import head_range
@@ -166,12 +175,21 @@ class Engine:
             h0, h1 = 0, cfg.num_kv_heads
         self.n_kv = h1 - h0                       # KV heads of this rank
         self.nq_local = 2 * self.n_kv             # query heads of this rank
-        if self.world > 1:
+        self.lm_head, self.v0 = self.embed, 0
+        if self.world > 1 and self.tp:
+            from .tp import TPExchange, shard_layer, split_range
+            f0, f1 = split_range(cfg.intermediate_size, self.rank, self.world)
+            self.v0, v1 = split_range(cfg.vocab_size, self.rank, self.world)
+            self.layers = [shard_layer(l, h0, h1, f0, f1, cfg.num_heads, cfg.num_kv_heads) for l in weights.layers]
+            self.lm_head = self.embed[self.v0:v1]
+            self.tpx = TPExchange(cfg.hidden_size, self.device, group)
+        elif self.world > 1:
             self.layers = [dict(l, qkv=_shard_qkv_rows(l["qkv"], h0, h1, cfg.num_heads, cfg.num_kv_heads))
                            for l in weights.layers]
             self.gather = NVLinkGather(1, self.nq_local, self.device, group)
             self.epoch_dev = torch.zeros(1, dtype=torch.int64, device=self.device)
         else:
+            self.tp = False
             self.layers = weights.layers
         self._sessions: dict = {}
 
@@ -184,12 +202,16 @@ class Engine:
         if self.gather is not None:
             self.gather.close()
             self.gather = None
+        if self.tpx is not None:
+            self.tpx.close()
+            self.tpx = None
 
     def _attend_one(self, q, cache_layer, n: int, out=None):
         """Decode attention of one query row over n keys: [1, nq_local, 128] in,
-        [1, n_heads, 128] out (all ranks' heads when sharded)."""
-        if self.world == 1:
-            return decode_attention(q, cache_layer, n, self.scale).reshape(1, self.n_heads, HEAD_DIM)
+        [1, n_heads, 128] out (all ranks' heads when KV-head sharded; this
+        rank's heads under tensor parallelism)."""
+        if self.world == 1 or self.tp:
+            return decode_attention(q, cache_layer, n, self.scale).reshape(1, self.nq_local, HEAD_DIM)
         from .attention import decode_workspace
         L = _lib.load()
         ws = decode_workspace(self.device, int(L.rib_decode_workspace_bytes(1, n, self.n_kv)))
@@ -199,6 +221,26 @@ class Engine:
             if out is None else out
         return self.gather.decode_into(q.reshape(1, self.nq_local, HEAD_DIM).contiguous(), ptrs, lens, n,
                                        cache_layer.shape[2], self.scale, ws, self.epoch_dev, out)
+
+    def _all_reduce_bf16(self, part):
+        """Sum of the ranks' FP32 partials [n, hidden] (NCCL), rounded once to BF16."""
+        import torch.distributed as dist
+        dist.all_reduce(part, group=self.group)
+        return part.to(torch.bfloat16)
+
+    def _gather_vocab(self, local):
+        """[..., V/N] FP32 logit slices of every rank -> [..., V] (NCCL all-gather)."""
+        import torch.distributed as dist
+        parts = [torch.empty_like(local) for _ in range(self.world)]
+        dist.all_gather(parts, local.contiguous(), group=self.group)
+        return torch.cat(parts, dim=-1)
+
+    def _proj_out(self, x, W):
+        """Row-parallel projection: the full output under tensor parallelism
+        (FP32 partials summed over ranks), else a plain BF16 GEMM."""
+        if self.tp:
+            return self._all_reduce_bf16(torch.mm(x, W.t(), out_dtype=torch.float32))
+        return _linear(x, W)
 
     def _gather_rows(self, o_local):
         """[n, nq_local * 128] per rank -> [n, n_heads * 128] (NCCL all-gather)."""
@@ -238,9 +280,10 @@ class Engine:
                 h = h[n - 1:]
             else:
                 kvl = cache.kv[i]
-                o = self._gather_rows(attention(q, kvl[0], kvl[1], n, off + n, self.scale))  # [n, H*128]
-            h, x = add_rms(h, _linear(o, w["o"]), w["post_norm"])
-            r = _linear(swiglu(_linear(x, w["gu"])), w["down"])
+                o = attention(q, kvl[0], kvl[1], n, off + n, self.scale)       # [n, nq_local*128]
+                o = o if self.tp else self._gather_rows(o)                     # [n, H*128]
+            h, x = add_rms(h, self._proj_out(o, w["o"]), w["post_norm"])
+            r = self._proj_out(swiglu(_linear(x, w["gu"])), w["down"])
             if final:
                 h = h + r
             else:
@@ -250,8 +293,10 @@ class Engine:
             return None
         if all_logits:
             hn = rms_norm(h, self.final_norm)
-            return torch.matmul(hn.float(), self.embed.float().t())[None]
-        return gemv(self.embed, h.reshape(-1), nw=self.final_norm, out_float=True)[None, None]
+            lg = torch.matmul(hn.float(), self.lm_head.float().t())
+            return (self._gather_vocab(lg) if self.tp else lg)[None]
+        lg = gemv(self.lm_head, h.reshape(-1), nw=self.final_norm, out_float=True)
+        return (self._gather_vocab(lg) if self.tp else lg)[None, None]
 
     # ---------------- decode (M = 1), eager ----------------
     def decode(self, token, cache: Cache, *, return_logits: bool = False):
@@ -261,6 +306,8 @@ class Engine:
         n = pos + 1
         if n > cache.capacity:
             raise ValueError("KV capacity exceeded")
+        if self.tp:
+            return self._decode_tp(token, cache, return_logits)
         h = embedding(self.embed, token.reshape(-1)).reshape(-1)
         for i, w in enumerate(self.layers):
             qkv = gemv(w["qkv"], h, nw=w["in_norm"])
@@ -275,6 +322,50 @@ class Engine:
         if return_logits:
             return logits
         return argmax(logits)
+
+    def _tp_layer(self, i: int, w: dict, hA, hB, qkv, a, pos_dev, attend) -> None:
+        """One tensor-parallel decode layer.  On entry hB holds the previous
+        layer's post-attention residual and the exchange holds its down
+        partials (layer 0: hA holds the embedding and nothing is pending); on
+        exit hA holds this layer's input residual, hB its post-attention
+        residual, and the exchange holds this layer's down partials."""
+        from .tp import EPI_PEER_PARTIAL
+        x = self.tpx
+        if i == 0:
+            x.gemv(w["qkv"], hA, nw=w["in_norm"], out=qkv)
+        else:
+            x.gemv(w["qkv"], hB, nw=w["in_norm"], out=qkv, in_sum=True, x_out=hA)
+        q = attend(qkv, w, i, pos_dev)
+        x.gemv(w["o"], q.reshape(-1), epi=EPI_PEER_PARTIAL)
+        x.gemv(w["gu"], hA, nw=w["post_norm"], epi=2, out=a, in_sum=True, x_out=hB)
+        x.gemv(w["down"], a, epi=EPI_PEER_PARTIAL)
+
+    def _decode_tp(self, token, cache: Cache, return_logits: bool):
+        """Engine.decode under tensor parallelism (eager)."""
+        pos = cache.offset
+        n = pos + 1
+        cfg, dev = self.cfg, self.device
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        hA, hB = torch.empty(cfg.hidden_size, **bf), torch.empty(cfg.hidden_size, **bf)
+        qkv = torch.empty((self.nq_local + 2 * self.n_kv) * HEAD_DIM, **bf)
+        a = torch.empty(cfg.intermediate_size // self.world, **bf)
+        embedding(self.embed, token.reshape(-1), out=hA.view(1, -1))
+
+        def attend(qkv_, w, i, _):
+            q = qk_norm_rope_append(qkv_, w["q_norm"], w["k_norm"], pos, self.nq_local, self.n_kv, self.base,
+                                    cache.kv[i])
+            return decode_attention(q, cache.kv[i], n, self.scale)
+
+        for i, w in enumerate(self.layers):
+            self._tp_layer(i, w, hA, hB, qkv, a, None, attend)
+        cache.offset += 1
+        logits = torch.empty(self.lm_head.shape[0], dtype=torch.float32, device=dev)
+        self.tpx.gemv(self.lm_head, hB, nw=self.final_norm, out=logits, out_float=True, in_sum=True, x_out=hA)
+        if return_logits:
+            return self._gather_vocab(logits)
+        ws = torch.empty(int(_lib.load().rib_argmax_workspace_bytes()), dtype=torch.uint8, device=dev)
+        out = torch.empty(1, dtype=torch.int32, device=dev)
+        return self.tpx.argmax(logits, self.v0, out, ws)
 
     def decode_graph(self, cache: Cache) -> "DecodeGraph":
         return DecodeGraph(self, cache)
@@ -374,9 +465,10 @@ class DecodeGraph:
         self.x = torch.empty((1, d), **bf)
         self.qkv = torch.empty(qkvw, **bf)
         self.q = torch.empty((self.e.nq_local, 1, HEAD_DIM), **bf)
-        self.o = torch.empty((1, self.e.n_heads, HEAD_DIM), **bf)
-        self.a = torch.empty(cfg.intermediate_size, **bf)
-        self.logits = torch.empty(cfg.vocab_size, dtype=torch.float32, device=dev)
+        heads = self.e.nq_local if engine.tp else self.e.n_heads        # attention outputs this rank holds
+        self.o = torch.empty((1, heads, HEAD_DIM), **bf)
+        self.a = torch.empty(cfg.intermediate_size // (engine.world if engine.tp else 1), **bf)
+        self.logits = torch.empty(engine.lm_head.shape[0], dtype=torch.float32, device=dev)
         L = _lib.load()
         self.max_n = cache.capacity
         ws_bytes = int(L.rib_decode_workspace_bytes(1, self.max_n, engine.n_kv))
@@ -404,6 +496,8 @@ class DecodeGraph:
         torch.cuda.synchronize(dev)
 
     def _step(self, count: bool) -> None:
+        if self.e.tp:
+            return self._step_tp(count)
         e, cfg, L = self.e, self.e.cfg, _lib.load()
         st = stream_handle(self.device)
         launches = 0
@@ -433,6 +527,37 @@ class DecodeGraph:
         self.nkeys.add_(1)
         if count:
             self.launches_per_step = launches
+
+    def _step_tp(self, count: bool) -> None:
+        """The step under tensor parallelism: per layer QKV GEMV (input: the
+        residual plus the previous layer's down partials), RoPE + append and
+        attention of this rank's heads, O GEMV to partials, gate/up GEMV +
+        SwiGLU (input: residual plus the O partials), down GEMV to partials;
+        then the LM-head slice and the cross-rank argmax."""
+        e, L = self.e, _lib.load()
+        st = stream_handle(self.device)
+        hA, hB = self.h[0], self.h[1]
+        embedding(e.embed, self.tok, out=hA.view(1, -1))
+        ptrs = self.ptrs
+
+        def attend(qkv, w, i, _):
+            qk_norm_rope_append_at(qkv, w["q_norm"], w["k_norm"], self.pos, e.nq_local, e.n_kv, e.base,
+                                   self.cache.kv[i], out=self.q)
+            rc = L.rib_decode_attention_batched(self.q.data_ptr(), ptrs.data_ptr() + 8 * i, self.nkeys.data_ptr(),
+                                                1, self.max_n, self.cache.capacity, e.nq_local, e.n_kv,
+                                                float(e.scale), self.o.data_ptr(), self.ws.data_ptr(),
+                                                self.ws.numel(), st)
+            _lib.check(rc, "decode_attention_batched")
+            return self.o
+
+        for i, w in enumerate(e.layers):
+            e._tp_layer(i, w, hA, hB, self.qkv, self.a, self.pos, attend)
+        e.tpx.gemv(e.lm_head, hB, nw=e.final_norm, out=self.logits, out_float=True, in_sum=True, x_out=hA)
+        e.tpx.argmax(self.logits, e.v0, self.tok, self.argmax_ws)
+        self.pos.add_(1)
+        self.nkeys.add_(1)
+        if count:
+            self.launches_per_step = 1 + 5 * len(e.layers) + 2
 
     def set_state(self, token, pos: int) -> None:
         """Next replay decodes `token` (int32 CUDA [1] or int) at position `pos`."""

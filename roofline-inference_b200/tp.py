@@ -1,0 +1,162 @@
+"""Tensor parallelism of the Qwen3 projections over the GPUs of one node.
+
+The single-GPU reference runs every GEMV of a decode step on one device
+(Engine.decode, agent-test/v2/engine.py:150-162).  Split over N ranks:
+
+  - rank r keeps KV heads head_range(r, N): their rows of the QKV projection,
+    their cache and their attention (as the KV-head sharded engine);
+  - the O projection keeps the columns of r's query heads, the gate and up
+    projections a slice of the intermediate rows, the down projection the
+    matching columns, the LM head a slice of the vocabulary rows;
+  - the O and down GEMVs then produce FP32 partial sums of the hidden vector.
+    Each rank's GEMV stores its partials straight into every rank's exchange
+    buffer over NVLink and raises a flag (RIB_EPI_PEER_PARTIAL); the next
+    GEMV of every rank waits for all flags and forms its input as
+    bf16(residual + bf16(sum of partials in rank order)).  No separate
+    collective runs, and every rank computes the same activations;
+  - the LM-head slices give per-rank argmax keys, exchanged the same way, so
+    every rank gets the same token.
+
+Per layer each rank reads 1/N of the projection weights, at the price of two
+cross-GPU exchanges (a few KB each).  Setup and close() are collective.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+MAX_RANKS = 8
+EPI_PEER_PARTIAL = 3
+
+
+class _TpExchangeStruct(ctypes.Structure):
+    """rib_tp_exchange (include/rib_attention.h)."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("buf", ctypes.c_uint64 * MAX_RANKS), ("epoch", ctypes.c_uint64),
+                ("done", ctypes.c_uint64), ("slot", ctypes.c_int)]
+
+
+def _bind(L: ctypes.CDLL) -> None:
+    vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    L.rib_tp_buffer_bytes.argtypes = [i, i]
+    L.rib_tp_buffer_bytes.restype = sz
+    L.rib_gemv_tp.argtypes = [vp, i, i, vp, vp, i, i, vp, ctypes.POINTER(_TpExchangeStruct), i, vp, vp]
+    L.rib_gemv_tp.restype = i
+    L.rib_argmax_f32_tp.argtypes = [vp, i, i, vp, vp, ctypes.POINTER(_TpExchangeStruct), vp]
+    L.rib_argmax_f32_tp.restype = i
+    L.rib_peer_buffer_alloc.argtypes = [i, sz, ctypes.POINTER(ctypes.c_void_p), vp]
+    L.rib_peer_buffer_alloc.restype = i
+    L.rib_peer_buffer_open.argtypes = [i, vp, ctypes.POINTER(ctypes.c_void_p)]
+    L.rib_peer_buffer_open.restype = i
+    L.rib_peer_buffer_close.argtypes = [i, vp]
+    L.rib_peer_buffer_close.restype = i
+    L.rib_peer_buffer_free.argtypes = [i, vp]
+    L.rib_peer_buffer_free.restype = i
+
+
+def split_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows [a, b) of an n-row dimension owned by `rank` (n % world == 0)."""
+    if world < 1 or not 0 <= rank < world or n % world:
+        raise ValueError(f"{n} does not split evenly over {world} ranks")
+    k = n // world
+    return rank * k, (rank + 1) * k
+
+
+def shard_layer(layer: dict, h0: int, h1: int, f0: int, f1: int, nq: int, nkv: int) -> dict:
+    """One layer's weights for the rank owning KV heads [h0, h1) and
+    intermediate rows [f0, f1): QKV rows of those heads, O columns of their
+    query heads, gate rows and up rows [f0, f1) (gate block first, as the
+    SwiGLU epilogue reads them), down columns [f0, f1)."""
+    from .model import HEAD_DIM, _shard_qkv_rows
+    F = layer["gu"].shape[0] // 2
+    out = dict(layer)
+    out["qkv"] = _shard_qkv_rows(layer["qkv"], h0, h1, nq, nkv)
+    out["o"] = layer["o"][:, 2 * h0 * HEAD_DIM:2 * h1 * HEAD_DIM].contiguous()
+    out["gu"] = torch.cat([layer["gu"][f0:f1], layer["gu"][F + f0:F + f1]]).contiguous()
+    out["down"] = layer["down"][:, f0:f1].contiguous()
+    return out
+
+
+class TPExchange:
+    """This rank's exchange buffer, its peers' mappings and the device
+    counters; `struct` is the rib_tp_exchange to pass to the kernels.
+    slot: the longest vector exchanged (floats, a multiple of 4)."""
+
+    def __init__(self, slot: int, device, group=None):
+        self.L = L = _lib.load()
+        _bind(L)
+        self.group = group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > MAX_RANKS:
+            raise ValueError(f"at most {MAX_RANKS} ranks")
+        self.device = torch.device(device)
+        self.dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.slot = (int(slot) + 3) // 4 * 4
+        self.nbytes = int(L.rib_tp_buffer_bytes(self.world, self.slot))
+        if self.nbytes == 0:
+            raise ValueError("bad exchange geometry")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        _lib.check(L.rib_peer_buffer_alloc(self.dev, self.nbytes, ctypes.byref(own), handle),
+                   "rib_peer_buffer_alloc")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.base = [0] * self.world
+        self._opened: list[int] = []
+        for r in range(self.world):
+            if r == self.rank:
+                self.base[r] = own.value
+                continue
+            ptr = ctypes.c_void_p()
+            buf = ctypes.create_string_buffer(handles[r], 64)
+            _lib.check(L.rib_peer_buffer_open(self.dev, buf, ctypes.byref(ptr)), "rib_peer_buffer_open")
+            self.base[r] = ptr.value
+            self._opened.append(ptr.value)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        s = _TpExchangeStruct()
+        s.world, s.rank, s.slot = self.world, self.rank, self.slot
+        for r in range(self.world):
+            s.buf[r] = self.base[r]
+        s.epoch, s.done = self.epoch.data_ptr(), self.done.data_ptr()
+        self.struct = s
+        self.closed = False
+        dist.barrier(group=group)
+
+    def gemv(self, W, x, *, nw=None, epi: int = 0, out=None, out_float: bool = False, in_sum: bool = False,
+             x_out=None, stream=None):
+        """rib_gemv_tp on torch's current stream; returns `out`."""
+        from ._tensors import stream_handle
+        if self.closed:
+            raise RuntimeError("TPExchange is closed")
+        st = stream_handle(self.device) if stream is None else stream
+        N, K = W.shape
+        _lib.check(self.L.rib_gemv_tp(
+            W.data_ptr(), N, K, x.data_ptr(), None if nw is None else nw.data_ptr(), epi, int(out_float),
+            None if out is None else out.data_ptr(), ctypes.byref(self.struct), int(in_sum),
+            None if x_out is None else x_out.data_ptr(), st), "gemv_tp")
+        return out
+
+    def argmax(self, logits, offset: int, out, workspace):
+        """Global greedy token over every rank's logit slice into out (int32 [1])."""
+        from ._tensors import stream_handle
+        _lib.check(self.L.rib_argmax_f32_tp(logits.data_ptr(), logits.numel(), int(offset), out.data_ptr(),
+                                            workspace.data_ptr(), ctypes.byref(self.struct),
+                                            stream_handle(self.device)), "argmax_f32_tp")
+        return out
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for ptr in self._opened:
+            self.L.rib_peer_buffer_close(self.dev, ctypes.c_void_p(ptr))
+        dist.barrier(group=self.group)
+        self.L.rib_peer_buffer_free(self.dev, ctypes.c_void_p(self.base[self.rank]))
+        self.closed = True

@@ -58,7 +58,8 @@ def gemv_abs_tol(mnp, W, x, nw):
 
 
 # ------------------------------------------------------------------ GEMV
-@pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 2048), (1024, 3072), (1000, 512), (40, 256)])
+@pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 2048), (1024, 3072), (1000, 512), (40, 256),
+                                 (1024, 384), (64, 1536), (72, 136)])
 @pytest.mark.parametrize("epi", ["none", "norm", "res", "swiglu"])
 def test_gemv(rib, mnp, N, K, epi):
     W = rand_bf16((N, K), 1, 0.05)
@@ -411,3 +412,41 @@ def test_scheduler_greedy_consistent(rib):
             margin = float(row.max() - row[t])
             assert margin <= 1e-2 * float(row.abs().max()), (rid, j, margin)
     assert rib._lib.take_device_status() == 0
+
+
+# ------------------------------------------------------------------ tensor-parallel exchange, one rank
+def test_tp_exchange_single_rank(rib):
+    """The tensor-parallel kernels in a one-rank group: the partial-sum
+    epilogue followed by an in_sum GEMV equals the residual GEMV chain
+    bit for bit (one rank: the sum is the partial), over several exchanges
+    (both buffer regions), and the exchanged argmax adds the slice offset."""
+    import torch.distributed as dist
+    from importlib import import_module
+    tp = import_module("roofline-inference_b200.tp")
+    dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1, device_id=DEV)
+    try:
+        x = tp.TPExchange(512, DEV)
+        L = rib.load_library()
+        ws = torch.empty(int(L.rib_argmax_workspace_bytes()), dtype=torch.uint8, device=DEV)
+        for it in range(3):
+            Wo, o = rand_bf16((512, 256), 20 + it, 0.05), rand_bf16((256,), 30 + it)
+            Wgu, nw = rand_bf16((768, 512), 40 + it, 0.05), rand_bf16((512,), 50 + it, 0.1) + 1
+            h = rand_bf16((512,), 60 + it)
+            x.gemv(Wo, o, epi=tp.EPI_PEER_PARTIAL)
+            h1 = torch.empty_like(h)
+            a = torch.empty(384, dtype=torch.bfloat16, device=DEV)
+            x.gemv(Wgu, h, nw=nw, epi=2, out=a, in_sum=True, x_out=h1)
+            want_h1 = rib.gemv(Wo, o, res=h)
+            assert torch.equal(h1, want_h1), it
+            assert torch.equal(a, rib.gemv(Wgu, want_h1, nw=nw, swiglu=True)), it
+            lg = torch.randn(1000, device=DEV)
+            lg[137 + it] = 50.0
+            tok = torch.empty(1, dtype=torch.int32, device=DEV)
+            x.argmax(lg, 5000, tok, ws)
+            assert int(tok) == 5137 + it
+        torch.cuda.synchronize()
+        assert int(x.epoch) == 6 and int(x.done) == 0
+        assert rib._lib.take_device_status() == 0
+        x.close()
+    finally:
+        dist.destroy_process_group()

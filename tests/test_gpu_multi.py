@@ -152,3 +152,75 @@ def test_sharded_engine_two_gpus():
         assert rel <= 1e-2, f"rank {r}: prefill logits differ by {rel}"
         assert graph == eager == single, (r, graph, eager, single)
     assert res[0][0] == res[1][0]
+
+
+# ------------------------------------------------------------------ tensor-parallel Qwen3 forward
+def _tp_worker(rank, world, port, q_out):
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                             timeout=datetime.timedelta(seconds=60))
+        rib = importlib.import_module("roofline-inference_b200")
+        cfg = rib.Qwen3Config(num_layers=2, hidden_size=256, num_heads=4, num_kv_heads=2,
+                              intermediate_size=512, vocab_size=1000)
+        w = rib.random_weights(cfg, seed=63).to(dev)           # identical on every rank
+        prompt = [int(t) for t in np.random.default_rng(64).integers(0, cfg.vocab_size, 45)]
+        eng = rib.Engine(w, tp=True)
+        assert eng.tp and eng.n_kv == 1 and eng.layers[0]["down"].shape[1] == 256
+        ref = rib.Engine(w)                                     # single GPU, no collective calls
+        toks = torch.tensor(prompt, dtype=torch.int32, device=dev)
+        # prefill logits, then three eager decode steps' logits, against the single-GPU engine
+        ct, cr = eng.new_cache(64), ref.new_cache(64)
+        rels = [float((eng.prefill(toks, ct, last=True).reshape(-1) - (lr := ref.prefill(toks, cr, last=True)
+                                                                        .reshape(-1))).abs().max()
+                      / lr.abs().max())]
+        t = torch.tensor([7], dtype=torch.int32, device=dev)
+        for _ in range(3):
+            lt = eng.decode(t, ct, return_logits=True)
+            lr = ref.decode(t, cr, return_logits=True)
+            rels.append(float((lt - lr).abs().max() / lr.abs().max()))
+            t = (t * 5 + 3) % cfg.vocab_size
+        graph = list(eng.generate(prompt, max_tokens=10))                 # CUDA-graph steps
+        eager = list(eng.generate(prompt, max_tokens=10, use_graph=False))
+        # every generated token is the single-GPU greedy choice for its prefix, up to a near tie
+        full = torch.tensor(prompt + graph[:-1], dtype=torch.int32, device=dev)
+        la = ref.prefill(full, ref.new_cache(64), last=True, all_logits=True)[0]
+        margins = [float((la[len(prompt) - 1 + j].max() - la[len(prompt) - 1 + j][tk])
+                         / la[len(prompt) - 1 + j].abs().max()) for j, tk in enumerate(graph)]
+        status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
+        eng.close()
+        torch.distributed.destroy_process_group()
+        q_out.put((rank, (graph, eager, rels, max(margins), status)))
+    except Exception as e:  # report to the parent
+        q_out.put((rank, repr(e)))
+
+
+def test_tp_engine_two_gpus():
+    """Tensor-parallel Qwen3 forward on 2 GPUs (projections split, partial
+    sums and argmax keys exchanged over NVLink inside the kernels): prefill and
+    decode logits match the single-GPU engine, graph and eager decode give the
+    same tokens on both ranks, and each token is the single-GPU greedy choice
+    for its prefix up to a near-tie margin."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert not isinstance(v, str), f"rank {r}: {v}"
+        graph, eager, rels, margin, status = v
+        assert status == 0, f"rank {r}: device status {status}"
+        assert max(rels) <= 1e-2, f"rank {r}: logits differ by {rels}"
+        assert graph == eager, (r, graph, eager)
+        assert margin <= 1e-2, (r, margin)
+    assert res[0][0] == res[1][0]

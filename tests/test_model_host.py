@@ -153,3 +153,61 @@ def test_batched_entry_points_reject_bad_arguments(rib):
                                              None) == 1
     assert L.rib_argmax_rows_f32(FAKE, 0, 10, FAKE, None) == 1
     assert L.rib_argmax_rows_f32(0x10002, 2, 10, FAKE, None) == 3
+
+
+# ------------------------------------------------------------------ tensor-parallel weight split
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_shard_layer_reconstructs_products(rib, world):
+    """The per-rank slices of shard_layer rebuild every projection: row
+    slices concatenate to the full output, column slices sum to it."""
+    import importlib
+    tp = importlib.import_module("roofline-inference_b200.tp")
+    sharding = importlib.import_module("roofline-inference_b200.sharding")
+    cfg = rib.Qwen3Config(num_layers=1, hidden_size=256, num_heads=8, num_kv_heads=4,
+                          intermediate_size=1024, vocab_size=1000)
+    layer = {k: v.double() for k, v in rib.random_weights(cfg, seed=9).layers[0].items()}
+    F = cfg.intermediate_size
+    g = torch.Generator().manual_seed(1)
+    o_in = torch.randn(cfg.q_dim, generator=g, dtype=torch.float64)
+    a_in = torch.randn(F, generator=g, dtype=torch.float64)
+    x = torch.randn(cfg.hidden_size, generator=g, dtype=torch.float64)
+    o_sum, d_sum, gates, ups = 0, 0, [], []
+    for r in range(world):
+        h0, h1 = sharding.head_range(r, world, cfg.num_kv_heads)
+        f0, f1 = tp.split_range(F, r, world)
+        s = tp.shard_layer(layer, h0, h1, f0, f1, cfg.num_heads, cfg.num_kv_heads)
+        o_sum = o_sum + s["o"] @ o_in[2 * h0 * 128:2 * h1 * 128]
+        d_sum = d_sum + s["down"] @ a_in[f0:f1]
+        gu = s["gu"] @ x
+        gates.append(gu[:f1 - f0])
+        ups.append(gu[f1 - f0:])
+    torch.testing.assert_close(o_sum, layer["o"] @ o_in)
+    torch.testing.assert_close(d_sum, layer["down"] @ a_in)
+    full = layer["gu"] @ x
+    torch.testing.assert_close(torch.cat(gates), full[:F])
+    torch.testing.assert_close(torch.cat(ups), full[F:])
+    with pytest.raises(ValueError):
+        tp.split_range(1000, 0, 3)
+
+
+def test_tp_entry_points_reject_bad_arguments(rib):
+    import ctypes
+    import importlib
+    tp = importlib.import_module("roofline-inference_b200.tp")
+    L = rib.load_library()
+    tp._bind(L)
+    assert L.rib_tp_buffer_bytes(2, 256) == 2 * 2 * 256 * 4 + 256
+    assert L.rib_tp_buffer_bytes(9, 256) == 0 and L.rib_tp_buffer_bytes(2, 6) == 0
+    ex = tp._TpExchangeStruct()
+    ex.world, ex.rank, ex.slot = 2, 0, 256
+    ex.buf[0], ex.buf[1], ex.epoch, ex.done = 0x10000, 0x20000, 0x30000, 0x30008
+    # partial epilogue wider than the slot; in_sum without x_out; misaligned peer buffer; bad rank
+    assert L.rib_gemv_tp(FAKE, 512, 256, FAKE, None, 3, 0, None, ctypes.byref(ex), 0, None, None) == 1
+    assert L.rib_gemv_tp(FAKE, 64, 256, FAKE, None, 0, 0, FAKE, ctypes.byref(ex), 1, None, None) == 1
+    ex.buf[1] = 0x20010
+    assert L.rib_gemv_tp(FAKE, 64, 256, FAKE, None, 3, 0, None, ctypes.byref(ex), 0, None, None) == 3
+    ex.buf[1], ex.rank = 0x20000, 2
+    assert L.rib_argmax_f32_tp(FAKE, 100, 0, FAKE, FAKE, ctypes.byref(ex), None) == 1
+    # a residual epilogue has no tensor-parallel form
+    ex.rank = 0
+    assert L.rib_gemv_tp(FAKE, 64, 256, FAKE, None, 1, 0, FAKE, ctypes.byref(ex), 0, None, None) == 1
