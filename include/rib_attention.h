@@ -416,15 +416,16 @@ int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out,
  * columns of the down projection and a slice of the LM-head rows.  The O and
  * down GEMVs then give FP32 partial sums of the full hidden vector, which
  * every rank stores straight into every rank's exchange buffer over NVLink
- * (RIB_EPI_PEER_PARTIAL) and flags with the exchange's epoch; the next GEMV
- * waits (bounded) for all ranks' flags and reads its input as
+ * (RIB_EPI_PEER_PARTIAL); the next GEMV reads its input as
  * bf16(residual + bf16(sum of the partials in rank order)), the rounding of
  * RIB_EPI_RESIDUAL, so every rank computes identical activations.
  *
  * Exchange buffer of one rank (rib_tp_buffer_bytes(world, slot) bytes,
- * zeroed, shared through rib_peer_buffer_alloc / _open):
- *   [2 regions][world][slot] FP32 partials, then (at a 256-byte boundary)
- *   [world] u64 epoch flags.  Exchange number e uses region e & 1.
+ * zeroed, shared through rib_peer_buffer_alloc / _open): [2 regions][world]
+ * [slot] 8-byte words.  Exchange number e uses region e & 1; a word holds a
+ * value in its low 32 bits and the low 32 bits of e in its high 32 bits and
+ * is written with one 8-byte store, so a reader polls the words themselves
+ * (bounded) until they carry e: no fence and no separate flag.
  * epoch: device u64 counting this rank's exchanges (zero on every rank
  * before the first); done: device u32 arrival counter (zero; every call
  * leaves it zero).  All ranks make the same exchanges in the same order. */
@@ -436,7 +437,7 @@ typedef struct rib_tp_exchange {
   uint64_t buf[RIB_TP_MAX_RANKS]; /* per rank: its exchange buffer (peer mapping) */
   uint64_t epoch;                  /* device address, u64                         */
   uint64_t done;                   /* device address, u32                         */
-  int slot;                        /* floats per rank slot (>= every N exchanged) */
+  int slot;                        /* words per rank slot (>= every N exchanged)  */
 } rib_tp_exchange;
 
 size_t rib_tp_buffer_bytes(int world, int slot);

@@ -32,43 +32,57 @@ enum Epilogue { kNone = 0, kResidual = 1, kSwiGLU = 2, kPeerPartial = 3 };
 __device__ __forceinline__ void record_status(int status) { atomicExch(&g_device_status, status); }
 
 // ------------------------------------------------------------------ tensor-parallel exchange
-// rib_tp_exchange on the device.  Rank q's buffer: [2 regions][world][slot]
-// FP32 partials, then [world] u64 epoch flags at byte offset flag_off.
+// rib_tp_exchange on the device.  Rank q's buffer holds [2 regions][world]
+// [slot] 8-byte words; exchange e uses region e & 1, and rank r's values go
+// to slot r.  Each word carries its value in the low 32 bits and the low 32
+// bits of e in the high ones, written with one 8-byte store (single-copy
+// atomic), so a reader that sees the epoch also sees the value: no fence, no
+// separate flag and one NVLink crossing per exchange.  A region is rewritten
+// two exchanges later, after every rank has read it (each rank produces
+// exchange e + 1 only after consuming exchange e).
 struct TpEx {
   int world, rank, slot;
-  float *buf[RIB_TP_MAX_RANKS];
-  size_t flag_off;
+  unsigned long long *buf[RIB_TP_MAX_RANKS];
   unsigned long long *epoch;  // this rank's exchange counter
   unsigned int *done;         // arrival counter of the producing kernel's warps
 };
 
-__device__ __forceinline__ unsigned long long *tp_flags(const TpEx &ex, int q) {
-  return reinterpret_cast<unsigned long long *>(reinterpret_cast<char *>(ex.buf[q]) + ex.flag_off);
-}
-
-// Slot of `rank`'s partials for exchange e, in rank q's buffer.
-__device__ __forceinline__ float *tp_slot(const TpEx &ex, int q, unsigned long long e, int rank) {
+// Slot of `rank`'s words for exchange e, in rank q's buffer.
+__device__ __forceinline__ unsigned long long *tp_slot(const TpEx &ex, int q, unsigned long long e, int rank) {
   return ex.buf[q] + (static_cast<size_t>(e & 1ull) * ex.world + rank) * ex.slot;
 }
 
-// Every thread of the CTA returns once all ranks' flags in this rank's buffer
-// reached e (thread t < world polls rank t's flag), or after kWaitLimitNs
-// with RIB_ETIMEOUT recorded.
-__device__ __forceinline__ void tp_wait_all(const TpEx &ex, unsigned long long e) {
-  if (static_cast<int>(threadIdx.x) < ex.world) {
-    const unsigned long long *f = tp_flags(ex, ex.rank) + threadIdx.x;
-    if (ld_acquire_sys(f) < e) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(f) < e) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
-          record_timeout();
-          break;
-        }
-        __nanosleep(64);
-      }
+__device__ __forceinline__ unsigned long long tp_word(uint32_t value_bits, unsigned long long e) {
+  return (static_cast<unsigned long long>(static_cast<uint32_t>(e)) << 32) | value_bits;
+}
+
+__device__ __forceinline__ void st_volatile_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ ulonglong2 ld_volatile_v2u64(const unsigned long long *p) {
+  ulonglong2 v;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+// Two words of exchange e at p (16-byte aligned), polled until both carry
+// e; gives up after kWaitLimitNs (shared deadline t0 per thread, 0: not
+// started) with RIB_ETIMEOUT recorded.
+__device__ __forceinline__ ulonglong2 tp_read2(const unsigned long long *p, unsigned long long e, uint64_t &t0) {
+  const uint32_t want = static_cast<uint32_t>(e);
+  ulonglong2 v = ld_volatile_v2u64(p);
+  while (static_cast<uint32_t>(v.x >> 32) != want || static_cast<uint32_t>(v.y >> 32) != want) {
+    const uint64_t now = global_timer_ns();
+    if (t0 == 0) t0 = now;
+    if (now - t0 > kWaitLimitNs) {
+      record_timeout();
+      break;
     }
+    __nanosleep(32);
+    v = ld_volatile_v2u64(p);
   }
-  __syncthreads();
+  return v;
 }
 
 // 16-byte streaming load that does not allocate in L1 (weights are read once).
@@ -163,12 +177,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   pdl_wait();
 
   // ---- x into shared memory (normalised when nw is given)
-  const float *part = nullptr;
+  const unsigned long long *part = nullptr;
+  unsigned long long ex_e = 0;
   if (TP && p.in_sum) {
-    const unsigned long long e = __ldcg(p.ex.epoch);  // the exchange the previous kernel published
-    tp_wait_all(p.ex, e);
-    part = tp_slot(p.ex, p.ex.rank, e, 0);
+    ex_e = __ldcg(p.ex.epoch);  // the exchange the previous kernel published
+    part = tp_slot(p.ex, p.ex.rank, ex_e, 0);
   }
+  uint64_t t0 = 0;
   float ss = 0.f;
   for (int i = tid * 8; i < K; i += blockDim.x * 8) {
     const uint4 v = *reinterpret_cast<const uint4 *>(p.x + i);
@@ -177,17 +192,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     if (TP && part) {
       float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int r = 0; r < p.ex.world; ++r) {
-        const float4 a = __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(r) * p.ex.slot + i));
-        const float4 b =
-            __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(r) * p.ex.slot + i + 4));
-        sum[0] += a.x;
-        sum[1] += a.y;
-        sum[2] += a.z;
-        sum[3] += a.w;
-        sum[4] += b.x;
-        sum[5] += b.y;
-        sum[6] += b.z;
-        sum[7] += b.w;
+        const unsigned long long *src = part + static_cast<size_t>(r) * p.ex.slot + i;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const ulonglong2 v = tp_read2(src + 2 * j, ex_e, t0);
+          sum[2 * j] += __uint_as_float(static_cast<uint32_t>(v.x));
+          sum[2 * j + 1] += __uint_as_float(static_cast<uint32_t>(v.y));
+        }
       }
 #pragma unroll
       for (int e = 0; e < 8; ++e) f[e] = round_bf16(f[e] + round_bf16(sum[e]));
@@ -252,27 +263,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   }
 #pragma unroll
   for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
-  if (lane != 0) return;
   if (TP && !SW && p.epi == kPeerPartial) {
-    // Rows into slot `rank` of every rank's buffer; the last warp to finish
-    // (of ceil(rows_out / R)) publishes the exchange's epoch to every rank.
+    // Lane q stores the warp's rows, tagged with the exchange's epoch, into
+    // slot `rank` of rank q's buffer.  The last warp to finish (of
+    // ceil(rows_out / R)) advances this rank's exchange counter.
     const unsigned long long e = __ldcg(p.ex.epoch) + 1;
-    for (int q = 0; q < p.ex.world; ++q) {
-      float *dst = tp_slot(p.ex, q, e, p.ex.rank);
+    if (lane < p.ex.world) {
+      unsigned long long *dst = tp_slot(p.ex, lane, e, p.ex.rank);
 #pragma unroll
       for (int r = 0; r < R; ++r)
-        if (row0 + r < p.rows_out) dst[row0 + r] = acc[r];
+        if (row0 + r < p.rows_out) st_volatile_u64(dst + row0 + r, tp_word(__float_as_uint(acc[r]), e));
     }
-    __threadfence_system();
-    const unsigned int warps = static_cast<unsigned int>((p.rows_out + R - 1) / R);
-    if (atomicAdd(p.ex.done, 1u) == warps - 1) {
-      __threadfence_system();
-      for (int q = 0; q < p.ex.world; ++q) st_release_sys(tp_flags(p.ex, q) + p.ex.rank, e);
-      *p.ex.epoch = e;
-      atomicExch(p.ex.done, 0u);
+    if (lane == 0) {
+      const unsigned int warps = static_cast<unsigned int>((p.rows_out + R - 1) / R);
+      if (atomicAdd(p.ex.done, 1u) == warps - 1) {
+        *p.ex.epoch = e;
+        atomicExch(p.ex.done, 0u);
+      }
     }
     return;
   }
+  if (lane != 0) return;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     const int row = row0 + r;
@@ -484,25 +495,18 @@ __global__ void __launch_bounds__(1024) argmax_tp_kernel(const float *__restrict
   __threadfence();
   const unsigned long long mine = atomicAdd(&ws->best, 0ull);
   const unsigned long long e = __ldcg(ex.epoch) + 1;
-  for (int q = 0; q < ex.world; ++q)
-    *reinterpret_cast<unsigned long long *>(tp_slot(ex, q, e, ex.rank)) = mine;
-  __threadfence_system();
-  for (int q = 0; q < ex.world; ++q) st_release_sys(tp_flags(ex, q) + ex.rank, e);
+  // this rank's key as two tagged words (low, high half) in every rank's slot
+  for (int q = 0; q < ex.world; ++q) {
+    unsigned long long *dst = tp_slot(ex, q, e, ex.rank);
+    st_volatile_u64(dst, tp_word(static_cast<uint32_t>(mine), e));
+    st_volatile_u64(dst + 1, tp_word(static_cast<uint32_t>(mine >> 32), e));
+  }
   unsigned long long g = 0;
+  uint64_t t0 = 0;
   for (int r = 0; r < ex.world; ++r) {
-    const unsigned long long *f = tp_flags(ex, ex.rank) + r;
-    if (ld_acquire_sys(f) < e) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(f) < e) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
-          record_timeout();
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    const unsigned long long k =
-        __ldcg(reinterpret_cast<const unsigned long long *>(tp_slot(ex, ex.rank, e, r)));
+    const ulonglong2 v = tp_read2(tp_slot(ex, ex.rank, e, r), e, t0);
+    const unsigned long long k = (static_cast<unsigned long long>(static_cast<uint32_t>(v.y)) << 32) |
+                                 static_cast<uint32_t>(v.x);
     g = k > g ? k : g;
   }
   out[0] = static_cast<int32_t>(0xffffffffu - static_cast<uint32_t>(g & 0xffffffffull));

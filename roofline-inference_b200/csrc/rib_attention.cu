@@ -689,8 +689,7 @@ int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const v
 
 size_t rib_tp_buffer_bytes(int world, int slot) {
   if (world < 1 || world > RIB_TP_MAX_RANKS || slot < 4 || slot % 4) return 0;
-  return round256(2 * static_cast<size_t>(world) * slot * sizeof(float)) +
-         round256(static_cast<size_t>(world) * sizeof(unsigned long long));
+  return round256(2 * static_cast<size_t>(world) * slot * sizeof(unsigned long long));
 }
 
 // Checks a rib_tp_exchange and converts it to the device form.
@@ -706,9 +705,8 @@ static int tp_ex_from(const rib_tp_exchange *ex, rib::model::TpEx &d) {
   for (int q = 0; q < ex->world; ++q) {
     if (!ex->buf[q]) return RIB_EINVAL;
     if (ex->buf[q] & 255u) return RIB_EALIGN;
-    d.buf[q] = reinterpret_cast<float *>(ex->buf[q]);
+    d.buf[q] = reinterpret_cast<unsigned long long *>(ex->buf[q]);
   }
-  d.flag_off = round256(2 * static_cast<size_t>(ex->world) * ex->slot * sizeof(float));
   d.epoch = reinterpret_cast<unsigned long long *>(ex->epoch);
   d.done = reinterpret_cast<unsigned int *>(ex->done);
   return RIB_OK;

@@ -10,10 +10,11 @@ The single-GPU reference runs every GEMV of a decode step on one device
     matching columns, the LM head a slice of the vocabulary rows;
   - the O and down GEMVs then produce FP32 partial sums of the hidden vector.
     Each rank's GEMV stores its partials straight into every rank's exchange
-    buffer over NVLink and raises a flag (RIB_EPI_PEER_PARTIAL); the next
-    GEMV of every rank waits for all flags and forms its input as
-    bf16(residual + bf16(sum of partials in rank order)).  No separate
-    collective runs, and every rank computes the same activations;
+    buffer over NVLink (RIB_EPI_PEER_PARTIAL), each value in an 8-byte word
+    tagged with the exchange's epoch; the next GEMV of every rank polls the
+    words until they carry the epoch and forms its input as
+    bf16(residual + bf16(sum of partials in rank order)).  No fence, flag or
+    separate collective runs, and every rank computes the same activations;
   - the LM-head slices give per-rank argmax keys, exchanged the same way, so
     every rank gets the same token.
 
@@ -84,7 +85,7 @@ def shard_layer(layer: dict, h0: int, h1: int, f0: int, f1: int, nq: int, nkv: i
 class TPExchange:
     """This rank's exchange buffer, its peers' mappings and the device
     counters; `struct` is the rib_tp_exchange to pass to the kernels.
-    slot: the longest vector exchanged (floats, a multiple of 4)."""
+    slot: the longest vector exchanged (words; rounded up to a multiple of 4)."""
 
     def __init__(self, slot: int, device, group=None):
         self.L = L = _lib.load()

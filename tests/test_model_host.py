@@ -196,7 +196,7 @@ def test_tp_entry_points_reject_bad_arguments(rib):
     tp = importlib.import_module("roofline-inference_b200.tp")
     L = rib.load_library()
     tp._bind(L)
-    assert L.rib_tp_buffer_bytes(2, 256) == 2 * 2 * 256 * 4 + 256
+    assert L.rib_tp_buffer_bytes(2, 256) == 2 * 2 * 256 * 8
     assert L.rib_tp_buffer_bytes(9, 256) == 0 and L.rib_tp_buffer_bytes(2, 6) == 0
     ex = tp._TpExchangeStruct()
     ex.world, ex.rank, ex.slot = 2, 0, 256
