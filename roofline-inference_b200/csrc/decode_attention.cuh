@@ -161,6 +161,134 @@ __device__ __forceinline__ void unpack8(const uint4 &r, float *f) {
   f[6] = bf16lo(r.w); f[7] = bf16hi(r.w);
 }
 
+// q of KV head h's two query heads for sequence b, pre-scaled: lane (g, j)
+// holds dims [8j, 8j+8) and [64+8j, 64+8j+8).
+__device__ __forceinline__ void load_q(const Params &p, int b, int h, int lane, float (&qa)[2][16]) {
+  const int j = lane & 7;
+  const uint16_t *qb = p.q + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    // L2-coherent loads: in the persistent decode step another CTA wrote q
+    // earlier in the same kernel (a line left in this SM's L1 could be stale).
+    const uint4 r0 = __ldcg(reinterpret_cast<const uint4 *>(qb + hh * D + 8 * j));
+    const uint4 r1 = __ldcg(reinterpret_cast<const uint4 *>(qb + hh * D + 64 + 8 * j));
+    unpack8(r0, &qa[hh][0]);
+    unpack8(r1, &qa[hh][8]);
+#pragma unroll
+    for (int d = 0; d < 16; ++d) qa[hh][d] *= p.qscale;
+  }
+}
+
+// Scores, online softmax and P.V of one ring tile of `rows` keys for both
+// query heads of a consumer warp (lane layout described at the top of this
+// file); ends with the warp converged, before the slot is released.
+__device__ __forceinline__ void consume_tile(const uint8_t *Kt, const uint8_t *Vt, float (&pbuf)[2][TK], int lane,
+                                             int rows, const float (&qa)[2][16], float (&m_run)[2],
+                                             float (&l_run)[2], float (&o)[2][4]) {
+  const int g = lane >> 3, j = lane & 7;
+
+  // ---- scores: group g handles keys g*8 .. g*8+7 of the tile
+  float s0[8], s1[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint8_t *row = Kt + (g * 8 + i) * ROW_BYTES;
+    float kf[16];
+    unpack8(*reinterpret_cast<const uint4 *>(row + 16 * j), &kf[0]);
+    unpack8(*reinterpret_cast<const uint4 *>(row + 128 + 16 * j), &kf[8]);
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int d = 0; d < 16; ++d) {
+      a0 = fmaf(qa[0][d], kf[d], a0);
+      a1 = fmaf(qa[1][d], kf[d], a1);
+    }
+    s0[i] = a0;
+    s1[i] = a1;
+  }
+  // ---- butterfly reduce-scatter over the 8 lanes of the group
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const bool up = j & 4;
+    const float snd0 = up ? s0[r] : s0[r + 4], kp0 = up ? s0[r + 4] : s0[r];
+    const float snd1 = up ? s1[r] : s1[r + 4], kp1 = up ? s1[r + 4] : s1[r];
+    s0[r] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 4);
+    s1[r] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 4);
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const bool up = j & 2;
+    const float snd0 = up ? s0[r] : s0[r + 2], kp0 = up ? s0[r + 2] : s0[r];
+    const float snd1 = up ? s1[r] : s1[r + 2], kp1 = up ? s1[r + 2] : s1[r];
+    s0[r] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 2);
+    s1[r] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 2);
+  }
+  {
+    const bool up = j & 1;
+    const float snd0 = up ? s0[0] : s0[1], kp0 = up ? s0[1] : s0[0];
+    const float snd1 = up ? s1[0] : s1[1], kp1 = up ? s1[1] : s1[0];
+    s0[0] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 1);
+    s1[0] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 1);
+  }
+  // lane l now holds the scores of key l of the tile
+  float sc0 = lane < rows ? s0[0] : -INFINITY;
+  float sc1 = lane < rows ? s1[0] : -INFINITY;
+  float mt0 = sc0, mt1 = sc1;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+    mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+  }
+  const float mn0 = fmaxf(m_run[0], mt0), mn1 = fmaxf(m_run[1], mt1);
+  const float al0 = fast_exp2(m_run[0] - mn0), al1 = fast_exp2(m_run[1] - mn1);
+  m_run[0] = mn0;
+  m_run[1] = mn1;
+  const float p0 = fast_exp2(sc0 - mn0), p1 = fast_exp2(sc1 - mn1);
+  l_run[0] = l_run[0] * al0 + p0;
+  l_run[1] = l_run[1] * al1 + p1;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    o[0][e] *= al0;
+    o[1][e] *= al1;
+  }
+  pbuf[0][lane] = p0;
+  pbuf[1][lane] = p1;
+  __syncwarp();
+
+  // ---- P.V: lane owns dims [4*lane, 4*lane+4)
+  int kk = 0;
+  for (; kk + 4 <= rows; kk += 4) {
+    const float4 pa = *reinterpret_cast<const float4 *>(&pbuf[0][kk]);
+    const float4 pb = *reinterpret_cast<const float4 *>(&pbuf[1][kk]);
+    const float pa_[4] = {pa.x, pa.y, pa.z, pa.w};
+    const float pb_[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint2 vr = *reinterpret_cast<const uint2 *>(Vt + (kk + u) * ROW_BYTES + 8 * lane);
+      const float v0 = bf16lo(vr.x), v1 = bf16hi(vr.x), v2 = bf16lo(vr.y), v3 = bf16hi(vr.y);
+      o[0][0] = fmaf(pa_[u], v0, o[0][0]);
+      o[0][1] = fmaf(pa_[u], v1, o[0][1]);
+      o[0][2] = fmaf(pa_[u], v2, o[0][2]);
+      o[0][3] = fmaf(pa_[u], v3, o[0][3]);
+      o[1][0] = fmaf(pb_[u], v0, o[1][0]);
+      o[1][1] = fmaf(pb_[u], v1, o[1][1]);
+      o[1][2] = fmaf(pb_[u], v2, o[1][2]);
+      o[1][3] = fmaf(pb_[u], v3, o[1][3]);
+    }
+  }
+  for (; kk < rows; ++kk) {
+    const float pa = pbuf[0][kk], pb = pbuf[1][kk];
+    const uint2 vr = *reinterpret_cast<const uint2 *>(Vt + kk * ROW_BYTES + 8 * lane);
+    const float v0 = bf16lo(vr.x), v1 = bf16hi(vr.x), v2 = bf16lo(vr.y), v3 = bf16hi(vr.y);
+    o[0][0] = fmaf(pa, v0, o[0][0]);
+    o[0][1] = fmaf(pa, v1, o[0][1]);
+    o[0][2] = fmaf(pa, v2, o[0][2]);
+    o[0][3] = fmaf(pa, v3, o[0][3]);
+    o[1][0] = fmaf(pb, v0, o[1][0]);
+    o[1][1] = fmaf(pb, v1, o[1][1]);
+    o[1][2] = fmaf(pb, v2, o[1][2]);
+    o[1][3] = fmaf(pb, v3, o[1][3]);
+  }
+}
+
 // One CTA's work unit: split `split` of KV head h of sequence b.  Used by
 // decode_kernel (one unit per CTA) and by the persistent decode-step kernel
 // (decode_step.cuh), which calls it with the unit it owns in that phase.
@@ -219,131 +347,13 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const int g = lane >> 3, j = lane & 7;
-    // q for both heads, dims [8j, 8j+8) and [64+8j, 64+8j+8), pre-scaled.
     float qa[2][16];
-    {
-      const uint16_t *qb = p.q + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        // L2-coherent loads: in the persistent decode step another CTA wrote q
-        // earlier in the same kernel (a line left in this SM's L1 could be stale).
-        const uint4 r0 = __ldcg(reinterpret_cast<const uint4 *>(qb + hh * D + 8 * j));
-        const uint4 r1 = __ldcg(reinterpret_cast<const uint4 *>(qb + hh * D + 64 + 8 * j));
-        unpack8(r0, &qa[hh][0]);
-        unpack8(r1, &qa[hh][8]);
-#pragma unroll
-        for (int d = 0; d < 16; ++d) qa[hh][d] *= p.qscale;
-      }
-    }
+    load_q(p, b, h, lane, qa);
     for (int t = warp, k = 0; t < ntiles; t += NCW, ++k) {
       const int slot = warp * SPW + k % SPW;
       if (!mbar_wait(&s.full[slot], (k / SPW) & 1)) break;
       const int k0 = k_begin + t * TK;
-      const int rows = min(TK, k_end - k0);
-      const uint8_t *Kt = s.k[slot];
-      const uint8_t *Vt = s.v[slot];
-
-      // ---- scores: group g handles keys g*8 .. g*8+7 of the tile
-      float s0[8], s1[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint8_t *row = Kt + (g * 8 + i) * ROW_BYTES;
-        float kf[16];
-        unpack8(*reinterpret_cast<const uint4 *>(row + 16 * j), &kf[0]);
-        unpack8(*reinterpret_cast<const uint4 *>(row + 128 + 16 * j), &kf[8]);
-        float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-        for (int d = 0; d < 16; ++d) {
-          a0 = fmaf(qa[0][d], kf[d], a0);
-          a1 = fmaf(qa[1][d], kf[d], a1);
-        }
-        s0[i] = a0;
-        s1[i] = a1;
-      }
-      // ---- butterfly reduce-scatter over the 8 lanes of the group
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const bool up = j & 4;
-        const float snd0 = up ? s0[r] : s0[r + 4], kp0 = up ? s0[r + 4] : s0[r];
-        const float snd1 = up ? s1[r] : s1[r + 4], kp1 = up ? s1[r + 4] : s1[r];
-        s0[r] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 4);
-        s1[r] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 4);
-      }
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const bool up = j & 2;
-        const float snd0 = up ? s0[r] : s0[r + 2], kp0 = up ? s0[r + 2] : s0[r];
-        const float snd1 = up ? s1[r] : s1[r + 2], kp1 = up ? s1[r + 2] : s1[r];
-        s0[r] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 2);
-        s1[r] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 2);
-      }
-      {
-        const bool up = j & 1;
-        const float snd0 = up ? s0[0] : s0[1], kp0 = up ? s0[1] : s0[0];
-        const float snd1 = up ? s1[0] : s1[1], kp1 = up ? s1[1] : s1[0];
-        s0[0] = kp0 + __shfl_xor_sync(0xffffffffu, snd0, 1);
-        s1[0] = kp1 + __shfl_xor_sync(0xffffffffu, snd1, 1);
-      }
-      // lane l now holds the scores of key l of the tile
-      float sc0 = lane < rows ? s0[0] : -INFINITY;
-      float sc1 = lane < rows ? s1[0] : -INFINITY;
-      float mt0 = sc0, mt1 = sc1;
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
-        mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
-      }
-      const float mn0 = fmaxf(m_run[0], mt0), mn1 = fmaxf(m_run[1], mt1);
-      const float al0 = fast_exp2(m_run[0] - mn0), al1 = fast_exp2(m_run[1] - mn1);
-      m_run[0] = mn0;
-      m_run[1] = mn1;
-      const float p0 = fast_exp2(sc0 - mn0), p1 = fast_exp2(sc1 - mn1);
-      l_run[0] = l_run[0] * al0 + p0;
-      l_run[1] = l_run[1] * al1 + p1;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        o[0][e] *= al0;
-        o[1][e] *= al1;
-      }
-      s.p[warp][0][lane] = p0;
-      s.p[warp][1][lane] = p1;
-      __syncwarp();
-
-      // ---- P.V: lane owns dims [4*lane, 4*lane+4)
-      int kk = 0;
-      for (; kk + 4 <= rows; kk += 4) {
-        const float4 pa = *reinterpret_cast<const float4 *>(&s.p[warp][0][kk]);
-        const float4 pb = *reinterpret_cast<const float4 *>(&s.p[warp][1][kk]);
-        const float pa_[4] = {pa.x, pa.y, pa.z, pa.w};
-        const float pb_[4] = {pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint2 vr = *reinterpret_cast<const uint2 *>(Vt + (kk + u) * ROW_BYTES + 8 * lane);
-          const float v0 = bf16lo(vr.x), v1 = bf16hi(vr.x), v2 = bf16lo(vr.y), v3 = bf16hi(vr.y);
-          o[0][0] = fmaf(pa_[u], v0, o[0][0]);
-          o[0][1] = fmaf(pa_[u], v1, o[0][1]);
-          o[0][2] = fmaf(pa_[u], v2, o[0][2]);
-          o[0][3] = fmaf(pa_[u], v3, o[0][3]);
-          o[1][0] = fmaf(pb_[u], v0, o[1][0]);
-          o[1][1] = fmaf(pb_[u], v1, o[1][1]);
-          o[1][2] = fmaf(pb_[u], v2, o[1][2]);
-          o[1][3] = fmaf(pb_[u], v3, o[1][3]);
-        }
-      }
-      for (; kk < rows; ++kk) {
-        const float pa = s.p[warp][0][kk], pb = s.p[warp][1][kk];
-        const uint2 vr = *reinterpret_cast<const uint2 *>(Vt + kk * ROW_BYTES + 8 * lane);
-        const float v0 = bf16lo(vr.x), v1 = bf16hi(vr.x), v2 = bf16lo(vr.y), v3 = bf16hi(vr.y);
-        o[0][0] = fmaf(pa, v0, o[0][0]);
-        o[0][1] = fmaf(pa, v1, o[0][1]);
-        o[0][2] = fmaf(pa, v2, o[0][2]);
-        o[0][3] = fmaf(pa, v3, o[0][3]);
-        o[1][0] = fmaf(pb, v0, o[1][0]);
-        o[1][1] = fmaf(pb, v1, o[1][1]);
-        o[1][2] = fmaf(pb, v2, o[1][2]);
-        o[1][3] = fmaf(pb, v3, o[1][3]);
-      }
+      consume_tile(s.k[slot], s.v[slot], s.p[warp], lane, min(TK, k_end - k0), qa, m_run, l_run, o);
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.empty[slot]);
     }

@@ -12,6 +12,7 @@
 #include "decode_attention.cuh"
 #include "decode_step.cuh"
 #include "prefill_attention.cuh"
+#include "decode_streamk.cuh"
 #include "model_kernels.cuh"
 #include "qk_norm_rope.cuh"
 
@@ -19,9 +20,19 @@
 #ifndef RIB_DECODE_MAX_CHUNK
 #define RIB_DECODE_MAX_CHUNK 4096
 #endif
+// Fewest waves of decode CTAs a launch is split into (a build-time tuning constant).
+#ifndef RIB_DECODE_MIN_WAVES
+#define RIB_DECODE_MIN_WAVES 1
+#endif
 // Decode CTAs per SM that one wave of splits aims to fill (a build-time tuning constant).
 #ifndef RIB_DECODE_SLOTS_PER_SM
 #define RIB_DECODE_SLOTS_PER_SM 2
+#endif
+// Decode kernel choice: 0 the fixed-split kernel always, 1 the stream-K
+// kernel (decode_streamk.cuh) where use_streamk() finds it faster, 2 stream-K
+// for every launch of at most kStreamMaxSeqs sequences.
+#ifndef RIB_DECODE_STREAMK
+#define RIB_DECODE_STREAMK 1
 #endif
 
 namespace {
@@ -151,6 +162,7 @@ int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offs
 
 // ------------------------------------------------------------------ decode
 struct DecodeGeometry {
+  bool streamk;   // stream-K kernel: max_splits = segments per unit, grid = one wave
   int chunk;
   int max_splits;
   size_t counters_bytes, ml_bytes, o_bytes, total;
@@ -165,9 +177,49 @@ struct DecodeGeometry {
 constexpr size_t kCounterRegionBytes = 16384;
 constexpr size_t kCounterRegionUnits = kCounterRegionBytes / sizeof(int) - 1;
 
-DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
+DecodeGeometry split_geometry(int batch, int max_n, int nkv);
+
+// Whether a decode launch runs the stream-K kernel.  Measured on B200
+// (28-layer batches, 1-8 KV heads, 1-32k keys, ragged batches of 64 and 200
+// sequences): stream-K is faster when the split kernel would run more than
+// one wave of short splits (under 96 tiles), as for one-head shards at 32k
+// (+8 %), 4k contexts (+22 %) and ragged batches of 512-4096 keys (+6 %);
+// the split kernel is faster when its grid is a single wave (one long
+// sequence), when its splits are long (2-8 heads at 32k), and when units are
+// short (at most 1024 keys: segments cost more than they stream).
+bool use_streamk(int batch, int max_n, int nkv) {
+  using namespace rib::decode;
+  const int wave = RIB_DECODE_SLOTS_PER_SM * sm_count();
+  if (!RIB_DECODE_STREAMK || batch > kStreamMaxSeqs || wave + 1 > kStreamMaxSegs) return false;
+  if (RIB_DECODE_STREAMK == 2) return true;  // build-time override: every launch that fits
+  if (max_n <= 1024) return false;
+  const DecodeGeometry sg = split_geometry(batch, max_n, nkv);
+  const long long split_ctas = static_cast<long long>(batch) * nkv * sg.max_splits;
+  return sg.chunk < 96 * TK && split_ctas > wave;
+}
+
+DecodeGeometry decode_geometry(int batch, int max_n, int nkv, bool streamk) {
+  using namespace rib::decode;
+  if (!streamk) return split_geometry(batch, max_n, nkv);
+  DecodeGeometry g;
+  g.streamk = true;
+  // A unit spans at most one CTA per kStreamMinTiles tiles plus one, and
+  // never more CTAs than one wave holds (plus one).
+  g.chunk = 0;
+  g.max_splits = std::min(stream_max_segments(max_n), RIB_DECODE_SLOTS_PER_SM * sm_count() + 1);
+  const size_t units = static_cast<size_t>(batch) * nkv;
+  g.clear_counters = units > kCounterRegionUnits;
+  g.counters_bytes = g.clear_counters ? (((units + 1) * sizeof(int) + 255) / 256) * 256 : kCounterRegionBytes;
+  g.ml_bytes = ((units * g.max_splits * 2 * 2 * sizeof(float) + 255) / 256) * 256;
+  g.o_bytes = units * g.max_splits * 2 * D * sizeof(float);
+  g.total = g.counters_bytes + g.ml_bytes + g.o_bytes;
+  return g;
+}
+
+DecodeGeometry split_geometry(int batch, int max_n, int nkv) {
   using namespace rib::decode;
   DecodeGeometry g;
+  g.streamk = false;
   // Split count: start from the larger of "chunks of at most
   // RIB_DECODE_MAX_CHUNK keys" and
   // "at least one full wave of 2 CTAs per SM", then take the smallest count
@@ -177,7 +229,7 @@ DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
   const long long slots = static_cast<long long>(RIB_DECODE_SLOTS_PER_SM) * sm_count();
   const long long n_units = static_cast<long long>(batch) * nkv;
   const int lo = std::max(ceil_div(max_n, RIB_DECODE_MAX_CHUNK),
-                          std::min(ceil_div(slots, n_units), ceil_div(max_n, TK)));
+                          std::min(ceil_div(RIB_DECODE_MIN_WAVES * slots, n_units), ceil_div(max_n, TK)));
   const int hi = std::max(lo, std::min(2 * lo, ceil_div(max_n, TK)));
   int best_chunk = ceil_div(ceil_div(max_n, lo), TK) * TK;
   double best_eff = -1.0;
@@ -205,12 +257,15 @@ DecodeGeometry decode_geometry(int batch, int max_n, int nkv) {
 }
 
 bool g_decode_smem_done[kMaxDevices];
+bool g_streamk_smem_done[kMaxDevices];
 
+// allow_streamk: false for callers whose scratch is sized for the split
+// kernel (the no-allocation entry point).
 int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, size_t workspace_bytes,
-                  void *stream) {
+                  void *stream, bool allow_streamk = true) {
   using namespace rib::decode;
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
-  const DecodeGeometry g = decode_geometry(batch, max_n, p.nkv);
+  const DecodeGeometry g = decode_geometry(batch, max_n, p.nkv, allow_streamk && use_streamk(batch, max_n, p.nkv));
   if (!workspace || workspace_bytes < g.total) return RIB_EINVAL;
   if (!aligned16(workspace)) return RIB_EALIGN;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -228,6 +283,14 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   p.chunk = g.chunk;
   p.max_splits = g.max_splits;
   p.max_n = max_n;
+  if (g.streamk) {
+    const int smem = static_cast<int>(sizeof(StreamSmem)) + 128;
+    if (!set_smem_once(decode_streamk_kernel, smem, g_streamk_smem_done))
+      return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(decode stream-K smem)", 0);
+    return launch_pdl("decode_streamk_kernel launch", decode_streamk_kernel,
+                      dim3(RIB_DECODE_SLOTS_PER_SM * sm_count()), dim3(NTHREADS), smem,
+                      static_cast<cudaStream_t>(stream), p, batch);
+  }
   const int smem = static_cast<int>(sizeof(Smem)) + 128;
   if (!set_smem_once(decode_kernel, smem, g_decode_smem_done))
     return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(decode smem)", 0);
@@ -306,7 +369,7 @@ struct StepLayout {
 
 StepLayout step_layout(const rib_qwen3_model *m, int cap) {
   StepLayout l;
-  l.g = decode_geometry(1, cap, m->num_kv_heads);
+  l.g = split_geometry(1, cap, m->num_kv_heads);
   size_t off = kCounterRegionBytes;  // decode split counters (fixed region)
   l.sync_off = off;
   off += round256(sizeof(rib::step::Sync));
@@ -421,7 +484,7 @@ int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw, const void *
 
 size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv) {
   if (batch < 1 || max_n < 1 || nkv < 1) return 0;
-  return decode_geometry(batch, max_n, nkv).total;
+  return decode_geometry(batch, max_n, nkv, use_streamk(batch, max_n, nkv)).total;
 }
 
 int rib_decode_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
@@ -460,7 +523,7 @@ int rib_decode_attention_noalloc(const void *q, const void *cache, int cap, int 
   if (n > cap) return RIB_ECAPACITY;
   if (!aligned16(q) || !aligned16(cache) || !aligned16(out)) return RIB_EALIGN;
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
-  const DecodeGeometry g = decode_geometry(1, n, nkv);
+  const DecodeGeometry g = split_geometry(1, n, nkv);
   if (g.total > kNoAllocScratchBytes) {
     snprintf(rib::g_last_error, sizeof(rib::g_last_error),
              "rib_decode_attention_noalloc: n=%d with %d KV heads needs %zu bytes of scratch, "
@@ -483,7 +546,7 @@ int rib_decode_attention_noalloc(const void *q, const void *cache, int cap, int 
   p.nkv = nkv;
   p.qscale = scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t *>(out);
-  return decode_launch(p, 1, n, scratch, kNoAllocScratchBytes, stream);
+  return decode_launch(p, 1, n, scratch, kNoAllocScratchBytes, stream, false);
 }
 
 size_t rib_peer_buffer_bytes(int batch, int nq_total) {

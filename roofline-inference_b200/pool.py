@@ -42,7 +42,8 @@ class KVPool:
         self.row_elems = n_layers * 2 * n_kv * head_dim
         self.arena = torch.zeros(self.pages * PAGE_ROWS * self.row_elems, dtype=dtype, device=device)
         self._free: list[tuple[int, int]] = [(0, self.pages)]     # (start page, pages), sorted by start
-        self._used: dict[int, tuple[int, int]] = {}                # id(cache) -> (start page, pages)
+        self._used: dict[int, tuple[int, int]] = {}                # block token -> (start page, pages)
+        self._next_token = 1
 
     @classmethod
     def for_engine(cls, engine, rows: int) -> "KVPool":
@@ -78,13 +79,16 @@ class KVPool:
         a = start * PAGE_ROWS * self.row_elems
         view = self.arena[a:a + rows * self.row_elems].view(self.n_layers, 2, self.n_kv, rows, self.head_dim)
         cache = Cache.over(view)
-        self._used[id(cache)] = (start, need)
+        cache.pool_token = (id(self), self._next_token)
+        self._used[self._next_token] = (start, need)
+        self._next_token += 1
         return cache
 
     def free(self, cache: Cache) -> None:
         """Returns the cache's block to the pool; the cache must not be used
         afterwards."""
-        blk = self._used.pop(id(cache), None)
+        token = getattr(cache, "pool_token", None)
+        blk = self._used.pop(token[1], None) if token and token[0] == id(self) else None
         if blk is None:
             raise ValueError("cache was not allocated from this pool (or was freed already)")
         start, n = blk

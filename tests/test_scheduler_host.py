@@ -83,7 +83,9 @@ class FakeEngine:
         if cache.offset + n > cache.capacity:
             raise ValueError("KV capacity exceeded")
         self.calls.append(n)
-        self.seen.setdefault(id(cache), []).extend(toks.tolist())
+        if cache.offset == 0:               # a new request (a freed cache's id can come back)
+            self.seen[id(cache)] = []
+        self.seen[id(cache)].extend(toks.tolist())
         cache.offset += n
         if not last:
             return None
