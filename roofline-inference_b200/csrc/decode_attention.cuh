@@ -55,6 +55,7 @@ struct Smem {
   float red_l[NCW][2];
   float merge_m[2][kMergeSplits];
   float merge_l[2][kMergeSplits];
+  alignas(16) uint16_t ostage[2 * D];  // a finished unit's BF16 outputs (NVLink gather)
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   int is_last;
@@ -101,7 +102,7 @@ struct Params {
 // until every peer's epoch has arrived, so when the kernel ends this rank's
 // buffer holds the outputs of all ranks.
 __device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int tid,
-                                              const float (&res)[2], int &flag) {
+                                              const float (&res)[2], int &flag, uint16_t *ostage) {
   if (p.world == 0) {
     if (tid < D) {
       uint16_t *outp = p.out + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
@@ -114,21 +115,33 @@ __device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int
   // region chosen by the epoch read from the device)
   const unsigned long long epoch = p.epoch_dev ? __ldcg(p.epoch_dev) + 1 : p.epoch;
   const size_t region = p.epoch_dev ? (epoch & 1ull) * p.region_elems : 0;
+  // Both heads' 512 bytes go to every rank as 16-byte stores (32 per rank),
+  // not one 2-byte NVLink write per element.
   if (tid < D) {
-    const size_t row = static_cast<size_t>(b) * p.nq_total + p.rank * p.nq + 2 * h;
-    for (int r = 0; r < p.world; ++r) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh)
-        p.gout[r][region + (row + hh) * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(res[hh]));
-    }
-    __threadfence_system();
+    for (int hh = 0; hh < 2; ++hh) ostage[hh * D + tid] = __bfloat16_as_ushort(__float2bfloat16_rn(res[hh]));
   }
   __syncthreads();
-  if (tid == 0) flag = (atomicAdd(p.done, 1) == p.total_units - 1);
+  {
+    const size_t row = static_cast<size_t>(b) * p.nq_total + p.rank * p.nq + 2 * h;
+    for (int k = tid; k < p.world * 32; k += NTHREADS) {
+      const int r = k >> 5, i = k & 31;
+      *reinterpret_cast<uint4 *>(p.gout[r] + region + row * D + 8 * i) =
+          *reinterpret_cast<const uint4 *>(ostage + 8 * i);
+    }
+  }
+  __syncthreads();
+  // One system-scope fence after the barrier orders every thread's peer
+  // stores (fences are cumulative over what the barrier ordered before them).
+  if (tid == 0) {
+    __threadfence_system();
+    flag = (atomicAdd(p.done, 1) == p.total_units - 1);
+  }
   __syncthreads();
   if (!flag) return;
   // last unit of this rank: signal every peer, then wait for every peer
-  __threadfence_system();
+  if (tid == 0) __threadfence_system();
+  __syncthreads();
   if (tid < p.world) st_release_sys(p.gsig[tid] + p.rank, epoch);
   if (tid < p.world) {
     const unsigned long long *slot = p.gsig[p.rank] + tid;
@@ -401,7 +414,7 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) res[hh] = Ox[hh] / Lx[hh];
     }
-    finalize_unit(p, b, h, tid, res, s.is_last);
+    finalize_unit(p, b, h, tid, res, s.is_last, s.ostage);
     return;
   }
   const size_t unit = static_cast<size_t>(b) * p.nkv + h;
@@ -469,7 +482,7 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
   }
   if (tid == 0) p.counters[unit] = 0;  // leave the workspace ready for the next call
   __syncthreads();
-  finalize_unit(p, b, h, tid, res, s.is_last);
+  finalize_unit(p, b, h, tid, res, s.is_last, s.ostage);
 }
 
 __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_constant__ Params p) {

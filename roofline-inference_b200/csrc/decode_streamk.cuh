@@ -36,6 +36,7 @@ struct StreamSmem {
   float red_l[NCW][2];
   float merge_m[2][kStreamMaxSegs];
   float merge_l[2][kStreamMaxSegs];
+  alignas(16) uint16_t ostage[2 * D];  // a finished unit's BF16 outputs
   int pre[kStreamMaxSeqs + 1];  // tiles before sequence b, all its heads included
   int scan[NTHREADS];
   uint64_t full[STAGES];
@@ -86,18 +87,24 @@ __device__ __forceinline__ void stream_finalize(const Params &p, StreamSmem &s, 
   const unsigned long long epoch = p.epoch_dev ? __ldcg(p.epoch_dev) + 1 : p.epoch;
   const size_t region = p.epoch_dev ? (epoch & 1ull) * p.region_elems : 0;
   const size_t row = static_cast<size_t>(b) * p.nq_total + p.rank * p.nq + 2 * h;
-  for (int r = 0; r < p.world; ++r)
-    for (int i = ct; i < 2 * D; i += NCT)
-      p.gout[r][region + row * D + i] = __bfloat16_as_ushort(__float2bfloat16_rn(s.red_o[0][i >> 7][i & 127]));
-  __threadfence_system();
+  for (int i = ct; i < 2 * D; i += NCT) s.ostage[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s.red_o[0][i >> 7][i & 127]));
   consumer_sync();
-  if (ct == 0) s.is_last = (atomicAdd(p.done, 1) == p.total_units - 1);
+  for (int k = ct; k < p.world * 32; k += NCT) {  // 16-byte NVLink stores, 32 per rank
+    const int r = k >> 5, i = k & 31;
+    *reinterpret_cast<uint4 *>(p.gout[r] + region + row * D + 8 * i) = *reinterpret_cast<const uint4 *>(s.ostage + 8 * i);
+  }
+  consumer_sync();
+  if (ct == 0) {  // one fence after the barrier orders every thread's peer stores
+    __threadfence_system();
+    s.is_last = (atomicAdd(p.done, 1) == p.total_units - 1);
+  }
   consumer_sync();
   const bool last = s.is_last;
   consumer_sync();  // is_last is reused by the next segment
   if (!last) return;
   // last unit of this rank: signal every peer, then wait for every peer
-  __threadfence_system();
+  if (ct == 0) __threadfence_system();
+  consumer_sync();
   if (ct < p.world) st_release_sys(p.gsig[ct] + p.rank, epoch);
   if (ct < p.world) {
     const unsigned long long *slot = p.gsig[p.rank] + ct;
