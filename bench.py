@@ -331,35 +331,33 @@ def run_ours(args):
         gather = importlib.import_module("roofline-inference_b200.nvlink_gather").NVLinkGather(
             N_LAYERS, 2 * w["nkv"], device)
 
-    def step(ev_pair=None):
-        if ev_pair is not None:
-            ev_pair[0].record(stream)
+    def step():
         if gather is not None:
             gather.decode(w["q"], plan.ptrs, plan.lens, w["n"], w["cap"], plan.scale, plan.ws)
         else:
             plan.launch()
-        if ev_pair is not None:
-            ev_pair[1].record(stream)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier(world)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         barrier(world)
         start.record(stream)
-        for k in range(args.steps):
-            step(ev[k])
+        for _ in range(args.steps):
+            step()
         end.record(stream)
         torch.cuda.synchronize()
         barrier(world)
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world, device)
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    # Each step is exactly one launch of the decode kernel, so the average
+    # launch duration is this rank's timed region over K.  (Events recorded
+    # between the launches would split the programmatic-dependent-launch
+    # chain and time the gaps they cause, not the kernel.)
+    launch_ms = ms_local
     bytes_step_total = N_LAYERS * 4096 * w["n"]          # all ranks
     bytes_launch_local = N_LAYERS * 2 * w["nkv"] * 128 * 2 * w["n"]
     value = bytes_step_total / (ms * 1e-3) / 1e9
