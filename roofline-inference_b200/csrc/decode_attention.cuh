@@ -53,9 +53,12 @@ struct Smem {
   alignas(16) float red_o[NCW][2][D];
   float red_m[NCW][2];
   float red_l[NCW][2];
-  float merge_m[2][kMergeSplits];
+  // merge_m also stages a finished unit's BF16 outputs for the NVLink gather
+  // (free by then).  No other buffer fits: with 2 CTAs per SM, the 8.8 KB an
+  // SM has left must still hold a GEMV CTA of the next kernel (its input
+  // vector), which then starts its weight prefetch beside the decode tail.
+  alignas(16) float merge_m[2][kMergeSplits];
   float merge_l[2][kMergeSplits];
-  alignas(16) uint16_t ostage[2 * D];  // a finished unit's BF16 outputs (NVLink gather)
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   int is_last;
@@ -76,6 +79,8 @@ struct Params {
   float *part_ml;              // [B][nkv][max_splits][2][2]  (m, l)
   float *part_o;               // [B][nkv][max_splits][2][128]
   int *counters;               // [B][nkv]
+  int *gcounters;              // [B][nkv][max_groups] first-level merge groups
+  int max_groups;              // ceil(max_splits / kMergeGroup)
   const int32_t *caps;         // [B] per-sequence capacities (rows per head), or null: cap
   // All-gather over NVLink (world > 0): the outputs of this rank's heads go
   // straight into every rank's gathered buffer instead of `out`.
@@ -302,6 +307,46 @@ __device__ __forceinline__ void consume_tile(const uint8_t *Kt, const uint8_t *V
   }
 }
 
+constexpr int kMergeGroup = 16;  // splits per first-level merge group
+#ifndef RIB_DECODE_TWO_LEVEL_ABOVE
+#define RIB_DECODE_TWO_LEVEL_ABOVE 64  // splits above which the merge takes two levels (build-time tuning)
+#endif
+
+// Merges `count` partials (m, l, o) of `unit` held at split slots first,
+// first + stride, ...: per head the largest m (M), and l and o weighted by
+// exp2(m - M), summed (L, O); thread tid < D computes dim tid.  The (m, l)
+// pairs are staged in shared memory by parallel loads (count <=
+// kMergeSplits); the o loads are issued in independent batches.
+__device__ __forceinline__ void merge_partials(const Params &p, Smem &s, size_t unit, int first, int stride,
+                                               int count, int tid, float (&M)[2], float (&L)[2], float (&O)[2]) {
+  const float *ml = p.part_ml + unit * p.max_splits * 4;  // [split][head][m, l]
+  const float *po = p.part_o + unit * p.max_splits * 2 * D;
+  for (int i = tid; i < 2 * count; i += NTHREADS) {
+    const int k = i >> 1, hh = i & 1;
+    const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + (first + k * stride) * 2 + hh);
+    s.merge_m[hh][k] = v.x;
+    s.merge_l[hh][k] = v.y;
+  }
+  __syncthreads();
+  if (tid < D) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      float m = -INFINITY;
+      for (int k = 0; k < count; ++k) m = fmaxf(m, s.merge_m[hh][k]);
+      float l = 0.f, o = 0.f;
+#pragma unroll 16
+      for (int k = 0; k < count; ++k) {
+        const float f = fast_exp2(s.merge_m[hh][k] - m);
+        l = fmaf(s.merge_l[hh][k], f, l);
+        o = fmaf(__ldcg(&po[((first + k * stride) * 2 + hh) * D + tid]), f, o);
+      }
+      M[hh] = m;
+      L[hh] = l;
+      O[hh] = o;
+    }
+  }
+}
+
 // One CTA's work unit: split `split` of KV head h of sequence b.  Used by
 // decode_kernel (one unit per CTA) and by the persistent decode-step kernel
 // (decode_step.cuh), which calls it with the unit it owns in that phase.
@@ -414,7 +459,7 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) res[hh] = Ox[hh] / Lx[hh];
     }
-    finalize_unit(p, b, h, tid, res, s.is_last, s.ostage);
+    finalize_unit(p, b, h, tid, res, s.is_last, reinterpret_cast<uint16_t *>(&s.merge_m[0][0]));
     return;
   }
   const size_t unit = static_cast<size_t>(b) * p.nkv + h;
@@ -431,58 +476,55 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) {
-    const int prev = atomicAdd(&p.counters[unit], 1);
-    s.is_last = (prev == nsplit - 1);
-  }
-  __syncthreads();
-  if (!s.is_last) return;
-  __threadfence();
-  // Merge the splits.  The (m, l) pairs of all splits are staged in shared
-  // memory by parallel loads; each thread then weighs its dimension of every
-  // split's partial o with loads issued in independent batches.
-  const float *ml = p.part_ml + unit * p.max_splits * 4;  // [split][head][m, l]
-  const float *po = p.part_o + unit * p.max_splits * 2 * D;
-  if (nsplit <= kMergeSplits) {
-    for (int i = tid; i < 2 * nsplit; i += NTHREADS) {
-      const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + i);
-      s.merge_m[i & 1][i >> 1] = v.x;
-      s.merge_l[i & 1][i >> 1] = v.y;
-    }
+  // Two-level merge: above RIB_DECODE_TWO_LEVEL_ABOVE splits, the last CTA of
+  // each group of kMergeGroup consecutive splits merges the group into the
+  // slot of its first split, and the last group merges the group results;
+  // one CTA merging hundreds of partials would spend tens of microseconds in
+  // dependent L2 round trips at the end of the launch.  For few splits one
+  // level is faster (the second level adds an atomic round trip).
+  const int ngroups = nsplit > RIB_DECODE_TWO_LEVEL_ABOVE ? (nsplit + kMergeGroup - 1) / kMergeGroup : 1;
+  int first = 0, stride = 1, count = nsplit;
+  if (ngroups > 1) {
+    const int g = split / kMergeGroup, g0 = g * kMergeGroup, gn = min(kMergeGroup, nsplit - g0);
+    int *gc = p.gcounters + unit * p.max_groups + g;
+    if (tid == 0) s.is_last = (atomicAdd(gc, 1) == gn - 1);
     __syncthreads();
+    if (!s.is_last) return;
+    __threadfence();
+    float M[2], L[2], O[2];
+    merge_partials(p, s, unit, g0, 1, gn, tid, M, L, O);
     if (tid < D) {
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        float M = -INFINITY;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, s.merge_m[hh][sp]);
-        float L = 0.f, O = 0.f;
-#pragma unroll 8
-        for (int sp = 0; sp < nsplit; ++sp) {
-          const float f = fast_exp2(s.merge_m[hh][sp] - M);
-          L = fmaf(s.merge_l[hh][sp], f, L);
-          O = fmaf(__ldcg(&po[(sp * 2 + hh) * D + tid]), f, O);
+        const size_t pi = (unit * p.max_splits + g0) * 2 + hh;
+        p.part_o[pi * D + tid] = O[hh];
+        if (tid == 0) {
+          p.part_ml[pi * 2 + 0] = M[hh];
+          p.part_ml[pi * 2 + 1] = L[hh];
         }
-        res[hh] = O / L;
       }
     }
-  } else if (tid < D) {
+    if (tid == 0) *gc = 0;  // leave the workspace ready for the next call
+    __threadfence();
+    __syncthreads();
+    stride = kMergeGroup;
+    count = ngroups;
+  }
+  if (tid == 0) s.is_last = (atomicAdd(&p.counters[unit], 1) == count - 1);
+  __syncthreads();
+  if (!s.is_last) return;
+  __threadfence();
+  {
+    float M[2], L[2], O[2];
+    merge_partials(p, s, unit, first, stride, count, tid, M, L, O);
+    if (tid < D) {
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float M = -INFINITY;
-      for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(&ml[(sp * 2 + hh) * 2]));
-      float L = 0.f, O = 0.f;
-#pragma unroll 8
-      for (int sp = 0; sp < nsplit; ++sp) {
-        const float f = fast_exp2(__ldcg(&ml[(sp * 2 + hh) * 2]) - M);
-        L = fmaf(__ldcg(&ml[(sp * 2 + hh) * 2 + 1]), f, L);
-        O = fmaf(__ldcg(&po[(sp * 2 + hh) * D + tid]), f, O);
-      }
-      res[hh] = O / L;
+      for (int hh = 0; hh < 2; ++hh) res[hh] = O[hh] / L[hh];
     }
   }
   if (tid == 0) p.counters[unit] = 0;  // leave the workspace ready for the next call
   __syncthreads();
-  finalize_unit(p, b, h, tid, res, s.is_last, s.ostage);
+  finalize_unit(p, b, h, tid, res, s.is_last, reinterpret_cast<uint16_t *>(&s.merge_m[0][0]));
 }
 
 __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_constant__ Params p) {

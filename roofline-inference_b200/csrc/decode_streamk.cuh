@@ -34,9 +34,8 @@ struct StreamSmem {
   alignas(16) float red_o[NCW][2][D];  // red_o[0] also holds a finished unit's results
   float red_m[NCW][2];
   float red_l[NCW][2];
-  float merge_m[2][kStreamMaxSegs];
+  alignas(16) float merge_m[2][kStreamMaxSegs];  // also stages a finished unit's BF16 outputs
   float merge_l[2][kStreamMaxSegs];
-  alignas(16) uint16_t ostage[2 * D];  // a finished unit's BF16 outputs
   int pre[kStreamMaxSeqs + 1];  // tiles before sequence b, all its heads included
   int scan[NTHREADS];
   uint64_t full[STAGES];
@@ -87,11 +86,12 @@ __device__ __forceinline__ void stream_finalize(const Params &p, StreamSmem &s, 
   const unsigned long long epoch = p.epoch_dev ? __ldcg(p.epoch_dev) + 1 : p.epoch;
   const size_t region = p.epoch_dev ? (epoch & 1ull) * p.region_elems : 0;
   const size_t row = static_cast<size_t>(b) * p.nq_total + p.rank * p.nq + 2 * h;
-  for (int i = ct; i < 2 * D; i += NCT) s.ostage[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s.red_o[0][i >> 7][i & 127]));
+  uint16_t *ostage = reinterpret_cast<uint16_t *>(&s.merge_m[0][0]);  // free once the unit is merged
+  for (int i = ct; i < 2 * D; i += NCT) ostage[i] = __bfloat16_as_ushort(__float2bfloat16_rn(s.red_o[0][i >> 7][i & 127]));
   consumer_sync();
   for (int k = ct; k < p.world * 32; k += NCT) {  // 16-byte NVLink stores, 32 per rank
     const int r = k >> 5, i = k & 31;
-    *reinterpret_cast<uint4 *>(p.gout[r] + region + row * D + 8 * i) = *reinterpret_cast<const uint4 *>(s.ostage + 8 * i);
+    *reinterpret_cast<uint4 *>(p.gout[r] + region + row * D + 8 * i) = *reinterpret_cast<const uint4 *>(ostage + 8 * i);
   }
   consumer_sync();
   if (ct == 0) {  // one fence after the barrier orders every thread's peer stores

@@ -165,6 +165,7 @@ struct DecodeGeometry {
   bool streamk;   // stream-K kernel: max_splits = segments per unit, grid = one wave
   int chunk;
   int max_splits;
+  int max_groups = 0;  // first-level merge groups per unit (split kernel)
   size_t counters_bytes, ml_bytes, o_bytes, total;
   bool clear_counters;  // counters outside the fixed region: cleared before the launch
 };
@@ -186,16 +187,20 @@ DecodeGeometry split_geometry(int batch, int max_n, int nkv);
 // (+8 %), 4k contexts (+22 %) and ragged batches of 512-4096 keys (+6 %);
 // the split kernel is faster when its grid is a single wave (one long
 // sequence), when its splits are long (2-8 heads at 32k), and when units are
-// short (at most 1024 keys: segments cost more than they stream).
+// short (at most 1024 keys: segments cost more than they stream), and when
+// the launch holds too few tiles for every CTA of the wave to take
+// kStreamMinTiles (a single short sequence).
 bool use_streamk(int batch, int max_n, int nkv) {
   using namespace rib::decode;
   const int wave = RIB_DECODE_SLOTS_PER_SM * sm_count();
   if (!RIB_DECODE_STREAMK || batch > kStreamMaxSeqs || wave + 1 > kStreamMaxSegs) return false;
   if (RIB_DECODE_STREAMK == 2) return true;  // build-time override: every launch that fits
   if (max_n <= 1024) return false;
+  // enough tiles for every CTA of the wave to take its minimum
+  const long long units = static_cast<long long>(batch) * nkv;
+  if (units * ceil_div(max_n, TK) < static_cast<long long>(wave) * kStreamMinTiles) return false;
   const DecodeGeometry sg = split_geometry(batch, max_n, nkv);
-  const long long split_ctas = static_cast<long long>(batch) * nkv * sg.max_splits;
-  return sg.chunk < 96 * TK && split_ctas > wave;
+  return sg.chunk < 96 * TK && units * sg.max_splits > wave;
 }
 
 DecodeGeometry decode_geometry(int batch, int max_n, int nkv, bool streamk) {
@@ -246,10 +251,13 @@ DecodeGeometry split_geometry(int batch, int max_n, int nkv) {
   }
   g.chunk = best_chunk;
   g.max_splits = ceil_div(max_n, best_chunk);
+  g.max_groups = ceil_div(g.max_splits, kMergeGroup);
   const size_t units = static_cast<size_t>(batch) * nkv;
-  // per-unit split counters, then one counter of units finalised (all-gather)
-  g.clear_counters = units > kCounterRegionUnits;
-  g.counters_bytes = g.clear_counters ? (((units + 1) * sizeof(int) + 255) / 256) * 256 : kCounterRegionBytes;
+  // per-unit split counters, one counter of units finalised (all-gather),
+  // then per-unit counters of the first-level merge groups
+  const size_t n_counters = units + 1 + units * g.max_groups;
+  g.clear_counters = n_counters * sizeof(int) > kCounterRegionBytes;
+  g.counters_bytes = g.clear_counters ? ((n_counters * sizeof(int) + 255) / 256) * 256 : kCounterRegionBytes;
   g.ml_bytes = ((units * g.max_splits * 2 * 2 * sizeof(float) + 255) / 256) * 256;
   g.o_bytes = units * g.max_splits * 2 * D * sizeof(float);
   g.total = g.counters_bytes + g.ml_bytes + g.o_bytes;
@@ -278,6 +286,9 @@ int decode_launch(rib::decode::Params p, int batch, int max_n, void *workspace, 
   }
   p.counters = reinterpret_cast<int *>(ws);
   p.done = p.counters + static_cast<size_t>(batch) * p.nkv;
+  p.gcounters = p.done + 1;
+  p.max_groups = g.max_groups;
+  if (!g.streamk && g.max_groups > kMergeSplits) return RIB_EINVAL;  // beyond any cache that fits a GPU
   p.part_ml = reinterpret_cast<float *>(ws + g.counters_bytes);
   p.part_o = reinterpret_cast<float *>(ws + g.counters_bytes + g.ml_bytes);
   p.chunk = g.chunk;
@@ -906,8 +917,11 @@ int rib_qwen3_decode_step(const rib_qwen3_model *m, const uint64_t *cache_ptrs, 
                           int32_t *pos, int32_t *nkeys, float *logits, void *workspace, size_t workspace_bytes,
                           void *stream) {
   if (!step_model_ok(m) || !cache_ptrs || !token || !pos || !nkeys || !workspace || cap < 1) return RIB_EINVAL;
-  if (m->num_kv_heads > static_cast<int>(kCounterRegionUnits)) return RIB_EINVAL;
   const StepLayout lay = step_layout(m, cap);
+  // split counters, the finalised-unit counter and the merge-group counters in the fixed region
+  if ((static_cast<size_t>(m->num_kv_heads) * (1 + lay.g.max_groups) + 1) * sizeof(int) > kCounterRegionBytes ||
+      lay.g.max_groups > rib::decode::kMergeSplits)
+    return RIB_EINVAL;
   if (workspace_bytes < lay.total) return RIB_EINVAL;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) || (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) ||
       (reinterpret_cast<uintptr_t>(token) & 3u) || (reinterpret_cast<uintptr_t>(pos) & 3u) ||
@@ -969,6 +983,8 @@ int rib_qwen3_decode_step(const rib_qwen3_model *m, const uint64_t *cache_ptrs, 
   dp.counters = reinterpret_cast<int *>(ws);
   dp.world = 0;
   dp.done = dp.counters + m->num_kv_heads;
+  dp.gcounters = dp.done + 1;
+  dp.max_groups = lay.g.max_groups;
   dp.total_units = m->num_kv_heads;
   if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
   const cudaStream_t st = static_cast<cudaStream_t>(stream);

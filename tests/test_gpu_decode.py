@@ -159,3 +159,26 @@ def test_decode_workspace_init_repairs_garbage(rib, wl, oracle):
     of, _ = oracle.decode_attention(u16(q), u16(cache), n, wl.SCALE)
     _assert_parity(out, of)
     assert not ws[:16384].any()
+
+
+@pytest.mark.parametrize("nkv,n", [(1, 32769), (2, 32769), (1, 70000), (4, 9000), (1, 600)])
+def test_decode_few_heads_many_splits(rib, wl, oracle, nkv, n):
+    """Few KV heads over long contexts (a KV-head shard of one sequence): one
+    launch cuts each head into tens to hundreds of splits, merged in two
+    levels (groups of 16 splits, then the groups); the counters of both
+    levels are left zero."""
+    cap = wl.round_cap(n)
+    cache = wl.randn_bf16((2, nkv, cap, 128), seed=nkv * 7 + n, device="cuda")
+    q = wl.randn_bf16((2 * nkv, 128), seed=n + nkv, device="cuda")
+    L = rib.load_library()
+    nbytes = L.rib_decode_workspace_bytes(1, n, nkv)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty((2 * nkv, 128), dtype=torch.bfloat16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the second call runs on the counters the first one left
+        assert L.rib_decode_attention(q.data_ptr(), cache.data_ptr(), cap, n, 2 * nkv, nkv, wl.SCALE,
+                                      out.data_ptr(), ws.data_ptr(), nbytes, st) == 0
+    torch.cuda.synchronize()
+    of, _ = oracle.decode_attention(u16(q), u16(cache), n, wl.SCALE)
+    _assert_parity(out, of)
+    assert not ws[:16384].any()
