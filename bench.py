@@ -956,8 +956,10 @@ def run_case(case: str):
     """Bounded workloads for ncu captures: decode-small is the layer-batched
     decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
     prefill-small is causal prefill at L = 16384 (128 MB of Q/K/V, above L2;
-    3 launches); model-decode is the Qwen3-0.6B decode step at context 4096
-    (1.19 GB of weights and 0.47 GB of K/V, above L2): the graph's eager
+    3 launches); decode-4k is the 28-layer sweep at ctx 4096 (470 MB of
+    KV, the stream-K decode kernel; 3 launches); model-decode is the
+    Qwen3-0.6B decode step at context 4096 (1.19 GB of weights and 0.47 GB of
+    K/V, above L2): the graph's eager
     warm-up step and 3 replays of 143 launches each; model-batch is the
     64-sequence ragged batched decode step (contexts U[512, 4096], 17.9 GB
     of K/V): the capture's eager warm-up step and 3 graph replays."""
@@ -965,8 +967,9 @@ def run_case(case: str):
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    if case == "decode-small":
-        w = make_decode_workload(0, 1, device, layers=4)
+    if case in ("decode-small", "decode-4k"):
+        w = make_decode_workload(0, 1, device, layers=4) if case == "decode-small" else \
+            make_decode_workload(0, 1, device, ctx=4096)
         plan = DecodePlan(rib, w, device)
         for _ in range(3):
             plan.launch()
@@ -1009,7 +1012,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "prefill-small", "model-decode", "model-batch"], default=None,
+    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "model-decode", "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()
     if args.case:
