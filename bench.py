@@ -555,8 +555,9 @@ def run_ragged(rib, rank, world, device, args, pk):
 def run_e2e(rib, w, rank, world, device, args, gather, plan):
     """Same sweep through the public API: per step, copy the 28 layers' qkv
     rows of the new token from pinned host memory, run the fused
-    norm + RoPE + append (28 launches, new token at position 32768) and one
-    layer-batched decode, and read the outputs back to pinned host memory."""
+    norm + RoPE + append of all 28 layers (one launch, new token at position
+    32768) and one layer-batched decode, and read the outputs back to pinned
+    host memory."""
     wl = importlib.import_module("roofline-inference_b200.workloads")
     nkv, pos = w["nkv"], w["n"] - 1
     nq = 2 * nkv
@@ -569,15 +570,16 @@ def run_e2e(rib, w, rank, world, device, args, gather, plan):
     kw = wl.norm_weights(2, device)
     qkv_dev = torch.empty((N_LAYERS, width), dtype=torch.bfloat16, device=device)
     lens = torch.full((N_LAYERS,), w["n"], dtype=torch.int32, device=device)
+    pos_dev = torch.full((N_LAYERS,), pos, dtype=torch.int32, device=device)
+    caps = torch.full((N_LAYERS,), w["cap"], dtype=torch.int32, device=device)
     caches = w["caches"]
     stream = torch.cuda.current_stream(device)
-    launches = N_LAYERS + 1
+    launches = 2
 
     def step():
         qkv_dev.copy_(qkv_host, non_blocking=True)
-        qs = [rib.qk_norm_rope_append(qkv_dev[i], qw, kw, pos, nq, nkv, 1e6, caches[i])
-              for i in range(N_LAYERS)]
-        q = torch.stack([x.reshape(nq, 128) for x in qs])
+        # every layer's norm + RoPE + append in one launch (the layers as a batch of caches)
+        q = rib.qk_norm_rope_append_batched(qkv_dev, qw, kw, pos_dev, plan.ptrs, caps, nq, nkv, 1e6)
         if gather is not None:
             full = gather.decode(q, plan.ptrs, lens, w["n"], w["cap"], 128 ** -0.5, plan.ws)
         else:
@@ -600,7 +602,7 @@ def run_e2e(rib, w, rank, world, device, args, gather, plan):
             "h2d_bytes_per_step": qkv_host.numel() * 2,
             "d2h_bytes_per_step": out_host.numel() * 2,
             "gpu_launches_per_step": launches,
-            "path": "qk_norm_rope_append x28 + decode_attention_batched (public API)"
+            "path": "qk_norm_rope_append_batched (28 layers, one launch) + decode_attention_batched (public API)"
                     + ("; NVLinkGather.decode (fused all-gather) at N > 1" if world > 1 else "")}
 
 

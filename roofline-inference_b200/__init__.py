@@ -14,7 +14,8 @@ from . import _lib
 from .attention import attention, decode_attention, decode_attention_batched
 from .cache import Cache
 from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope, qk_norm_rope_append,
-                      qk_norm_rope_append_at, qk_norm_rope_prefill, rms_norm, swiglu)
+                      qk_norm_rope_append_at, qk_norm_rope_append_batched, qk_norm_rope_prefill, rms_norm,
+                      swiglu)
 from .model import QWEN3_0_6B, DecodeGraph, Engine, Qwen3Config, Qwen3Weights, random_weights
 from .batch import BatchDecoder, SlotDecoder, generate_batch
 from .pool import KVPool, PoolFull
@@ -39,6 +40,7 @@ __all__ = [
     "gemv",
     "generate_batch",
     "qk_norm_rope_append_at",
+    "qk_norm_rope_append_batched",
     "random_weights",
     "rms_norm",
     "swiglu",

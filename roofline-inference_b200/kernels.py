@@ -125,6 +125,36 @@ def qk_norm_rope_append_at(qkv, qw, kw, offset_dev, nq: int, nkv: int, base: flo
     return q
 
 
+def qk_norm_rope_append_batched(qkv, qw, kw, pos, cache_ptrs, caps, nq: int, nkv: int, base: float,
+                                out=None):
+    """qk_norm_rope_append of one new token for each of B caches in one launch.
+
+    qkv [B, (nq + 2 nkv) * 128] BF16; pos int32 CUDA [B] (each token's
+    position, the cache row written); cache_ptrs int64 CUDA [B] (device
+    addresses of [2, nkv, caps[b], 128] BF16 caches: sequences of a batch, or
+    the layers of one decode step); caps int32 CUDA [B].  Returns q [B, nq,
+    128].  A position outside [0, caps[b]) writes nothing for that row and is
+    reported by rib_take_device_status (RIB_ECAPACITY)."""
+    require_bf16_cuda("qkv", qkv)
+    require_bf16_cuda("qw", qw)
+    require_bf16_cuda("kw", kw)
+    if qkv.dim() != 2 or qkv.shape[1] != (nq + 2 * nkv) * HEAD_DIM or not qkv.is_contiguous():
+        raise ValueError(f"qkv must be contiguous [B, {(nq + 2 * nkv) * HEAD_DIM}]")
+    B = qkv.shape[0]
+    for name, t, dt in (("pos", pos, torch.int32), ("cache_ptrs", cache_ptrs, torch.int64),
+                        ("caps", caps, torch.int32)):
+        if not isinstance(t, torch.Tensor) or t.dtype != dt or not t.is_cuda or t.numel() != B \
+                or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor of {B} elements")
+        require_same_device(qkv, t)
+    q = _out_or_new(out, (B, nq, HEAD_DIM), torch.bfloat16, qkv.device, "out")
+    st = _lib.load().rib_qk_norm_rope_append_batched(
+        qkv.data_ptr(), qw.data_ptr(), kw.data_ptr(), pos.data_ptr(), cache_ptrs.data_ptr(), caps.data_ptr(), B,
+        nq, nkv, float(base), q.data_ptr(), stream_handle(qkv.device))
+    _lib.check(st, "qk_norm_rope_append_batched")
+    return q
+
+
 # ----------------------------------------------------------------- model ops
 # The remaining operations of the Qwen3 forward (agent-test/v2/engine.py:102-163):
 # fused GEMVs for decode, residual + RMSNorm, RMSNorm, SwiGLU, embedding gather

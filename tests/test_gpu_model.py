@@ -450,3 +450,27 @@ def test_tp_exchange_single_rank(rib):
         x.close()
     finally:
         dist.destroy_process_group()
+
+
+def test_qk_norm_rope_append_batched_matches_per_cache(rib):
+    """The batched append (one launch for B caches of different capacities,
+    each at its own position) writes the same K/V rows and returns the same q
+    as B single-cache appends, bit for bit."""
+    nq, nkv, B = 16, 8, 5
+    g = torch.Generator(device=DEV).manual_seed(3)
+    qkv = (torch.randn((B, (nq + 2 * nkv) * 128), generator=g, device=DEV)).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(128, generator=g, device=DEV)).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(128, generator=g, device=DEV)).to(torch.bfloat16)
+    caps = [256, 512, 256, 768, 1024]
+    positions = [0, 300, 255, 700, 513]
+    ca = [torch.zeros((2, nkv, c, 128), dtype=torch.bfloat16, device=DEV) for c in caps]
+    cb = [torch.zeros_like(c) for c in ca]
+    q = rib.qk_norm_rope_append_batched(
+        qkv, qw, kw, torch.tensor(positions, dtype=torch.int32, device=DEV),
+        torch.tensor([c.data_ptr() for c in ca], dtype=torch.int64, device=DEV),
+        torch.tensor(caps, dtype=torch.int32, device=DEV), nq, nkv, 1e6)
+    for i in range(B):
+        qi = rib.qk_norm_rope_append(qkv[i], qw, kw, positions[i], nq, nkv, 1e6, cb[i])
+        assert torch.equal(q[i], qi.reshape(nq, 128)), i
+        assert torch.equal(ca[i], cb[i]), i
+    assert rib._lib.take_device_status() == 0
