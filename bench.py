@@ -27,7 +27,6 @@ import argparse
 import datetime
 import importlib
 import json
-import math
 import os
 import statistics
 import subprocess

@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from .peer_memory import PeerBuffers
 from ._tensors import require_bf16_cuda, stream_handle
 
 MAX_PEERS = 8
@@ -44,14 +45,6 @@ def _bind(L: ctypes.CDLL) -> None:
     vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
     L.rib_peer_buffer_bytes.argtypes = [i, i]
     L.rib_peer_buffer_bytes.restype = sz
-    L.rib_peer_buffer_alloc.argtypes = [i, sz, ctypes.POINTER(ctypes.c_void_p), vp]
-    L.rib_peer_buffer_alloc.restype = i
-    L.rib_peer_buffer_open.argtypes = [i, vp, ctypes.POINTER(ctypes.c_void_p)]
-    L.rib_peer_buffer_open.restype = i
-    L.rib_peer_buffer_close.argtypes = [i, vp]
-    L.rib_peer_buffer_close.restype = i
-    L.rib_peer_buffer_free.argtypes = [i, vp]
-    L.rib_peer_buffer_free.restype = i
     L.rib_decode_attention_gather.argtypes = [vp, vp, vp, i, i, i, i, i, ctypes.c_float,
                                               ctypes.POINTER(_PeerGatherStruct),
                                               ctypes.c_ulonglong, vp, sz, vp]
@@ -81,24 +74,8 @@ class NVLinkGather:
         self.nq_total = nq_local * self.world
         self.nbytes = self.L.rib_peer_buffer_bytes(batch, self.nq_total)
         self.region_bytes = (self.nbytes - 256) // 2
-        own = ctypes.c_void_p()
-        handle = (ctypes.c_char * 64)()
-        _lib.check(self.L.rib_peer_buffer_alloc(self.dev, self.nbytes, ctypes.byref(own), handle),
-                   "rib_peer_buffer_alloc")
-        handles: list = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.base = [0] * self.world
-        self._opened: list[int] = []
-        for r in range(self.world):
-            if r == self.rank:
-                self.base[r] = own.value
-                continue
-            ptr = ctypes.c_void_p()
-            buf = ctypes.create_string_buffer(handles[r], 64)
-            _lib.check(self.L.rib_peer_buffer_open(self.dev, buf, ctypes.byref(ptr)),
-                       "rib_peer_buffer_open")
-            self.base[r] = ptr.value
-            self._opened.append(ptr.value)
+        self.peers = PeerBuffers(self.nbytes, self.device, group)
+        self.base = self.peers.base
         self.g = _PeerGatherStruct()
         self.g.world, self.g.rank, self.g.region_bytes = self.world, self.rank, self.region_bytes
         for r in range(self.world):
@@ -163,11 +140,6 @@ class NVLinkGather:
         """Collective: unmap the peers' buffers and free this rank's."""
         if self.closed:
             return
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        for ptr in self._opened:
-            self.L.rib_peer_buffer_close(self.dev, ctypes.c_void_p(ptr))
-        dist.barrier(group=self.group)
-        self.L.rib_peer_buffer_free(self.dev, ctypes.c_void_p(self.base[self.rank]))
+        self.peers.close()
         self._views = []
         self.closed = True

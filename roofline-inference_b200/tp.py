@@ -29,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from .peer_memory import PeerBuffers
 
 MAX_RANKS = 8
 EPI_PEER_PARTIAL = 3
@@ -49,14 +50,6 @@ def _bind(L: ctypes.CDLL) -> None:
     L.rib_gemv_tp.restype = i
     L.rib_argmax_f32_tp.argtypes = [vp, i, i, vp, vp, ctypes.POINTER(_TpExchangeStruct), vp]
     L.rib_argmax_f32_tp.restype = i
-    L.rib_peer_buffer_alloc.argtypes = [i, sz, ctypes.POINTER(ctypes.c_void_p), vp]
-    L.rib_peer_buffer_alloc.restype = i
-    L.rib_peer_buffer_open.argtypes = [i, vp, ctypes.POINTER(ctypes.c_void_p)]
-    L.rib_peer_buffer_open.restype = i
-    L.rib_peer_buffer_close.argtypes = [i, vp]
-    L.rib_peer_buffer_close.restype = i
-    L.rib_peer_buffer_free.argtypes = [i, vp]
-    L.rib_peer_buffer_free.restype = i
 
 
 def split_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -100,23 +93,8 @@ class TPExchange:
         self.nbytes = int(L.rib_tp_buffer_bytes(self.world, self.slot))
         if self.nbytes == 0:
             raise ValueError("bad exchange geometry")
-        own = ctypes.c_void_p()
-        handle = (ctypes.c_char * 64)()
-        _lib.check(L.rib_peer_buffer_alloc(self.dev, self.nbytes, ctypes.byref(own), handle),
-                   "rib_peer_buffer_alloc")
-        handles: list = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.base = [0] * self.world
-        self._opened: list[int] = []
-        for r in range(self.world):
-            if r == self.rank:
-                self.base[r] = own.value
-                continue
-            ptr = ctypes.c_void_p()
-            buf = ctypes.create_string_buffer(handles[r], 64)
-            _lib.check(L.rib_peer_buffer_open(self.dev, buf, ctypes.byref(ptr)), "rib_peer_buffer_open")
-            self.base[r] = ptr.value
-            self._opened.append(ptr.value)
+        self.peers = PeerBuffers(self.nbytes, self.device, group)
+        self.base = self.peers.base
         self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
         s = _TpExchangeStruct()
@@ -154,10 +132,5 @@ class TPExchange:
         """Collective: unmap the peers' buffers and free this rank's."""
         if self.closed:
             return
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        for ptr in self._opened:
-            self.L.rib_peer_buffer_close(self.dev, ctypes.c_void_p(ptr))
-        dist.barrier(group=self.group)
-        self.L.rib_peer_buffer_free(self.dev, ctypes.c_void_p(self.base[self.rank]))
+        self.peers.close()
         self.closed = True
