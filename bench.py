@@ -961,7 +961,8 @@ def run_case(case: str):
     KV, the stream-K decode kernel; 3 launches); model-decode is the
     Qwen3-0.6B decode step at context 4096 (1.19 GB of weights and 0.47 GB of
     K/V, above L2): the graph's eager
-    warm-up step and 3 replays of 143 launches each; model-batch is the
+    warm-up step and 3 replays of 143 launches each (the append fused into
+    the decode attention launch); model-batch is the
     64-sequence ragged batched decode step (contexts U[512, 4096], 17.9 GB
     of K/V): the capture's eager warm-up step and 3 graph replays."""
     rib = load_rib()

@@ -402,6 +402,22 @@ int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw,
                                     int nkv, double base, void *q_out,
                                     void *stream);
 
+/* Decode attention with the new token's norm + RoPE + append fused in: as
+ * rib_decode_attention_batched (uniform capacity cap, lens[b] keys of
+ * sequence b), but q is formed inside the kernel from the token's projection
+ * qkv [B, (nq + 2 nkv) * 128] (per-head RMSNorm with qw / kw, RoPE at
+ * position lens[b] - 1 with base `base`), and the token's K and V rows are
+ * written into the cache at that position first.  Outputs and cache rows are
+ * bit-identical to rib_qk_norm_rope_append_batched followed by
+ * rib_decode_attention_batched; one launch and one dependency fewer per
+ * layer (agent-test/v2/engine.py:150-155 in one kernel). */
+int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw,
+                             double base, const uint64_t *cache_ptrs,
+                             const int32_t *lens, int batch, int max_n, int cap,
+                             int nq, int nkv, float scale, void *out,
+                             void *workspace, size_t workspace_bytes,
+                             void *stream);
+
 /* Greedy token of each row of x [rows, n] FP32 (the first index on ties). */
 int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out,
                         void *stream);

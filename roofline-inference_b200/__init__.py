@@ -11,7 +11,7 @@ The directory name contains a hyphen, so it is imported with importlib:
     rib = importlib.import_module("roofline-inference_b200")
 """
 from . import _lib
-from .attention import attention, decode_attention, decode_attention_batched
+from .attention import attention, decode_attention, decode_attention_batched, decode_attention_qkv
 from .cache import Cache
 from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope, qk_norm_rope_append,
                       qk_norm_rope_append_at, qk_norm_rope_append_batched, qk_norm_rope_prefill, rms_norm,
@@ -47,6 +47,7 @@ __all__ = [
     "attention",
     "decode_attention",
     "decode_attention_batched",
+    "decode_attention_qkv",
     "qk_norm_rope",
     "qk_norm_rope_append",
     "qk_norm_rope_prefill",

@@ -121,6 +121,7 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_decode_attention_ragged": ([vp, vp, vp, vp, i, i, i, i, f, vp, vp, sz, vp], i),
         "rib_qk_norm_rope_append_batched": ([vp, vp, vp, vp, vp, vp, i, i, i, d, vp, vp], i),
         "rib_argmax_rows_f32": ([vp, i, i, vp, vp], i),
+        "rib_decode_attention_qkv": ([vp, vp, vp, d, vp, vp, i, i, i, i, i, f, vp, vp, sz, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -130,6 +130,63 @@ def decode_attention_batched(q, caches, lens, scale: float, max_n: int | None = 
     return out
 
 
+def decode_attention_qkv(qkv, qw, kw, base: float, caches, lens, scale: float, max_n: int | None = None):
+    """One decode step of B sequences with the new token's norm + RoPE +
+    append fused into the attention launch (engine.py:150-155 in one kernel).
+
+    qkv: [B, (nq + 2 nkv) * 128] projections of the new tokens; qw, kw: the
+    per-head norm weights; caches as decode_attention_batched (the token of
+    sequence b is appended at row lens[b] - 1, then attends over lens[b]
+    keys).  Returns [B, nq, 128] BF16; outputs and cache rows equal
+    qk_norm_rope_append followed by decode_attention_batched, bit for bit."""
+    require_bf16_cuda("qkv", qkv)
+    require_bf16_cuda("qw", qw)
+    require_bf16_cuda("kw", kw)
+    if qkv.dim() != 2 or not qkv.is_contiguous():
+        raise ValueError(f"qkv must be contiguous [B, (nq + 2 nkv) * 128], got {tuple(qkv.shape)}")
+    B, dev = qkv.shape[0], qkv.device
+    if isinstance(caches, torch.Tensor):
+        require_bf16_cuda("caches", caches)
+        if caches.dim() != 5 or caches.shape[0] != B or caches.shape[1] != 2:
+            raise ValueError(f"caches must be [B, 2, nkv, cap, 128], got {tuple(caches.shape)}")
+        nkv, cap = caches.shape[2], caches.shape[3]
+        stride = caches[0].numel() * caches.element_size()
+        ptrs = torch.tensor([caches.data_ptr() + b * stride for b in range(B)], dtype=torch.int64)
+    else:
+        if len(caches) != B:
+            raise ValueError("need one cache per sequence")
+        nkv, cap = caches[0].shape[1], caches[0].shape[2]
+        for c in caches:
+            require_bf16_cuda("cache", c)
+            require_same_device(qkv, c)
+            if tuple(c.shape) != (2, nkv, cap, HEAD_DIM):
+                raise ValueError("every cache must be [2, nkv, cap, 128] with the same nkv and cap")
+        ptrs = torch.tensor([c.data_ptr() for c in caches], dtype=torch.int64)
+    nq = 2 * nkv
+    if qkv.shape[1] != (nq + 2 * nkv) * HEAD_DIM:
+        raise ValueError(f"qkv rows must hold {(nq + 2 * nkv) * HEAD_DIM} values for {nkv} KV heads")
+    ptrs = ptrs.to(dev, non_blocking=True)
+    if isinstance(lens, torch.Tensor):
+        lens_d = lens.to(device=dev, dtype=torch.int32)
+        if max_n is None:
+            max_n = int(lens_d.max().item())
+    else:
+        if max_n is None:
+            max_n = max(int(x) for x in lens)
+        lens_d = torch.tensor([int(x) for x in lens], dtype=torch.int32).to(dev, non_blocking=True)
+    if max_n > cap:
+        raise ValueError("KV capacity exceeded")
+    L = _lib.load()
+    out = torch.empty((B, nq, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        ws = decode_workspace(dev, L.rib_decode_workspace_bytes(B, max(int(max_n), 1), nkv))
+        st = L.rib_decode_attention_qkv(qkv.data_ptr(), qw.data_ptr(), kw.data_ptr(), float(base), ptrs.data_ptr(),
+                                        lens_d.data_ptr(), B, int(max_n), cap, nq, nkv, float(scale),
+                                        out.data_ptr(), ws.data_ptr(), ws.numel(), stream_handle(dev))
+    _lib.check(st, "decode_attention_qkv")
+    return out
+
+
 # --------------------------------------------------------------- prefill
 def attention(Q, K, V, qL: int, kL: int, scale: float, nsg=4, bk=16, kt=False, vf32=False,
               skip=True):

@@ -30,6 +30,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "qk_norm_rope.cuh"
 
 namespace rib {
 namespace decode {
@@ -97,6 +98,14 @@ struct Params {
   unsigned long long *epoch_dev;
   size_t region_elems;
   uint16_t *gcopy;
+  // Fused norm + RoPE + append (qkv set): q is not read from `q` but formed
+  // in each CTA from the new token's projection qkv [B][(nq + 2 nkv) * 128]
+  // (per-head RMSNorm with qw, RoPE at position lens[b] - 1), and the CTA
+  // whose split holds that position writes the token's K and V rows into the
+  // cache first -- the arithmetic of rope::qk_norm_rope_kernel, bit for bit.
+  const uint16_t *qkv;
+  const uint16_t *qw, *kw;
+  double inv_freq[64];  // base^(-d/64)
 };
 
 
@@ -347,6 +356,19 @@ __device__ __forceinline__ void merge_partials(const Params &p, Smem &s, size_t 
   }
 }
 
+// q of a CTA's two query heads from shared memory (staged by the fused
+// norm + RoPE prologue), with the lane layout and scaling of load_q.
+__device__ __forceinline__ void load_q_staged(const uint16_t *qs, float qscale, int lane, float (&qa)[2][16]) {
+  const int j = lane & 7;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    unpack8(*reinterpret_cast<const uint4 *>(qs + hh * D + 8 * j), &qa[hh][0]);
+    unpack8(*reinterpret_cast<const uint4 *>(qs + hh * D + 64 + 8 * j), &qa[hh][8]);
+#pragma unroll
+    for (int d = 0; d < 16; ++d) qa[hh][d] *= qscale;
+  }
+}
+
 // One CTA's work unit: split `split` of KV head h of sequence b.  Used by
 // decode_kernel (one unit per CTA) and by the persistent decode-step kernel
 // (decode_step.cuh), which calls it with the unit it owns in that phase.
@@ -382,6 +404,27 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
     }
     fence_mbar_init();
   }
+  // Fused prologue: the merge buffers are free until the merge, so they hold
+  // the RoPE angles and the staged q meanwhile.
+  float *cos_t = &s.merge_m[0][0], *sin_t = &s.merge_m[0][64];
+  uint16_t *qstage = reinterpret_cast<uint16_t *>(&s.merge_m[1][0]);
+  if (p.qkv) {
+    rope::rope_angles(n - 1, p.inv_freq, cos_t, sin_t, tid);
+    __syncthreads();
+    const int j = lane & 15, half = lane >> 4;
+    const unsigned half_mask = 0xffffu << (lane & 16);
+    const uint16_t *row = p.qkv + static_cast<size_t>(b) * (p.nq + 2 * p.nkv) * D;
+    if (warp == 0) {  // query heads 2h (lanes 0-15) and 2h + 1 (lanes 16-31)
+      const uint4 raw = *reinterpret_cast<const uint4 *>(row + (2 * h + half) * D + 8 * j);
+      *reinterpret_cast<uint4 *>(qstage + half * D + 8 * j) = rope::norm_rope8(raw, p.qw, j, half_mask, cos_t, sin_t);
+    } else if (warp == 1 && k_end == n) {  // the split holding the new token appends its K and V rows
+      const uint4 raw = *reinterpret_cast<const uint4 *>(row + (half ? p.nq + p.nkv + h : p.nq + h) * D + 8 * j);
+      const uint4 val = half ? raw : rope::norm_rope8(raw, p.kw, j, half_mask, cos_t, sin_t);
+      uint16_t *dst = const_cast<uint16_t *>(half ? Vh : Kh) + static_cast<size_t>(n - 1) * D + 8 * j;
+      *reinterpret_cast<uint4 *>(dst) = val;
+      fence_proxy_async_global();  // the row is read back by this CTA's bulk copies
+    }
+  }
   __syncthreads();
 
   float m_run[2] = {-INFINITY, -INFINITY};
@@ -406,7 +449,10 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
   } else {
     // ------------------------------------------------------------ consumers
     float qa[2][16];
-    load_q(p, b, h, lane, qa);
+    if (p.qkv)
+      load_q_staged(qstage, p.qscale, lane, qa);
+    else
+      load_q(p, b, h, lane, qa);
     for (int t = warp, k = 0; t < ntiles; t += NCW, ++k) {
       const int slot = warp * SPW + k % SPW;
       if (!mbar_wait(&s.full[slot], (k / SPW) & 1)) break;

@@ -495,7 +495,10 @@ int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw, const void *
 
 size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv) {
   if (batch < 1 || max_n < 1 || nkv < 1) return 0;
-  return decode_geometry(batch, max_n, nkv, use_streamk(batch, max_n, nkv)).total;
+  // the larger of the two kernels' needs: entry points that force the split
+  // kernel (rib_decode_attention_qkv) take the same workspace
+  return std::max(split_geometry(batch, max_n, nkv).total,
+                  decode_geometry(batch, max_n, nkv, use_streamk(batch, max_n, nkv)).total);
 }
 
 int rib_decode_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
@@ -706,6 +709,35 @@ int rib_decode_attention_batched(const void *q, const uint64_t *cache_ptrs, cons
   p.qscale = scale * 1.4426950408889634f;
   p.out = static_cast<uint16_t *>(out);
   return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
+}
+
+int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw, double base,
+                             const uint64_t *cache_ptrs, const int32_t *lens, int batch, int max_n, int cap,
+                             int nq, int nkv, float scale, void *out, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+  if (!qkv || !qw || !kw || !cache_ptrs || !lens || !out) return RIB_EINVAL;
+  if (batch < 1 || nkv < 1 || nq != 2 * nkv || nq + 2 * nkv > rib::rope::kMaxItems || max_n < 1 || cap < 1 ||
+      !(scale > 0.f) || !(base > 0.0))
+    return RIB_EINVAL;
+  if (max_n > cap) return RIB_ECAPACITY;
+  if (!aligned16(qkv) || !aligned16(qw) || !aligned16(kw) || !aligned16(out) ||
+      (reinterpret_cast<uintptr_t>(cache_ptrs) & 7u) || (reinterpret_cast<uintptr_t>(lens) & 3u))
+    return RIB_EALIGN;
+  rib::decode::Params p = {};
+  p.q = static_cast<const uint16_t *>(qkv);  // (q is formed from qkv in the kernel)
+  p.qkv = static_cast<const uint16_t *>(qkv);
+  p.qw = static_cast<const uint16_t *>(qw);
+  p.kw = static_cast<const uint16_t *>(kw);
+  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
+  p.cache = nullptr;
+  p.cache_ptrs = cache_ptrs;
+  p.lens = lens;
+  p.cap = cap;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.qscale = scale * 1.4426950408889634f;
+  p.out = static_cast<uint16_t *>(out);
+  return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream, false);
 }
 
 int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL, int kL, int qLp,

@@ -505,17 +505,14 @@ class DecodeGraph:
         launches += 1
         for i, w in enumerate(e.layers):
             gemv(w["qkv"], h, nw=w["in_norm"], out=self.qkv)
-            qk_norm_rope_append_at(self.qkv, w["q_norm"], w["k_norm"], self.pos, e.nq_local, e.n_kv, e.base,
-                                   self.cache.kv[i], out=self.q)
             if e.world > 1:   # this rank's heads, every rank's outputs into self.o over NVLink
+                qk_norm_rope_append_at(self.qkv, w["q_norm"], w["k_norm"], self.pos, e.nq_local, e.n_kv, e.base,
+                                       self.cache.kv[i], out=self.q)
                 e.gather.decode_into(self.q.view(1, e.nq_local, HEAD_DIM), self.ptrs[i:i + 1], self.nkeys,
                                      self.max_n, self.cache.capacity, e.scale, self.ws, e.epoch_dev, self.o)
-            else:
-                rc = L.rib_decode_attention_batched(self.q.data_ptr(), self.ptrs.data_ptr() + 8 * i,
-                                                    self.nkeys.data_ptr(), 1, self.max_n, self.cache.capacity,
-                                                    e.nq_local, e.n_kv, float(e.scale), self.o.data_ptr(),
-                                                    self.ws.data_ptr(), self.ws.numel(), st)
-                _lib.check(rc, "decode_attention_batched")
+                launches += 1
+            else:             # norm + RoPE + append inside the attention launch
+                self._attend_fused(L, st, w, i)
             h1 = gemv(w["o"], self.o.view(-1), res=h, out=self.h[1])
             gemv(w["gu"], h1, nw=w["post_norm"], swiglu=True, out=self.a)
             h = gemv(w["down"], self.a, res=h1, out=self.h[2 if h is not self.h[2] else 0])
@@ -527,6 +524,17 @@ class DecodeGraph:
         self.nkeys.add_(1)
         if count:
             self.launches_per_step = launches
+
+    def _attend_fused(self, L, st, w, i: int) -> None:
+        """Layer i's norm + RoPE + KV append of the new token and its decode
+        attention in one launch (rib_decode_attention_qkv): q from self.qkv,
+        the position is nkeys - 1, the output goes to self.o."""
+        e = self.e
+        rc = L.rib_decode_attention_qkv(self.qkv.data_ptr(), w["q_norm"].data_ptr(), w["k_norm"].data_ptr(),
+                                        float(e.base), self.ptrs.data_ptr() + 8 * i, self.nkeys.data_ptr(), 1,
+                                        self.max_n, self.cache.capacity, e.nq_local, e.n_kv, float(e.scale),
+                                        self.o.data_ptr(), self.ws.data_ptr(), self.ws.numel(), st)
+        _lib.check(rc, "decode_attention_qkv")
 
     def _step_tp(self, count: bool) -> None:
         """The step under tensor parallelism: per layer QKV GEMV (input: the
@@ -541,13 +549,7 @@ class DecodeGraph:
         ptrs = self.ptrs
 
         def attend(qkv, w, i, _):
-            qk_norm_rope_append_at(qkv, w["q_norm"], w["k_norm"], self.pos, e.nq_local, e.n_kv, e.base,
-                                   self.cache.kv[i], out=self.q)
-            rc = L.rib_decode_attention_batched(self.q.data_ptr(), ptrs.data_ptr() + 8 * i, self.nkeys.data_ptr(),
-                                                1, self.max_n, self.cache.capacity, e.nq_local, e.n_kv,
-                                                float(e.scale), self.o.data_ptr(), self.ws.data_ptr(),
-                                                self.ws.numel(), st)
-            _lib.check(rc, "decode_attention_batched")
+            self._attend_fused(L, st, w, i)   # (qkv is self.qkv)
             return self.o
 
         for i, w in enumerate(e.layers):

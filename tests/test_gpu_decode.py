@@ -182,3 +182,34 @@ def test_decode_few_heads_many_splits(rib, wl, oracle, nkv, n):
     of, _ = oracle.decode_attention(u16(q), u16(cache), n, wl.SCALE)
     _assert_parity(out, of)
     assert not ws[:16384].any()
+
+
+@pytest.mark.parametrize("B,lens,nkv", [(1, [1], 8), (3, [5, 4097, 700], 8), (2, [32769, 200], 4),
+                                        (1, [32769], 1)])
+def test_decode_fused_append_bit_exact(rib, wl, oracle, B, lens, nkv):
+    """The fused norm + RoPE + append + attention launch writes the same K/V
+    rows and returns the same outputs, bit for bit, as the two-kernel path
+    (batched append, then batched decode), at a single key, short and long
+    contexts (one to hundreds of splits) and 1-8 KV heads; and it meets the
+    oracle's tolerance."""
+    nq = 2 * nkv
+    cap = wl.round_cap(max(lens) + 1)
+    base_cache = wl.randn_bf16((B, 2, nkv, cap, 128), seed=sum(lens) + B, device="cuda")
+    ca, cb = base_cache.clone(), base_cache.clone()
+    g = torch.Generator(device="cuda").manual_seed(B * 7 + nkv)
+    qkv = torch.randn((B, (nq + 2 * nkv) * 128), generator=g, device="cuda").to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(128, generator=g, device="cuda")).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(128, generator=g, device="cuda")).to(torch.bfloat16)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    fused = rib.decode_attention_qkv(qkv, qw, kw, 1e6, ca, lens_d, wl.SCALE)
+    ptrs = torch.tensor([cb[b].data_ptr() for b in range(B)], dtype=torch.int64, device="cuda")
+    caps = torch.full((B,), cap, dtype=torch.int32, device="cuda")
+    q = rib.qk_norm_rope_append_batched(qkv, qw, kw, lens_d - 1, ptrs, caps, nq, nkv, 1e6)
+    two = rib.decode_attention_batched(q, cb, lens_d, wl.SCALE)
+    torch.cuda.synchronize()
+    assert torch.equal(ca, cb)
+    assert torch.equal(fused, two)
+    for b in range(B):
+        of, _ = oracle.decode_attention(u16(q[b]), u16(cb[b]), lens[b], wl.SCALE)
+        _assert_parity(fused[b], of)
+    assert rib._lib.take_device_status() == 0
