@@ -823,9 +823,11 @@ def run_full_model(rib, rank, world, device, args, tp: bool = False):
     out["decode_step"] = {
         "context": f"{ctx + warm}..{ctx + warm + steps}", "steps": steps, "ms_per_token": ms,
         "tokens_per_s": 1000.0 / ms, "launches_per_step": dg.launches_per_step,
-        "path": "one CUDA-graph replay per token (embedding, 28 x [norm+QKV GEMV, qk-norm+RoPE+KV "
-                "append, split-KV decode attention, O GEMV+residual, norm+gate/up GEMV+SwiGLU, "
-                "down GEMV+residual], final norm + LM-head GEMV, argmax)",
+        "path": "one CUDA-graph replay per token (embedding, 28 x [norm+QKV GEMV, split-KV decode "
+                "attention with the qk-norm+RoPE+KV append fused in, O GEMV+residual, norm+gate/up "
+                "GEMV+SwiGLU, down GEMV+residual], final norm + LM-head GEMV, argmax)"
+                + ("; tensor parallel: O/down partial sums and argmax keys exchanged over NVLink "
+                   "inside the GEMV and argmax kernels" if tp else ""),
         "reference_line_ms": line["time_s"] * 1e3, "reference_bottleneck": line["bottleneck"],
         "reference_line_scope": "one GPU (the whole model's bytes over one GPU's bandwidth)",
         "fraction_of_line": line["time_s"] * 1e3 / ms}
