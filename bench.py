@@ -966,7 +966,9 @@ def run_case(case: str):
     warm-up step and 3 replays of 143 launches each (the append fused into
     the decode attention launch); model-batch is the
     64-sequence ragged batched decode step (contexts U[512, 4096], 17.9 GB
-    of K/V): the capture's eager warm-up step and 3 graph replays."""
+    of K/V): the capture's eager warm-up step and 3 graph replays;
+    model-prefill is three 4096-token prefills of Qwen3-0.6B (last row's
+    logits), the TTFT path of the request benchmark."""
     rib = load_rib()
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
@@ -990,6 +992,12 @@ def run_case(case: str):
         dg.set_state(1, ctx)
         for _ in range(3):
             dg.replay()
+    elif case == "model-prefill":
+        eng = rib.Engine(rib.random_weights(rib.QWEN3_0_6B, seed=11, device=device))
+        toks = torch.randint(0, rib.QWEN3_0_6B.vocab_size, (4096,), generator=torch.Generator().manual_seed(13))
+        toks = toks.to(torch.int32).to(device)
+        for _ in range(3):
+            eng.prefill(toks, eng.new_cache(4096 + 256), last=True)
     elif case == "model-batch":
         eng = rib.Engine(rib.random_weights(rib.QWEN3_0_6B, seed=11, device=device))
         _, dec = batch_workload(eng, device, 8)
@@ -1016,7 +1024,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "model-decode", "model-batch"], default=None,
+    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "model-decode", "model-prefill",
+                             "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()
     if args.case:

@@ -316,6 +316,67 @@ struct RowParams {
   int rows, W;
 };
 
+// One warp per row for W = 256 * C: lane l holds the 16-byte chunks
+// l, l + 32, ... of the row (8 elements each) in registers, the sum of
+// squares is a warp reduction, and 8 rows share a CTA, so a long prompt runs
+// a few hundred CTAs with every operand load issued up front.  Same rounding
+// points as add_rms_kernel (the FP32 sum of squares adds in another order).
+template <int C>
+__global__ void __launch_bounds__(256) add_rms_rows_kernel(const __grid_constant__ RowParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
+  const size_t base = static_cast<size_t>(row) * p.W;
+  uint4 va[C], vb[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) va[c] = *reinterpret_cast<const uint4 *>(p.a + base + (c * 32 + lane) * 8);
+  if (p.b) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) vb[c] = *reinterpret_cast<const uint4 *>(p.b + base + (c * 32 + lane) * 8);
+  }
+  float f[C][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const uint4 a = va[c];
+    f[c][0] = bf16lo(a.x); f[c][1] = bf16hi(a.x); f[c][2] = bf16lo(a.y); f[c][3] = bf16hi(a.y);
+    f[c][4] = bf16lo(a.z); f[c][5] = bf16hi(a.z); f[c][6] = bf16lo(a.w); f[c][7] = bf16hi(a.w);
+    if (p.b) {
+      const uint4 b = vb[c];
+      const float g[8] = {bf16lo(b.x), bf16hi(b.x), bf16lo(b.y), bf16hi(b.y),
+                          bf16lo(b.z), bf16hi(b.z), bf16lo(b.w), bf16hi(b.w)};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[c][e] = round_bf16(f[c][e] + g[e]);
+      uint4 o;
+      o.x = pack_bf16x2(f[c][0], f[c][1]);
+      o.y = pack_bf16x2(f[c][2], f[c][3]);
+      o.z = pack_bf16x2(f[c][4], f[c][5]);
+      o.w = pack_bf16x2(f[c][6], f[c][7]);
+      *reinterpret_cast<uint4 *>(p.residual + base + (c * 32 + lane) * 8) = o;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(f[c][e], f[c][e], ss);
+  }
+  const float inv = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(p.W) + kEps);
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(p.w + (c * 32 + lane) * 8);
+    const float wf[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                         bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
+    float n[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) n[e] = wf[e] * round_bf16(f[c][e] * inv);
+    uint4 o;
+    o.x = pack_bf16x2(n[0], n[1]);
+    o.y = pack_bf16x2(n[2], n[3]);
+    o.z = pack_bf16x2(n[4], n[5]);
+    o.w = pack_bf16x2(n[6], n[7]);
+    *reinterpret_cast<uint4 *>(p.out + base + (c * 32 + lane) * 8) = o;
+  }
+}
+
 // One CTA per row, 8 elements per thread per step.  The row is kept in
 // shared memory between the sum of squares and the normalisation.
 __global__ void __launch_bounds__(256) add_rms_kernel(const __grid_constant__ RowParams p) {
