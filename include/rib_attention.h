@@ -410,7 +410,12 @@ int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw,
  * written into the cache at that position first.  Outputs and cache rows are
  * bit-identical to rib_qk_norm_rope_append_batched followed by
  * rib_decode_attention_batched; one launch and one dependency fewer per
- * layer (agent-test/v2/engine.py:150-155 in one kernel). */
+ * layer (agent-test/v2/engine.py:150-155 in one kernel).
+ * The kernel starts streaming the cache before its programmatic-launch wait:
+ * lens, cache_ptrs and the cache rows below lens[b] - 1 must be complete
+ * when it starts (written by host copies, by a kernel that does not trigger
+ * programmatic launch, or earlier); only qkv may come from the kernel
+ * launched immediately before. */
 int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw,
                              double base, const uint64_t *cache_ptrs,
                              const int32_t *lens, int batch, int max_n, int cap,

@@ -106,6 +106,12 @@ struct Params {
   const uint16_t *qkv;
   const uint16_t *qw, *kw;
   double inv_freq[64];  // base^(-d/64)
+  // early (decode_kernel only): lens, caps, cache_ptrs and every cache row
+  // below lens[b] - 1 are complete when the kernel starts, so the producer
+  // fills the ring with tiles below the new token's row before the
+  // programmatic-launch wait; only qkv (and the appended row) come from the
+  // kernel launched just before.
+  int early;
 };
 
 
@@ -373,7 +379,7 @@ __device__ __forceinline__ void load_q_staged(const uint16_t *qs, float qscale, 
 // decode_kernel (one unit per CTA) and by the persistent decode-step kernel
 // (decode_step.cuh), which calls it with the unit it owns in that phase.
 // All NTHREADS threads enter; returns are CTA-uniform.
-__device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, int h, int b) {
+__device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, int h, int b, bool early = false) {
   const int n = p.lens ? p.lens[b] : p.n_single;
   const int cap = p.caps ? p.caps[b] : p.cap;  // rows per head of this sequence's cache
   if (n < 1 || n > cap || n > p.max_n) {  // bad device-side length: record, write nothing
@@ -403,6 +409,24 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
       mbar_init(&s.empty[i], 1);
     }
     fence_mbar_init();
+  }
+  // Early start: tiles that end below the new token's row do not depend on the
+  // kernel before this one; one ring's worth is in flight before the wait.
+  const int pre = early ? max(0, min(min(STAGES, ntiles), (n - 1 - k_begin) / TK)) : 0;
+  if (early) {
+    __syncthreads();  // barriers initialised
+    if (warp == NCW && lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int t = 0; t < pre; ++t) {  // t < STAGES: every slot is free, no empty wait
+        const int slot = (t % NCW) * SPW + (t / NCW) % SPW;
+        const int k0 = k_begin + t * TK;
+        const uint32_t bytes = static_cast<uint32_t>(min(TK, k_end - k0)) * ROW_BYTES;
+        mbar_arrive_expect_tx(&s.full[slot], 2 * bytes);
+        bulk_g2s(s.k[slot], Kh + static_cast<size_t>(k0) * D, bytes, &s.full[slot], pol);
+        bulk_g2s(s.v[slot], Vh + static_cast<size_t>(k0) * D, bytes, &s.full[slot], pol);
+      }
+    }
+    pdl_wait();
   }
   // Fused prologue: the merge buffers are free until the merge, so they hold
   // the RoPE angles and the staged q meanwhile.
@@ -435,7 +459,7 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      for (int t = 0; t < ntiles; ++t) {
+      for (int t = pre; t < ntiles; ++t) {
         const int k = t / NCW;  // k-th tile of consumer warp t % NCW
         const int slot = (t % NCW) * SPW + k % SPW;
         if (k >= SPW && !mbar_wait(&s.empty[slot], ((k / SPW) - 1) & 1)) break;
@@ -577,8 +601,8 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_kernel(const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   pdl_launch_dependents();
-  pdl_wait();
-  decode_cta(p, s, blockIdx.x, blockIdx.y, blockIdx.z);
+  if (!p.early) pdl_wait();  // (with early, decode_cta waits after its first bulk copies)
+  decode_cta(p, s, blockIdx.x, blockIdx.y, blockIdx.z, p.early != 0);
 }
 
 }  // namespace decode

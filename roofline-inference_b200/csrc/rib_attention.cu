@@ -729,6 +729,7 @@ int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw, do
   rib::decode::Params p = {};
   p.q = static_cast<const uint16_t *>(qkv);  // (q is formed from qkv in the kernel)
   p.qkv = static_cast<const uint16_t *>(qkv);
+  p.early = 1;
   p.qw = static_cast<const uint16_t *>(qw);
   p.kw = static_cast<const uint16_t *>(kw);
   for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
