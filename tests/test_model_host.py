@@ -211,3 +211,34 @@ def test_tp_entry_points_reject_bad_arguments(rib):
     # a residual epilogue has no tensor-parallel form
     ex.rank = 0
     assert L.rib_gemv_tp(FAKE, 64, 256, FAKE, None, 1, 0, FAKE, ctypes.byref(ex), 0, None, None) == 1
+
+
+def test_fused_decode_entry_rejects_bad_arguments(rib):
+    """rib_decode_attention_qkv argument checks (no launch): GQA factor, null
+    pointers, non-positive base, misaligned qkv, capacity below max_n."""
+    L = rib.load_library()
+    args = dict(qkv=FAKE, qw=FAKE, kw=FAKE, base=1e6, ptrs=FAKE, lens=FAKE, B=1, max_n=100, cap=256, nq=16,
+                nkv=8, scale=0.09, out=FAKE, ws=FAKE, wsb=1 << 20)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return L.rib_decode_attention_qkv(a["qkv"], a["qw"], a["kw"], a["base"], a["ptrs"], a["lens"], a["B"],
+                                          a["max_n"], a["cap"], a["nq"], a["nkv"], a["scale"], a["out"], a["ws"],
+                                          a["wsb"], None)
+    assert call(nq=15) == 1
+    assert call(qkv=None) == 1
+    assert call(base=0.0) == 1
+    assert call(B=0) == 1
+    assert call(qkv=MISALIGNED) == 3
+    assert call(lens=0x10002) == 3
+    assert call(max_n=300) == 2          # RIB_ECAPACITY: max_n above the capacity
+
+
+def test_fused_decode_wrapper_checks_shapes(rib):
+    """decode_attention_qkv refuses CPU tensors and a qkv width that does not
+    match the caches' KV heads before any launch."""
+    qkv = torch.zeros((1, 32 * 128), dtype=torch.bfloat16)
+    w = torch.ones(128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        rib.decode_attention_qkv(qkv, w, w, 1e6, torch.zeros((1, 2, 8, 256, 128), dtype=torch.bfloat16), [5],
+                                 0.09)
