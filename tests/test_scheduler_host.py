@@ -203,3 +203,72 @@ def test_scheduler_argument_checks():
         s.submit([1], -1)
     with pytest.raises(ValueError):
         s.submit([1] * 500, 20)               # capacity above max_len
+
+
+# ------------------------------------------------------------------ randomized
+def test_pool_random_alloc_free_invariants():
+    """Random allocate / free sequences: live blocks never overlap, the free
+    list stays sorted and fully merged, and free + used pages always add up
+    to the arena."""
+    import random
+    rng = random.Random(7)
+    p = KVPool(1, 1, rows=64 * 256, head_dim=8)
+    live = []
+    for _ in range(2000):
+        if live and (rng.random() < 0.45 or p.free_pages == 0):
+            c = live.pop(rng.randrange(len(live)))
+            p.free(c)
+        else:
+            want = rng.randint(1, 12 * 256)
+            try:
+                live.append(p.allocate(want))
+            except PoolFull:
+                assert p.largest_free_rows < want
+                continue
+        spans = sorted((c.storage.data_ptr(), c.storage.data_ptr() + c.storage.numel() * 2) for c in live)
+        for (a0, a1), (b0, _) in zip(spans, spans[1:]):
+            assert a1 <= b0
+        starts = [s for s, _ in p._free]
+        assert starts == sorted(starts)
+        for (s0, n0), (s1, _) in zip(p._free, p._free[1:]):
+            assert s0 + n0 < s1                      # adjacent free blocks are merged
+        used = sum(c.capacity // 256 for c in live)
+        assert used + p.free_pages == p.pages
+    for c in live:
+        p.free(c)
+    assert p._free == [(0, 64)]
+
+
+def test_scheduler_random_workload_matches_single_stream():
+    """Random prompts, output lengths, end-of-sequence ids, slot counts, pool
+    sizes and chunk sizes: every request gets exactly the single-stream
+    greedy tokens, every cache and slot is returned, and the chunk budget per
+    step is never exceeded."""
+    import random
+    rng = random.Random(11)
+    for trial in range(25):
+        slots = rng.randint(1, 5)
+        chunk = rng.choice([16, 64, 100, 4096])
+        rows = rng.randint(4, 24) * 256
+        s, eng = make(slots=slots, rows=rows, chunk=chunk, max_len=rows)
+        reqs = []
+        for _ in range(rng.randint(1, 12)):
+            n = rng.randint(1, 300)
+            m = rng.randint(0, 40)
+            if n + m + 1 > rows:
+                continue
+            prompt = [rng.randrange(VOCAB) for _ in range(n)]
+            eos = [rng.randrange(VOCAB)] if rng.random() < 0.5 else []
+            reqs.append((s.submit(prompt, m, eos), prompt, m, eos))
+        before = len(eng.calls)
+        steps_before = s.steps
+        out = s.run()
+        for rid, prompt, m, eos in reqs:
+            assert out[rid] == expected(prompt, m, eos), (trial, rid)
+        assert s.pool.free_pages == s.pool.pages
+        assert all(c is None for c in s.dec.caches)
+        # prompt tokens per step never exceed the chunk
+        per_step = eng.calls[before:]
+        assert all(c <= chunk for c in per_step)
+        assert sum(per_step) == sum(len(p) for _, p, m, _ in reqs if m > 0)
+        assert s.steps >= steps_before
