@@ -151,3 +151,62 @@ def test_balance_sequences_is_lpt_and_complete():
     assert max(loads) <= 4 / 3 * max(sum(lens) / 2, max(lens))
     assert loads == [130, 170]
     assert sh.slots_per_rank(a) == max(len(x) for x in a)
+
+
+def _tp_worker(rank, world, port, result_q):
+    """One tensor-parallel layer on CPU: this rank's slices of the O, gate/up
+    and down projections (tp.shard_layer), FP32 partial sums all-reduced over
+    gloo, the SwiGLU on this rank's intermediate slice, and the LM-head slice
+    all-gathered."""
+    try:
+        _init(rank, world, port)
+        rib = importlib.import_module("roofline-inference_b200")
+        tp = importlib.import_module("roofline-inference_b200.tp")
+        sh = importlib.import_module("roofline-inference_b200.sharding")
+        cfg = rib.Qwen3Config(num_layers=1, hidden_size=256, num_heads=8, num_kv_heads=4,
+                              intermediate_size=512, vocab_size=1000)
+        w = rib.random_weights(cfg, seed=21)
+        layer = {k: v.float() for k, v in w.layers[0].items()}
+        h0, h1 = sh.head_range(rank, world, cfg.num_kv_heads)
+        f0, f1 = tp.split_range(cfg.intermediate_size, rank, world)
+        v0, v1 = tp.split_range(cfg.vocab_size, rank, world)
+        s = tp.shard_layer(layer, h0, h1, f0, f1, cfg.num_heads, cfg.num_kv_heads)
+        g = torch.Generator().manual_seed(3)
+        o_all = torch.randn(4, cfg.q_dim, generator=g)           # attention outputs of 4 tokens
+        x = torch.randn(4, cfg.hidden_size, generator=g)          # normalised MLP input
+        part = o_all[:, 2 * h0 * 128:2 * h1 * 128] @ s["o"].t()   # row-parallel O
+        dist.all_reduce(part)
+        gu = x @ s["gu"].t()                                      # column-parallel gate / up
+        F = f1 - f0
+        act = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+        down = act @ s["down"].t()                                # row-parallel down
+        dist.all_reduce(down)
+        logits = x @ w.embed[v0:v1].float().t()                   # vocabulary-parallel LM head
+        parts = [torch.empty_like(logits) for _ in range(world)]
+        dist.all_gather(parts, logits)
+        result_q.put((rank, (part.numpy(), down.numpy(), torch.cat(parts, dim=1).numpy())))
+        dist.destroy_process_group()
+    except Exception as e:
+        result_q.put((rank, repr(e)))
+
+
+def test_tensor_parallel_layer_matches_unsharded():
+    """Two gloo ranks: the tensor-parallel split of a Qwen3 layer reproduces
+    the unsplit products (O, SwiGLU MLP, LM head) on every rank."""
+    results = _run(_tp_worker)
+    rib = importlib.import_module("roofline-inference_b200")
+    cfg = rib.Qwen3Config(num_layers=1, hidden_size=256, num_heads=8, num_kv_heads=4,
+                          intermediate_size=512, vocab_size=1000)
+    w = rib.random_weights(cfg, seed=21)
+    layer = {k: v.float() for k, v in w.layers[0].items()}
+    g = torch.Generator().manual_seed(3)
+    o_all = torch.randn(4, cfg.q_dim, generator=g)
+    x = torch.randn(4, cfg.hidden_size, generator=g)
+    F = cfg.intermediate_size
+    gu = x @ layer["gu"].t()
+    want = (o_all @ layer["o"].t(),
+            (torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]) @ layer["down"].t(),
+            x @ w.embed.float().t())
+    for r, got in results.items():
+        for a, b in zip(got, want):
+            np.testing.assert_allclose(a, b.numpy(), rtol=1e-4, atol=1e-4)
