@@ -56,6 +56,19 @@ const char *rib_last_error_string(void);
  * Synchronises the current device. */
 int rib_take_device_status(int *status_host);
 
+/* Wall-clock limit of every device-side wait of this library (mbarrier
+ * waits, the NVLink gather's epoch poll, the tensor-parallel word polls, the
+ * persistent step's grid barrier) on the current device, in nanoseconds:
+ * 2 s unless set, accepted range 1 ms .. 60 s (RIB_EINVAL otherwise).  A wait
+ * that runs out records RIB_ETIMEOUT (rib_take_device_status) and its kernel
+ * returns instead of spinning; the reference's analogue is the v3 harness's
+ * per-unit timeout with an exclusion record (agent-test/v3/run.py:238-261).
+ * The new limit applies to kernels launched after the call returns; set it
+ * while none of this library's kernels runs on the device.  No reference
+ * counterpart as an entry point. */
+int rib_set_wait_limit_ns(unsigned long long ns);
+int rib_get_wait_limit_ns(unsigned long long *ns);
+
 /* ------------------------------------------------------------------------ *
  * Fused per-head RMSNorm + RoPE, one token (decode).
  * Replaces qk_norm_rope(qkv, qw, kw, pos, nq, nkv, base)
@@ -268,6 +281,18 @@ int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw,
                                 const void *kw, const int32_t *offset_dev,
                                 int nq, int nkv, double base, int Lp,
                                 void *q_out, void *cache, int cap, void *stream);
+
+/* rib_qk_norm_rope_prefill with the first position read on the device
+ * (*offset_dev, int32): the form of qk_norm_rope(qkv, qw, kw, pos, ...)
+ * (agent-test/v2/kernels.py:157-164), whose pos is an int32 array, and of
+ * qk_norm_rope_prefill (kernels.py:215-224), without a host read of the
+ * position.  L = 1, Lp = 1 is the single-token form.  Outputs as
+ * rib_qk_norm_rope_prefill; a negative position writes nothing and the device
+ * status word reads RIB_ECAPACITY. */
+int rib_qk_norm_rope_prefill_dev(const void *qkv, int L, const void *qw,
+                                 const void *kw, const int32_t *offset_dev,
+                                 int nq, int nkv, double base, int Lp,
+                                 void *q_out, void *kv_out, void *stream);
 
 /* Epilogues of rib_gemv. */
 #define RIB_EPI_NONE 0     /* y = bf16(W x), or FP32 W x when out_f32      */

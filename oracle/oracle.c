@@ -11,8 +11,13 @@
  *     agent-test/v2/test_engine.py:52-59 (mx.fast.rms_norm eps 1e-6,
  *     mx.fast.rope(dims 128, traditional=False, base, scale 1.0, offset)).
  *     RMSNorm rounding points n = bf16(w * bf16(x * inv)) (kernels.py:131-133).
- *     The RoPE angle and its cosine/sine are evaluated in FP64 (the exact
- *     value the FP32 Metal/MLX arithmetic approximates), then rounded to BF16.
+ *     The RoPE angle is the reference's FP32 value (kernels.py:134-138, 152):
+ *     theta = float(pos) * exp2(-(d/64) * float(log2(base))), each product
+ *     rounded to FP32 and exp2 rounded once to FP32 (mx.fast.rope forms it
+ *     the same way).  Its cosine/sine are then evaluated in FP64, the value
+ *     the Metal fast::cos / fast::sin approximate.  With angle_f64 set the
+ *     angle itself is formed in FP64 instead (the idealised rope), to count
+ *     how far the reference's FP32 angle moves the BF16 outputs.
  *   - decode attention: the MLX call at agent-test/v2/engine.py:154-155,
  *     softmax(scale * q K^T) V over n keys, GQA head h -> KV head h / 2,
  *     no mask (engine.py:148-155).  FP32 arithmetic, exact max, one rounding
@@ -67,16 +72,23 @@ int oracle_version(void) { return 1; }
  * kv_out [2][nkv][kv_rows][128] written at rows kv_row0 + t. */
 void oracle_qk_norm_rope(const uint16_t *qkv, int L, const uint16_t *qw, const uint16_t *kw,
                          int offset, int nq, int nkv, double base, int Lp, uint16_t *q_out,
-                         uint16_t *kv_out, int kv_rows, int kv_row0) {
+                         uint16_t *kv_out, int kv_rows, int kv_row0, int angle_f64) {
   const int items = nq + 2 * nkv;
-  double inv_freq[64];
-  for (int d = 0; d < 64; ++d) inv_freq[d] = pow(base, -(double)d / 64.0);
+  float inv_freq[64];
+  double inv_freq64[64];
+  const float lb = (float)log2(base); /* the f-string literal, read as FP32 */
+  for (int d = 0; d < 64; ++d) {
+    volatile float x = -((float)d / 64.0f) * lb; /* one FP32 rounding */
+    inv_freq[d] = (float)exp2((double)x);
+    inv_freq64[d] = pow(base, -(double)d / 64.0);
+  }
   memset(q_out, 0, sizeof(uint16_t) * (size_t)nq * Lp * D);
 #pragma omp parallel for schedule(static)
   for (int t = 0; t < L; ++t) {
     double cs[64], sn[64];
     for (int d = 0; d < 64; ++d) {
-      const double th = (double)(offset + t) * inv_freq[d];
+      volatile float th32 = (float)(offset + t) * inv_freq[d]; /* FP32 product */
+      const double th = angle_f64 ? (double)(offset + t) * inv_freq64[d] : (double)th32;
       cs[d] = cos(th);
       sn[d] = sin(th);
     }

@@ -31,7 +31,8 @@ def lib() -> ctypes.CDLL:
         L = ctypes.CDLL(str(path))
         L.oracle_qk_norm_rope.argtypes = [_u16p, ctypes.c_int, _u16p, _u16p, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, ctypes.c_double,
-                                          ctypes.c_int, _u16p, _u16p, ctypes.c_int, ctypes.c_int]
+                                          ctypes.c_int, _u16p, _u16p, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int]
         L.oracle_qk_norm_rope.restype = None
         L.oracle_decode_attention_batched.argtypes = [
             _u16p, ctypes.POINTER(ctypes.c_void_p), _i32p, ctypes.c_int, ctypes.c_int,
@@ -62,16 +63,20 @@ def _u16(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.uint16)
 
 
-def qk_norm_rope(qkv, qw, kw, offset: int, nq: int, nkv: int, base: float, Lp: int | None = None):
+def qk_norm_rope(qkv, qw, kw, offset: int, nq: int, nkv: int, base: float, Lp: int | None = None,
+                 angle_f64: bool = False):
     """qkv [L, (nq+2nkv)*128] u16 -> (Q [nq, Lp, 128] u16 with zero pad rows,
-    KV [2, nkv, L, 128] u16).  agent-test/v2/kernels.py:169-224."""
+    KV [2, nkv, L, 128] u16).  agent-test/v2/kernels.py:169-224.
+
+    The RoPE angle is the reference's FP32 one (kernels.py:134-138); with
+    angle_f64 it is formed in FP64 instead (the idealised rope)."""
     qkv = _u16(qkv).reshape(-1, (nq + 2 * nkv) * 128)
     L = qkv.shape[0]
     Lp = L if Lp is None else Lp
     q = np.zeros((nq, Lp, 128), np.uint16)
     kv = np.zeros((2, nkv, L, 128), np.uint16)
     lib().oracle_qk_norm_rope(qkv, L, _u16(qw), _u16(kw), int(offset), nq, nkv, float(base), Lp,
-                              q, kv, L, 0)
+                              q, kv, L, 0, int(bool(angle_f64)))
     return q, kv
 
 

@@ -98,6 +98,8 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_status_string": ([i], ctypes.c_char_p),
         "rib_last_error_string": ([], ctypes.c_char_p),
         "rib_take_device_status": ([ctypes.POINTER(ctypes.c_int)], i),
+        "rib_set_wait_limit_ns": ([ctypes.c_ulonglong], i),
+        "rib_get_wait_limit_ns": ([ctypes.POINTER(ctypes.c_ulonglong)], i),
         "rib_qk_norm_rope": ([vp, vp, vp, i, i, i, d, vp, vp, vp], i),
         "rib_qk_norm_rope_prefill": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, vp], i),
         "rib_qk_norm_rope_append": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, i, vp], i),
@@ -108,6 +110,7 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_decode_attention_batched": ([vp, vp, vp, i, i, i, i, i, f, vp, vp, sz, vp], i),
         "rib_prefill_attention": ([vp, vp, vp, i, i, i, i, i, i, f, vp, vp], i),
         "rib_qk_norm_rope_append_dev": ([vp, i, vp, vp, vp, i, i, d, i, vp, vp, i, vp], i),
+        "rib_qk_norm_rope_prefill_dev": ([vp, i, vp, vp, vp, i, i, d, i, vp, vp, vp], i),
         "rib_gemv": ([vp, i, i, vp, vp, vp, i, i, vp, vp], i),
         "rib_add_rms": ([vp, vp, vp, i, i, vp, vp, vp], i),
         "rib_rms_norm": ([vp, vp, i, i, vp, vp], i),
@@ -156,4 +159,20 @@ def take_device_status() -> int:
     """Reads and clears the device status word (synchronises the device)."""
     v = ctypes.c_int(0)
     check(load().rib_take_device_status(ctypes.byref(v)), "rib_take_device_status")
+    return v.value
+
+
+DEFAULT_WAIT_LIMIT_NS = 2_000_000_000
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Sets the wall-clock limit of every device-side wait on the current
+    device (1 ms .. 60 s; the default is 2 s).  Takes effect for kernels
+    launched afterwards; call it while none of this library's kernels runs."""
+    check(load().rib_set_wait_limit_ns(int(ns)), "rib_set_wait_limit_ns")
+
+
+def wait_limit_ns() -> int:
+    v = ctypes.c_ulonglong(0)
+    check(load().rib_get_wait_limit_ns(ctypes.byref(v)), "rib_get_wait_limit_ns")
     return v.value

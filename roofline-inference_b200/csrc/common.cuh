@@ -17,8 +17,14 @@ namespace rib {
 // and clears it with rib_take_device_status().
 __device__ int g_device_status;
 
-// Wall-clock bound on any single wait (nanoseconds, %globaltimer).
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Wall-clock bound on any single wait (nanoseconds, %globaltimer): 2 s by
+// default, set per device with rib_set_wait_limit_ns().  Read only on a wait's
+// slow path, after its first poll failed.
+constexpr unsigned long long kDefaultWaitLimitNs = 2000000000ull;
+__device__ unsigned long long g_wait_limit_ns = kDefaultWaitLimitNs;
+__device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *reinterpret_cast<volatile const unsigned long long *>(&g_wait_limit_ns);
+}
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
@@ -126,13 +132,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs, records RIB_ETIMEOUT and returns false.
+// wait_limit_ns(), records RIB_ETIMEOUT and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > wait_limit_ns()) {
       record_timeout();
       return false;
     }

@@ -105,7 +105,7 @@ struct Params {
   // cache first -- the arithmetic of rope::qk_norm_rope_kernel, bit for bit.
   const uint16_t *qkv;
   const uint16_t *qw, *kw;
-  double inv_freq[64];  // base^(-d/64)
+  float inv_freq[64];   // rope_inv_freq
   // early (decode_kernel only): lens, caps, cache_ptrs and every cache row
   // below lens[b] - 1 are complete when the kernel starts, so the producer
   // fills the ring with tiles below the new token's row before the
@@ -168,7 +168,7 @@ __device__ __forceinline__ void finalize_unit(const Params &p, int b, int h, int
     if (ld_acquire_sys(slot) < epoch) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_sys(slot) < epoch) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > wait_limit_ns()) {
           record_timeout();
           break;
         }

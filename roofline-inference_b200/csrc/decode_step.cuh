@@ -55,7 +55,7 @@ struct Params {
   int L, hidden, nq, nkv, inter, vocab, cap;
   const uint16_t *embed, *final_norm;
   Layer layer[kMaxLayers];
-  double inv_freq[64];
+  float inv_freq[64];   // rope_inv_freq
   const uint64_t *cache_ptrs;  // [L] layer caches [2][nkv][cap][128]
   int32_t *tok, *pos, *nkeys;  // device state: token in/out, position, key count
   uint16_t *h[3], *qkv, *q, *o, *a;
@@ -93,7 +93,7 @@ __device__ __forceinline__ bool grid_sync(Sync *sy, int *ok_s) {
             ok = 0;
             break;
           }
-          if (global_timer_ns() - t0 > kWaitLimitNs) {
+          if (global_timer_ns() - t0 > wait_limit_ns()) {
             record_timeout();
             atomicExch(&sy->abort, 1);
             ok = 0;

@@ -111,7 +111,7 @@ __device__ __forceinline__ void stream_finalize(const Params &p, StreamSmem &s, 
     if (ld_acquire_sys(slot) < epoch) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_sys(slot) < epoch) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > wait_limit_ns()) {
           record_timeout();
           break;
         }

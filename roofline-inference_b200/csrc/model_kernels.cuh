@@ -67,7 +67,7 @@ __device__ __forceinline__ ulonglong2 ld_volatile_v2u64(const unsigned long long
 }
 
 // Two words of exchange e at p (16-byte aligned), polled until both carry
-// e; gives up after kWaitLimitNs (shared deadline t0 per thread, 0: not
+// e; gives up after wait_limit_ns() (shared deadline t0 per thread, 0: not
 // started) with RIB_ETIMEOUT recorded.
 __device__ __forceinline__ ulonglong2 tp_read2(const unsigned long long *p, unsigned long long e, uint64_t &t0) {
   const uint32_t want = static_cast<uint32_t>(e);
@@ -75,7 +75,7 @@ __device__ __forceinline__ ulonglong2 tp_read2(const unsigned long long *p, unsi
   while (static_cast<uint32_t>(v.x >> 32) != want || static_cast<uint32_t>(v.y >> 32) != want) {
     const uint64_t now = global_timer_ns();
     if (t0 == 0) t0 = now;
-    if (now - t0 > kWaitLimitNs) {
+    if (now - t0 > wait_limit_ns()) {
       record_timeout();
       break;
     }

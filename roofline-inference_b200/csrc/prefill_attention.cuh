@@ -52,7 +52,10 @@ constexpr int NTHREADS = NWARPS * 32;
 constexpr int PANEL_BYTES = 128 * 128;          // [128 rows][64 dims] BF16, one swizzle panel
 constexpr int TILE_BYTES = 2 * PANEL_BYTES;     // [128 rows][128 dims]
 constexpr uint32_t TMEM_COLS = 512;
-constexpr float kRescaleThreshold = 8.0f;       // log2 units
+#ifndef RIB_PREFILL_RESCALE_LOG2
+#define RIB_PREFILL_RESCALE_LOG2 8.0f
+#endif
+constexpr float kRescaleThreshold = RIB_PREFILL_RESCALE_LOG2;  // log2 units
 constexpr int kLaunchRegs = 168;                 // registers per thread at launch
 constexpr int kRegsLow = 40;                     // warpgroup 0 after setmaxnreg.dec
 constexpr int kRegsHigh = 232;                   // softmax warpgroups after setmaxnreg.inc

@@ -5,19 +5,25 @@
 //   inv  = 1 / sqrt(mean(x^2) + 1e-6)                      (kernels.py:129-130)
 //   n_d  = bf16( w_d * bf16( x_d * inv ) )                  (kernels.py:131-133)
 //   non-traditional RoPE, pairs (d, d+64), d in [0, 64):    (kernels.py:136-143)
-//     theta_d = pos * base^(-d/64)
+//     theta_d = float(pos) * exp2(-(d/64) * log2(base)), all in FP32
 //     o_d    = n_d cos - n_{d+64} sin,  o_{d+64} = n_d sin + n_{d+64} cos
 //   V heads are copied bit for bit                         (kernels.py:123-127)
+// The angle is the reference's FP32 value: the FP32 product -(d/64)*log2(base)
+// (kernels.py:137-138, log2(base) rounded to FP32 as the Python f-string
+// literal makes it, kernels.py:152), its exp2 rounded to FP32 on the host, and
+// the FP32 product with float(pos).  mx.fast.rope forms theta the same way.
 // Differences from the Metal source, by design:
-//   - theta is formed and reduced to [-pi, pi] in FP64 and evaluated with the
-//     full-range sincosf, so large positions (32k) keep full FP32 accuracy
-//     (the Metal code uses an FP32 product and fast::cos / fast::sin);
+//   - cos/sin of that FP32 angle are evaluated to full accuracy (reduced to
+//     [-pi, pi] in FP64, then sincosf) where the Metal code calls
+//     fast::cos / fast::sin, whose error grows with |theta|;
 //   - K and V are written straight into the cache rows (engine.py:42-48 fused).
 //
 // Layout of the work: one CTA per token; each warp owns two (token, head)
 // items, one per half-warp; lane j of a half-warp owns dims [8j, 8j+8), moved
 // as one 16-byte vector.  The RoPE partner of dim d < 64 lives in lane j ^ 8.
 #pragma once
+
+#include <cmath>
 
 #include "common.cuh"
 
@@ -36,17 +42,33 @@ struct Params {
   int L, Lp, offset, nq, nkv;
   int kv_rows;          // rows per head in kv (L, or the cache capacity)
   int kv_row0;          // first row written (0, or the cache offset)
-  const int32_t *offset_dev;  // when set: the offset (and first cache row) read on the device
-  double inv_freq[64];  // base^(-d/64), FP64
+  const int32_t *offset_dev;  // when set: the offset read on the device
+  int rows_follow_offset;     // with offset_dev: K/V rows start at the device offset (cache
+                              // append) rather than at kv_row0
+  float inv_freq[64];   // exp2(-(d/64) log2(base)) rounded to FP32 (rope_inv_freq)
 };
 
-// cos/sin of the 64 RoPE angles at position `pos`: theta_d = pos * inv_freq[d],
-// reduced to [-pi, pi] in FP64, then full-range sincosf.  Threads 0..63 write.
-__device__ __forceinline__ void rope_angles(int pos, const double *inv_freq, float *cos_t, float *sin_t,
+// Host: the 64 inverse frequencies exp2(-(d/64) * log2(base)) as the
+// reference's FP32 arithmetic forms them (kernels.py:137-138, 152): log2(base)
+// rounded to FP32, the FP32 product with -(d/64), and exp2 of that product
+// rounded once to FP32.
+inline void rope_inv_freq(float *out, double base) {
+  const float lb = static_cast<float>(std::log2(base));
+  for (int d = 0; d < 64; ++d) {
+    volatile float x = -(static_cast<float>(d) / 64.0f) * lb;  // one FP32 rounding
+    out[d] = static_cast<float>(std::exp2(static_cast<double>(x)));
+  }
+}
+
+// cos/sin of the 64 RoPE angles at position `pos`: theta_d = float(pos) *
+// inv_freq[d] as one FP32 product (kernels.py:134-138), then reduced to
+// [-pi, pi] in FP64 and evaluated with the full-range sincosf.  Threads 0..63
+// write.
+__device__ __forceinline__ void rope_angles(int pos, const float *inv_freq, float *cos_t, float *sin_t,
                                             int tid) {
   if (tid < 64) {
     const double two_pi = 6.283185307179586476925286766559;
-    const double th = static_cast<double>(pos) * inv_freq[tid];
+    const double th = static_cast<double>(__fmul_rn(static_cast<float>(pos), inv_freq[tid]));
     const double r = th - rint(th * (1.0 / two_pi)) * two_pi;
     float s, c;
     sincosf(static_cast<float>(r), &s, &c);
@@ -109,10 +131,10 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
   const int t = blockIdx.x;
   const int tid = threadIdx.x;
   int offset = p.offset, kv_row0 = p.kv_row0;
-  if (p.offset_dev) {  // position kept on the device (CUDA-graph replay)
+  if (p.offset_dev) {  // position kept on the device (CUDA-graph replay, no host sync)
     offset = *p.offset_dev;
-    kv_row0 = offset;
-    if (offset < 0 || static_cast<long long>(offset) + p.L > p.kv_rows) {
+    if (p.rows_follow_offset) kv_row0 = offset;
+    if (offset < 0 || static_cast<long long>(kv_row0) + p.L > p.kv_rows) {
       if (t == 0 && tid == 0) atomicExch(&g_device_status, RIB_ECAPACITY);
       return;
     }
@@ -172,7 +194,7 @@ struct BatchParams {
   const int32_t *caps;          // [B]
   const int32_t *pos;           // [B] positions (the row written)
   int nq, nkv;
-  double inv_freq[64];
+  float inv_freq[64];   // rope_inv_freq
 };
 
 __global__ void __launch_bounds__(1024) qk_norm_rope_batched_kernel(const __grid_constant__ BatchParams p) {

@@ -131,7 +131,7 @@ bool bind_stream_device(void *stream) {
 // ------------------------------------------------------------------ rope
 int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offset, int nq, int nkv,
                 double base, int Lp, void *q_out, void *kv, int kv_rows, int kv_row0, void *stream,
-                const int32_t *offset_dev = nullptr) {
+                const int32_t *offset_dev = nullptr, bool rows_follow_offset = true) {
   if (L < 1 || Lp < L || nq < 1 || nkv < 1 || nq + 2 * nkv > rib::rope::kMaxItems || offset < 0 ||
       !(base > 0.0) || kv_rows < 1)
     return RIB_EINVAL;
@@ -153,7 +153,8 @@ int rope_launch(const void *qkv, int L, const void *qw, const void *kw, int offs
   p.kv_rows = kv_rows;
   p.kv_row0 = kv_row0;
   p.offset_dev = offset_dev;
-  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
+  p.rows_follow_offset = rows_follow_offset ? 1 : 0;
+  rib::rope::rope_inv_freq(p.inv_freq, base);
   const int items = nq + 2 * nkv;
   const int threads = ((items + 1) / 2) * 32;
   // One CTA per token: measured faster on B200 for a 4096-token prompt
@@ -477,6 +478,20 @@ int rib_take_device_status(int *status_host) {
   return RIB_OK;
 }
 
+int rib_set_wait_limit_ns(unsigned long long ns) {
+  if (ns < 1000000ull || ns > 60000000000ull) return RIB_EINVAL;
+  const cudaError_t e = cudaMemcpyToSymbol(rib::g_wait_limit_ns, &ns, sizeof(ns));
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemcpyToSymbol(wait limit)", e);
+  return RIB_OK;
+}
+
+int rib_get_wait_limit_ns(unsigned long long *ns) {
+  if (!ns) return RIB_EINVAL;
+  const cudaError_t e = cudaMemcpyFromSymbol(ns, rib::g_wait_limit_ns, sizeof(*ns));
+  if (e != cudaSuccess) return rib::host_fail_cuda("cudaMemcpyFromSymbol(wait limit)", e);
+  return RIB_OK;
+}
+
 int rib_qk_norm_rope(const void *qkv, const void *qw, const void *kw, int pos, int nq, int nkv,
                      double base, void *q_out, void *kv_out, void *stream) {
   return rope_launch(qkv, 1, qw, kw, pos, nq, nkv, base, 1, q_out, kv_out, 1, 0, stream);
@@ -732,7 +747,7 @@ int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw, do
   p.early = 1;
   p.qw = static_cast<const uint16_t *>(qw);
   p.kw = static_cast<const uint16_t *>(kw);
-  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
+  rib::rope::rope_inv_freq(p.inv_freq, base);
   p.cache = nullptr;
   p.cache_ptrs = cache_ptrs;
   p.lens = lens;
@@ -752,6 +767,14 @@ int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL, i
 
 
 // ------------------------------------------------------------------ model kernels
+int rib_qk_norm_rope_prefill_dev(const void *qkv, int L, const void *qw, const void *kw,
+                                 const int32_t *offset_dev, int nq, int nkv, double base, int Lp,
+                                 void *q_out, void *kv_out, void *stream) {
+  if (L < 1 || !offset_dev) return RIB_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(offset_dev) & 3u)) return RIB_EALIGN;
+  return rope_launch(qkv, L, qw, kw, 0, nq, nkv, base, Lp, q_out, kv_out, L, 0, stream, offset_dev, false);
+}
+
 int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw, const void *kw,
                                 const int32_t *offset_dev, int nq, int nkv, double base, int Lp,
                                 void *q_out, void *cache, int cap, void *stream) {
@@ -996,7 +1019,7 @@ int rib_qwen3_decode_step(const rib_qwen3_model *m, const uint64_t *cache_ptrs, 
                   static_cast<const uint16_t *>(w.in_norm), static_cast<const uint16_t *>(w.post_norm),
                   static_cast<const uint16_t *>(w.q_norm), static_cast<const uint16_t *>(w.k_norm)};
   }
-  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(m->rope_theta, -static_cast<double>(d) / 64.0);
+  rib::rope::rope_inv_freq(p.inv_freq, m->rope_theta);
   p.cache_ptrs = cache_ptrs;
   p.tok = token;
   p.pos = pos;
@@ -1082,7 +1105,7 @@ int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw, const void 
   p.pos = pos;
   p.nq = nq;
   p.nkv = nkv;
-  for (int d = 0; d < 64; ++d) p.inv_freq[d] = std::pow(base, -static_cast<double>(d) / 64.0);
+  rib::rope::rope_inv_freq(p.inv_freq, base);
   const int threads = ((nq + 2 * nkv + 1) / 2) * 32;
   return launch_pdl("qk_norm_rope_batched_kernel launch", rib::rope::qk_norm_rope_batched_kernel, dim3(batch),
                     dim3(threads), 0, static_cast<cudaStream_t>(stream), p);

@@ -16,7 +16,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._tensors import HEAD_DIM, as_int, require_bf16_cuda, require_same_device, stream_handle
+from ._tensors import HEAD_DIM, as_int, device_position, require_bf16_cuda, require_same_device, stream_handle
 
 
 def _check_common(qkv, qw, kw, nq: int, nkv: int) -> int:
@@ -37,13 +37,22 @@ def qk_norm_rope(qkv, qw, kw, pos, nq: int, nkv: int, base: float):
 
     qkv: [(nq+2nkv)*128] (or [1, ...]) projection output of one token.
     Returns q [1, nq, 1, 128] and kv [2, nkv, 1, 128] (K and V stacked),
-    as agent-test/v2/kernels.py:157-164."""
+    as agent-test/v2/kernels.py:157-164.  pos: an int, or a 1-element int32
+    tensor as the engine passes it (engine.py:148); a CUDA tensor is read by
+    the kernel on the device, so the call does not synchronise the host."""
     L = _check_common(qkv, qw, kw, nq, nkv)
     if L != 1:
         raise ValueError("qk_norm_rope takes one token; use qk_norm_rope_prefill for L > 1")
-    pos = as_int(pos, "pos")
     q = torch.empty((1, nq, 1, HEAD_DIM), dtype=torch.bfloat16, device=qkv.device)
     kv = torch.empty((2, nkv, 1, HEAD_DIM), dtype=torch.bfloat16, device=qkv.device)
+    pos_dev = device_position(pos, "pos", qkv.device)
+    if pos_dev is not None:
+        st = _lib.load().rib_qk_norm_rope_prefill_dev(qkv.data_ptr(), 1, qw.data_ptr(), kw.data_ptr(),
+                                                      pos_dev.data_ptr(), nq, nkv, float(base), 1, q.data_ptr(),
+                                                      kv.data_ptr(), stream_handle(qkv.device))
+        _lib.check(st, "qk_norm_rope")
+        return q, kv
+    pos = as_int(pos, "pos")
     st = _lib.load().rib_qk_norm_rope(qkv.data_ptr(), qw.data_ptr(), kw.data_ptr(), pos, nq, nkv,
                                       float(base), q.data_ptr(), kv.data_ptr(),
                                       stream_handle(qkv.device))
@@ -54,13 +63,21 @@ def qk_norm_rope(qkv, qw, kw, pos, nq: int, nkv: int, base: float):
 def qk_norm_rope_prefill(qkv, qw, kw, offset, nq: int, nkv: int, base: float, Lp: int):
     """qkv [L, (nq+2nkv)*128] -> Q [nq, Lp, 128] (pad rows zero), KV [2, nkv, L, 128].
 
-    Tokens sit at positions offset .. offset+L-1 (agent-test/v2/kernels.py:215-224)."""
+    Tokens sit at positions offset .. offset+L-1 (agent-test/v2/kernels.py:215-224);
+    a 1-element CUDA int32 offset is read on the device."""
     L = _check_common(qkv, qw, kw, nq, nkv)
-    offset = as_int(offset, "offset")
     if Lp < L:
         raise ValueError(f"Lp ({Lp}) must be >= L ({L})")
     q = torch.empty((nq, Lp, HEAD_DIM), dtype=torch.bfloat16, device=qkv.device)
     kv = torch.empty((2, nkv, L, HEAD_DIM), dtype=torch.bfloat16, device=qkv.device)
+    off_dev = device_position(offset, "offset", qkv.device)
+    if off_dev is not None:
+        st = _lib.load().rib_qk_norm_rope_prefill_dev(qkv.data_ptr(), L, qw.data_ptr(), kw.data_ptr(),
+                                                      off_dev.data_ptr(), nq, nkv, float(base), Lp, q.data_ptr(),
+                                                      kv.data_ptr(), stream_handle(qkv.device))
+        _lib.check(st, "qk_norm_rope_prefill")
+        return q, kv
+    offset = as_int(offset, "offset")
     st = _lib.load().rib_qk_norm_rope_prefill(qkv.data_ptr(), L, qw.data_ptr(), kw.data_ptr(),
                                               offset, nq, nkv, float(base), Lp, q.data_ptr(),
                                               kv.data_ptr(), stream_handle(qkv.device))
@@ -77,13 +94,17 @@ def qk_norm_rope_append(qkv, qw, kw, offset, nq: int, nkv: int, base: float, cac
     reference's qk_norm_rope[_prefill] + Cache.update pair (engine.py:111-113,
     152-153).  Returns Q [nq, Lp, 128] (Lp defaults to L; pad rows zero).
     Raises ValueError("... KV capacity exceeded") if offset + L > cap
-    (engine.py:45-46)."""
+    (engine.py:45-46).  A 1-element CUDA int32 offset goes to
+    qk_norm_rope_append_at (read on the device, capacity checked there)."""
     L = _check_common(qkv, qw, kw, nq, nkv)
     require_bf16_cuda("cache_layer", cache_layer)
     require_same_device(qkv, cache_layer)
     if cache_layer.dim() != 4 or cache_layer.shape[0] != 2 or cache_layer.shape[1] != nkv \
             or cache_layer.shape[3] != HEAD_DIM:
         raise ValueError(f"cache_layer must be [2, {nkv}, cap, 128], got {tuple(cache_layer.shape)}")
+    off_dev = device_position(offset, "offset", qkv.device)
+    if off_dev is not None:
+        return qk_norm_rope_append_at(qkv, qw, kw, off_dev, nq, nkv, base, cache_layer, Lp)
     offset = as_int(offset, "offset")
     Lp = L if Lp is None else Lp
     if Lp < L:

@@ -272,7 +272,7 @@ class Engine:
                                     self.n_kv, self.base, cache.kv[i], Lp)    # [nq_local, Lp, 128]
             final = i == nl - 1
             if final and not last:
-                break        # last layer's K/V written; its outputs are dead for a middle chunk
+                break        # a middle chunk only needs the final layer's cache rows, now written
             if final and not all_logits:
                 # Only the final row feeds the logits: attention/MLP for one row (engine.py:118-121).
                 qrow = q[:, n - 1, :].contiguous()

@@ -88,9 +88,9 @@ class Scheduler:
         if min(prompt) < 0 or max(prompt) >= self.e.cfg.vocab_size:
             raise ValueError("Token outside vocabulary")
         r = Request(self._next_id, [int(t) for t in prompt], int(max_tokens), frozenset(eos_ids))
-        self._next_id += 1
-        if r.capacity > self.max_len:
+        if r.capacity > self.max_len:  # rejected before it takes an id: ids stay consecutive
             raise ValueError(f"prompt + max_tokens + 1 = {r.capacity} exceeds max_len {self.max_len}")
+        self._next_id += 1
         if max_tokens == 0:
             r.done, r.reason = True, "length"
             self.finished[r.rid] = r

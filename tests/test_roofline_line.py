@@ -1,10 +1,11 @@
 """CPU: the B200 device spec follows the reference's schema, and the
 attention reference lines use the reference's own work counts.
 
-When the reference tree is mounted (this build container), the spec is loaded
-with the reference's src/roofline/device.py:load_device and the counts are
-compared with src/roofline/workload.py:decode/prefill for Qwen3-0.6B; without
-it those two tests skip and the closed-form checks still run."""
+When a checkout of the reference is found (REFERENCE_ROOT; by default the
+one the build container mounts), the spec is loaded with the reference's
+src/roofline/device.py:load_device and the counts are compared with
+src/roofline/workload.py:decode/prefill for Qwen3-0.6B; without it those
+tests skip and the closed-form checks still run."""
 from __future__ import annotations
 
 import importlib
@@ -13,8 +14,10 @@ from pathlib import Path
 
 import pytest
 
-REF_SRC = Path("/root/reference/src")
-REF_MODEL = Path("/root/reference/configs/models/qwen3_0.6b.yaml")
+from oracle.msl.runner import reference_root
+
+REF_SRC = reference_root() / "src"
+REF_MODEL = reference_root() / "configs" / "models" / "qwen3_0.6b.yaml"
 
 
 @pytest.fixture(scope="module")

@@ -203,6 +203,8 @@ def test_scheduler_argument_checks():
         s.submit([1], -1)
     with pytest.raises(ValueError):
         s.submit([1] * 500, 20)               # capacity above max_len
+    # a rejected request takes no id: accepted ones stay consecutive
+    assert [s.submit([1, 2], 3), s.submit([3], 2)] == [0, 1]
 
 
 # ------------------------------------------------------------------ randomized
