@@ -27,6 +27,7 @@ import argparse
 import datetime
 import importlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -47,16 +48,20 @@ NKV_TOTAL = 8
 PREFILL_L = 32768
 
 
+def profile_traffic(name: str) -> dict | None:
+    """The DRAM traffic record of one ncu capture (profiles/<name>.json:
+    dram__bytes_read.sum + dram__bytes_write.sum of the captured launch and
+    the algorithmic bytes or FLOPs it carried), or None."""
+    p = ROOT / "profiles" / f"{name}.json"
+    return json.loads(p.read_text()) if p.exists() else None
+
+
 def decode_traffic_ratio() -> float | None:
-    """DRAM bytes (read + write) per algorithmic KV byte of the decode kernel,
-    from the committed ncu summary of a 4-layer capture; traffic grows with
-    the keys processed, so it scales to any launch of the same kernel."""
-    p = ROOT / "profiles" / "decode_kernel_ctx32k_4layers.md"
-    if p.exists():
-        for line in p.read_text().splitlines():
-            if "traffic_per_algorithmic_byte:" in line:
-                return float(line.split("traffic_per_algorithmic_byte:")[1].strip(" `\n"))
-    return None
+    """DRAM bytes (read + write) per algorithmic KV byte of the decode kernel
+    from a 4-layer capture; traffic grows with the keys processed, so it
+    scales to any launch of the same kernel."""
+    rec = profile_traffic("decode_kernel_traffic")
+    return None if rec is None else float(rec["traffic_per_algorithmic_byte"])
 
 
 def peaks() -> dict:
@@ -218,6 +223,179 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
+# ---------------------------------------------------------------- parity checks
+# Run after the timed regions, on the outputs the timed path produced: a plain
+# PyTorch FP32 restatement on the device (not the CUDA kernels, not the CPU
+# oracle) recomputes a sample of each result from the same seeds, and the
+# error is the max over ranks.  Tolerance: the contract's max-abs <= 2e-2 and
+# mean-abs <= 2e-3 on attention outputs; for the model, logits within 2e-2 of
+# the largest logit and greedy tokens equal unless the reference's top two
+# logits are within that margin (a near tie).
+PARITY_MAX_ABS, PARITY_MEAN_ABS, PARITY_LOGIT_REL = 2e-2, 2e-3, 2e-2
+
+
+def _bf(x: torch.Tensor) -> torch.Tensor:
+    """Round an FP32 tensor to BF16 and back (the kernels' rounding points)."""
+    return x.to(torch.bfloat16).float()
+
+
+def ref_attention(q, K, V, scale, causal_offset=None):
+    """softmax(scale q K^T) V in FP32: q [H, m, 128], K/V [nkv, n, 128] -> [H, m, 128]
+    (GQA head h -> h // (H / nkv)); causal_offset: query i sees keys <= offset + i."""
+    g = q.shape[0] // K.shape[0]
+    Kf = K.float().repeat_interleave(g, 0)
+    Vf = V.float().repeat_interleave(g, 0)
+    s = torch.matmul(q.float(), Kf.transpose(1, 2)) * scale
+    if causal_offset is not None:
+        m, n = q.shape[1], K.shape[1]
+        mask = torch.arange(n, device=q.device)[None, :] > (causal_offset + torch.arange(m, device=q.device))[:, None]
+        s = s.masked_fill(mask, float("-inf"))
+    return torch.matmul(torch.softmax(s, dim=-1), Vf)
+
+
+def attention_errors(got: torch.Tensor, want: torch.Tensor) -> dict:
+    d = (got.float() - want.float()).abs()
+    return {"max_abs": float(d.max()), "mean_abs": float(d.mean())}
+
+
+def reduce_errors(errs: list[dict], world: int, device) -> dict:
+    """Max over the listed checks and over ranks; pass against the contract."""
+    mx = max((e["max_abs"] for e in errs), default=0.0)
+    mean = max((e["mean_abs"] for e in errs), default=0.0)
+    mx, mean = max_over_ranks(mx, world, device), max_over_ranks(mean, world, device)
+    return {"max_abs": mx, "mean_abs": mean, "checks": len(errs) * world,
+            "pass": bool(mx <= PARITY_MAX_ABS and mean <= PARITY_MEAN_ABS)}
+
+
+def ref_rms(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """n = bf16(w * bf16(x * inv)), inv = 1/sqrt(mean(x^2) + 1e-6) (agent-test/v2/kernels.py:48-55)."""
+    inv = torch.rsqrt(x.double().pow(2).mean(-1, keepdim=True) + 1e-6).float()
+    return _bf(w.float() * _bf(x * inv))
+
+
+def ref_rope(x: torch.Tensor, pos: torch.Tensor, base: float) -> torch.Tensor:
+    """Non-traditional RoPE of [n, heads, 128] at positions pos [n]; the angle
+    float(pos) * exp2(-(d/64) log2(base)) in FP32 (kernels.py:134-143)."""
+    d = torch.arange(64, dtype=torch.float32, device=x.device) / 64.0
+    lb = torch.tensor(math.log2(base), dtype=torch.float32, device=x.device)
+    inv = torch.exp2((-d * lb).double()).float()
+    th = (pos.float()[:, None] * inv[None]).double()[:, None, :]
+    c, s = torch.cos(th), torch.sin(th)
+    x1, x2 = x[..., :64].double(), x[..., 64:].double()
+    return _bf(torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1).float())
+
+
+def ref_model_logits(wt, tokens: list[int]) -> torch.Tensor:
+    """FP32 logits of the last of `tokens` from a full causal pass of the
+    Qwen3 forward (agent-test/v2/engine.py:102-142) in plain PyTorch on the
+    device, BF16 rounding where the reference's kernels round."""
+    cfg = wt.config
+    nq, nkv = cfg.num_heads, cfg.num_kv_heads
+    dev = wt.embed.device
+    idx = torch.tensor(tokens, dtype=torch.long, device=dev)
+    n = len(tokens)
+    pos = torch.arange(n, device=dev)
+    h = wt.embed[idx].float()
+    x = ref_rms(h, wt.layers[0]["in_norm"])
+    for i, l in enumerate(wt.layers):
+        qkv = _bf(x @ l["qkv"].float().t()).reshape(n, nq + 2 * nkv, 128)
+        q = ref_rope(ref_rms(qkv[:, :nq], l["q_norm"]), pos, cfg.rope_theta)
+        k = ref_rope(ref_rms(qkv[:, nq:nq + nkv], l["k_norm"]), pos, cfg.rope_theta)
+        v = qkv[:, nq + nkv:]
+        o = ref_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1), 128 ** -0.5,
+                          causal_offset=0)
+        o = _bf(o.transpose(0, 1).reshape(n, nq * 128))
+        h = _bf(h + _bf(o @ l["o"].float().t()))
+        x = ref_rms(h, l["post_norm"])
+        gu = _bf(x @ l["gu"].float().t())
+        F = gu.shape[-1] // 2
+        g, u = gu[:, :F], gu[:, F:]
+        a = _bf(_bf(g * _bf(torch.sigmoid(g))) * u)
+        h = _bf(h + _bf(a @ l["down"].float().t()))
+        if i + 1 < len(wt.layers):
+            x = ref_rms(h, wt.layers[i + 1]["in_norm"])
+    return ref_rms(h[-1:], wt.final_norm)[0] @ wt.embed.float().t()
+
+
+def decode_sweep_parity(out_full: torch.Tensor, world: int, device, ctx: int = CTX,
+                        layers=(0, N_LAYERS - 1)) -> dict:
+    """The decode sweep's outputs [28, 16, 128] (every head of every layer,
+    gathered over NVLink at N > 1) against the FP32 restatement for `layers`,
+    regenerated from the workload's seeds."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    n = ctx + 1
+    errs = []
+    for layer in layers:
+        K = torch.empty((NKV_TOTAL, n, 128), dtype=torch.bfloat16, device=device)
+        V = torch.empty_like(K)
+        for h in range(NKV_TOTAL):
+            K[h] = wl.randn_bf16((n, 128), seed=(layer * 64 + h) * 2, device=device)
+            V[h] = wl.randn_bf16((n, 128), seed=(layer * 64 + h) * 2 + 1, device=device)
+        q = torch.cat([wl.randn_bf16((2, 128), seed=900000 + layer * 64 + h, device=device)
+                       for h in range(NKV_TOTAL)])
+        want = ref_attention(q[:, None], K, V, 128 ** -0.5)[:, 0]
+        errs.append(attention_errors(out_full[layer], want))
+        del K, V
+    r = reduce_errors(errs, world, device)
+    r["sample"] = f"layers {list(layers)}, all 16 heads, {n} keys"
+    return r
+
+
+def model_parity(rib, world: int, device, steps: int = 6) -> dict:
+    """The Qwen3 forward (2 layers at Qwen3-0.6B widths, vocab 151936, seeded
+    random weights) as the bench runs it -- one GPU, or at N > 1 KV-head
+    sharded and tensor parallel -- against ref_model_logits: the prefill's
+    logits of a 37-token prompt, then `steps` decode steps teacher-forced with
+    the reference's greedy tokens (eager path), and the greedy tokens of
+    Engine.generate (the CUDA-graph step) against the reference's greedy
+    continuation."""
+    cfg = rib.Qwen3Config(num_layers=2)
+    wt = rib.random_weights(cfg, seed=11, device=device)
+    g = torch.Generator().manual_seed(5)
+    prompt = [int(t) for t in torch.randint(0, cfg.vocab_size, (37,), generator=g)]
+    # the reference's greedy continuation, with each step's top-two margin
+    ref_toks, margins, ref_logits = list(prompt), [], []
+    for _ in range(steps + 1):
+        lg = ref_model_logits(wt, ref_toks)
+        top = torch.topk(lg, 2).values
+        margins.append(float((top[0] - top[1]) / lg.abs().max()))
+        ref_logits.append(lg)
+        ref_toks.append(int(torch.argmax(lg)))
+    modes = [("single_gpu", {})] if world == 1 else [("kv_head_shard", {"shard": True}),
+                                                     ("tensor_parallel", {"tp": True})]
+    out = {}
+    for name, kw in modes:
+        eng = rib.Engine(wt, **kw)
+        cache = eng.new_cache(64)
+        lg = eng.prefill(torch.tensor(prompt, dtype=torch.int32, device=device), cache, last=True).reshape(-1)
+        worst, tok_ok = 0.0, True
+        for t in range(steps + 1):
+            ref = ref_logits[t]
+            worst = max(worst, float((lg - ref).abs().max() / ref.abs().max()))
+            if int(torch.argmax(lg)) != ref_toks[len(prompt) + t] and margins[t] > PARITY_LOGIT_REL:
+                tok_ok = False
+            if t < steps:
+                lg = eng.decode(torch.tensor([ref_toks[len(prompt) + t]], dtype=torch.int32, device=device),
+                                cache, return_logits=True).reshape(-1)
+        gen = list(eng.generate(prompt, max_tokens=steps + 1))
+        gen_ok = True
+        for t, tok in enumerate(gen):
+            if tok != ref_toks[len(prompt) + t]:
+                gen_ok = margins[t] <= PARITY_LOGIT_REL  # a near tie: later tokens may diverge
+                break
+        eng.close()
+        worst = max_over_ranks(worst, world, device)
+        ok = max_over_ranks(0.0 if (tok_ok and gen_ok) else 1.0, world, device) == 0.0
+        out[name] = {"logits_max_rel": worst, "tokens_ok": ok,
+                     "pass": bool(ok and worst <= PARITY_LOGIT_REL)}
+    out["sample"] = (f"2 layers, Qwen3-0.6B widths, 37-token prompt + {steps} teacher-forced decode steps; "
+                     f"greedy tokens of Engine.generate (CUDA-graph step)")
+    out["pass"] = all(v["pass"] for k, v in out.items() if isinstance(v, dict))
+    del wt
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------- CPU leg
 def cpu_sample_workload(layers_sample: int = 4, ctx: int = CTX):
     """Host copies of `layers_sample` layers of the decode sweep (the same
@@ -352,6 +530,9 @@ def run_ours(args):
         barrier(world)
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world, device)
+    # parity of the timed step's own outputs (every rank's heads at N > 1)
+    parity = {"decode_sweep": decode_sweep_parity(gather.output() if gather is not None else plan.out,
+                                                  world, device)}
     # Each step is exactly one launch of the decode kernel, so the average
     # launch duration is this rank's timed region over K.  (Events recorded
     # between the launches would split the programmatic-dependent-launch
@@ -408,14 +589,20 @@ def run_ours(args):
 
     # ---- batched ragged decode (64 sequences), sequence-sharded
     ragged = run_ragged(rib, rank, world, device, args, pk)
+    parity["ragged_batch"] = ragged.pop("parity")
 
     # ---- prefill (tcgen05 kernel), one GPU's view
     prefill = run_prefill(rib, device, args, pk) if not args.no_prefill else None
+    if prefill is not None and "unavailable" not in prefill:
+        prefill["by_length"] = run_prefill_sweep(rib, device, args, pk)
 
     # ---- the full Qwen3-0.6B forward (one replica per GPU)
     full_model = run_full_model(rib, rank, world, device, args) if not args.no_model else None
     if full_model is not None and world > 1:   # the same sequence with the projections split too
         full_model["tensor_parallel"] = run_full_model(rib, rank, world, device, args, tp=True)
+    if not args.no_model:
+        parity["model"] = model_parity(rib, world, device)
+    parity["pass"] = all(v.get("pass", False) for v in parity.values())
 
     device_status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
     if gather is not None:
@@ -442,8 +629,9 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"],
                      "traffic": None if ratio is None else bytes_launch_local * ratio,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
-                                       "profiles/decode_kernel_ctx32k_4layers.md, scaled by keys",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                       "4-layer capture (profiles/decode_kernel_traffic.json), "
+                                       "scaled by keys",
                      "kernel": "rib::decode::decode_kernel",
                      "peak_source": pk["source"] + " hbm_gbs (copy, burst)",
                      "bytes_per_launch": bytes_launch_local, "launch_ms": launch_ms},
@@ -459,6 +647,7 @@ def run_ours(args):
         "gpu_launches": args.steps,
         "device_status": device_status,
         "clocks": clk,
+        "parity": parity,
     }
     rl = importlib.import_module("roofline-inference_b200.roofline_line")
     dline = rl.decode_attention_line(w["n"])
@@ -541,6 +730,20 @@ def run_ragged(rib, rank, world, device, args, pk):
     b.record(stream)
     torch.cuda.synchronize()
     ms = max_over_ranks(a.elapsed_time(b) / args.steps, world, device)
+    # parity of the timed step's outputs: 4 sequences, wherever they ran
+    gout = gather.output() if gather is not None else None
+    errs = []
+    for i in range(4):
+        r = next(rr for rr in range(world) if i in assign[rr])
+        j = assign[r].index(i)
+        got = gout[j, 16 * r:16 * r + 16] if gout is not None else out[j]
+        kv = wl.randn_bf16((2, NKV_TOTAL, lens[i], 128), seed=1000 + i, device=device)
+        want = ref_attention(wl.randn_bf16((16, 128), seed=2000 + i, device=device)[:, None], kv[0], kv[1],
+                             128 ** -0.5)[:, 0]
+        errs.append(attention_errors(got, want))
+        del kv
+    parity = reduce_errors(errs, world, device)
+    parity["sample"] = "sequences 0-3 (all 16 heads), read from the rank and slot that ran them"
     if gather is not None:
         gather.close()
     total = sum(4096 * n for n in lens)
@@ -548,7 +751,7 @@ def run_ragged(rib, rank, world, device, args, pk):
     return {"value": v, "unit": "GB/s", "ms_per_step": ms, "sequences": len(lens),
             "kv_bytes_per_step": total, "frac_of_hbm_peak_x_gpus": v / (pk["hbm_gbs"] * world),
             "sharding": f"sequences, LPT by context, {slots} slots per rank",
-            "contexts": "U[512, 32768], seed 0"}
+            "contexts": "U[512, 32768], seed 0", "parity": parity}
 
 
 def run_e2e(rib, w, rank, world, device, args, gather, plan):
@@ -647,6 +850,76 @@ def run_prefill(rib, device, args, pk):
                          "peak_sustained": pk["bf16_tflops_sustained"],
                          "frac_of_sustained": tf / pk["bf16_tflops_sustained"],
                          "kernel": "rib::prefill::prefill_kernel"}}
+
+
+def run_prefill_sweep(rib, device, args, pk) -> dict:
+    """Causal prefill at every prompt length of the prefill configuration,
+    L in {16, 64, 256, 1024, 4096, 32768}, with the fused work in the timed
+    call: per call the pre-norm qkv rows [L, 4096] go through the fused
+    per-head RMSNorm + RoPE (theta 1e6, positions 0..L-1) + KV-cache append
+    (rib.qk_norm_rope_append) and then the causal attention over the written
+    cache (rib.attention), the order Engine.prefill runs them.
+
+    Device time: the pair is captured once in a CUDA graph and replayed; L2 is
+    flushed (a 256 MB write) before every replay and CUDA events bracket the
+    replay alone.  Host-to-host time: the same pair called eagerly through
+    the public API, back to back (the host path a short prompt pays).
+    TFLOP/s counts the attention's 4096 L (L + 1) FLOPs; the append moves
+    16 KiB per token (qkv read, Q and K/V written)."""
+    wl = importlib.import_module("roofline-inference_b200.workloads")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    out = {}
+    for L in (16, 64, 256, 1024, 4096, 32768):
+        qkv, qw, kw = wl.prefill_qkv(L, seed=L + 3, device=device)
+        cap = wl.round_cap(L)
+        cache = torch.zeros((2, 8, cap, 128), dtype=torch.bfloat16, device=device)
+        Lp = (L + 31) // 32 * 32
+
+        def pair():
+            Q = rib.qk_norm_rope_append(qkv, qw, kw, 0, 16, 8, wl.ROPE_THETA, cache, Lp)
+            return rib.attention(Q, cache[0:1], cache[1:2], L, L, wl.SCALE)
+
+        for _ in range(max(args.warmup, 3)):
+            pair()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            pair()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=side):
+                pair()
+        torch.cuda.synchronize()
+        reps = 10 if L == 32768 else 30
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for a, b in evs:
+            flush.zero_()
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+        torch.cuda.synchronize()
+        dev_ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            pair()
+        b.record(stream)
+        torch.cuda.synchronize()
+        eager_ms = a.elapsed_time(b) / reps
+        del g
+        fl = wl.prefill_flops(L)
+        tf = fl / (dev_ms * 1e-3) / 1e12
+        out[str(L)] = {"us_device": dev_ms * 1e3, "us_eager": eager_ms * 1e3, "tflops": tf,
+                       "frac_of_bf16_peak": tf / pk["bf16_tflops"], "flops": fl,
+                       "append_bytes": 16384 * L}
+        del qkv, cache
+        torch.cuda.empty_cache()
+    return {"lengths": out, "unit": "TFLOP/s (attention FLOPs over the fused append + attention time)",
+            "timing": "device: CUDA-graph replay of the pair, L2 flushed before each, median of 10-30; "
+                      "eager: public API back to back"}
 
 
 def sm_clock_mhz(device):
@@ -975,7 +1248,9 @@ def run_case(case: str):
     64-sequence ragged batched decode step (contexts U[512, 4096], 17.9 GB
     of K/V): the capture's eager warm-up step and 3 graph replays;
     model-prefill is three 4096-token prefills of Qwen3-0.6B (last row's
-    logits), the TTFT path of the request benchmark."""
+    logits), the TTFT path of the request benchmark; gemm is one launch of
+    each Qwen3 prefill projection at 4096 tokens (O, gate/up + SwiGLU, down,
+    QKV + norm + RoPE + append)."""
     rib = load_rib()
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
@@ -1005,6 +1280,18 @@ def run_case(case: str):
         toks = toks.to(torch.int32).to(device)
         for _ in range(3):
             eng.prefill(toks, eng.new_cache(4096 + 256), last=True)
+    elif case == "gemm":
+        G = importlib.import_module("roofline-inference_b200.gemm")
+        M = 4096
+        x = wl.randn_bf16((M, 1024), seed=81, device=device)
+        for N, K, epi in ((1024, 2048, "bf16"), (6144, 1024, "swiglu"), (1024, 3072, "bf16")):
+            A = x if K == 1024 else wl.randn_bf16((M, K), seed=K, device=device)
+            W = wl.randn_bf16((N, K), seed=N, device=device, scale=0.02)
+            G.gemm(A, W, epi=epi)
+        W = wl.randn_bf16((4096, 1024), seed=82, device=device, scale=0.02)
+        qw, kw = wl.norm_weights(1, device), wl.norm_weights(2, device)
+        cache = torch.zeros((2, 8, M, 128), dtype=torch.bfloat16, device=device)
+        G.gemm_qkv_rope(x, W, qw, kw, G.rope_table(0, M, 1e6, device), 0, 16, 8, cache, M)
     elif case == "model-batch":
         eng = rib.Engine(rib.random_weights(rib.QWEN3_0_6B, seed=11, device=device))
         _, dec = batch_workload(eng, device, 8)
@@ -1031,7 +1318,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "model-decode", "model-prefill",
+    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "model-decode", "model-prefill", "gemm",
                              "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()

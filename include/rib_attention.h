@@ -80,7 +80,9 @@ int rib_get_wait_limit_ns(unsigned long long *ns);
  *   q_out  [nq, 128]              == the reference's q [1, nq, 1, 128]
  *   kv_out [2, nkv, 128]          == the reference's kv [2, nkv, 1, 128]
  * RMSNorm eps is 1e-6; rounding points n = bf16(w * bf16(x * inv)); RoPE is
- * the non-traditional form pairing (d, d+64) with theta = pos * base^(-d/64).
+ * the non-traditional form pairing (d, d+64) with theta = pos * base^(-d/64),
+ * formed in FP32 as the reference forms it (float(pos) * exp2(-(d/64) *
+ * log2(base)), kernels.py:134-138) and evaluated to full accuracy.
  * V is copied bit for bit.
  * ------------------------------------------------------------------------ */
 int rib_qk_norm_rope(const void *qkv, const void *qw, const void *kw, int pos,
@@ -228,6 +230,12 @@ int rib_peer_buffer_open(int device, const void *ipc_handle, void **peer_ptr);
 int rib_peer_buffer_close(int device, void *peer_ptr);
 int rib_peer_buffer_free(int device, void *dev_ptr);
 
+/* Host-epoch form.  lens, cache_ptrs and every cache row below lens[b] - 1
+ * must be complete when the launch starts (written by host copies, by a
+ * kernel that does not trigger programmatic launch, or earlier): each CTA
+ * streams its first K/V tiles before waiting for the previous kernel, so a
+ * call overlaps the previous call's exchange with the peers.  q and the new
+ * token's row may come from the kernel launched just before. */
 int rib_decode_attention_gather(const void *q, const uint64_t *cache_ptrs,
                                 const int32_t *lens, int batch, int max_n,
                                 int cap, int nq, int nkv, float scale,
@@ -261,10 +269,18 @@ int rib_decode_attention_gather_dev(const void *q, const uint64_t *cache_ptrs,
  *   O      [qL, H * 128]         o_proj input layout (attention.py:10)
  * Causal mask is bottom-right aligned: query i sees keys <= kL - qL + i
  * (attention.py:24, 111).  Requires H == 2 * nkv, qL <= qLp, qL <= kL <= cap.
+ *   workspace  device scratch of rib_prefill_workspace_bytes(kL, nkv) bytes
+ *              (16-byte aligned): the call writes an FP16 copy of V there
+ *              and runs P.V in FP16 (the reference keeps P in FP32,
+ *              attention.py:141-153; FP16 P keeps the error at the BF16
+ *              rounding floor).  V values beyond the FP16 range (|v| > 65504)
+ *              are recorded as RIB_EINVAL on the device status word.
  * ------------------------------------------------------------------------ */
+size_t rib_prefill_workspace_bytes(int kL, int nkv);
 int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL,
                           int kL, int qLp, int cap, int H, int nkv,
-                          float scale, void *O, void *stream);
+                          float scale, void *O, void *workspace,
+                          size_t workspace_bytes, void *stream);
 
 /* ======================================================================== *
  * Qwen3 forward around the attention path (agent-test/v2/engine.py:102-163).
@@ -447,6 +463,41 @@ int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw,
                              int nq, int nkv, float scale, void *out,
                              void *workspace, size_t workspace_bytes,
                              void *stream);
+
+/* ------------------------------------------------------------------------ *
+ * Prefill projections: a persistent tcgen05 GEMM C = epi(A W^T) with
+ * A [M][K] and W [N][K] row-major BF16 (K a multiple of 64).  Replaces the
+ * matmul the reference's engine runs for prompts of more than 32 tokens
+ * (agent-test/v2/engine.py:95-99; mx.matmul, a library GEMM) and fuses what
+ * follows it in Engine.prefill (engine.py:110-135).
+ *   RIB_GEMM_BF16    C [M][ldc] = bf16(A W^T); N a multiple of 8
+ *   RIB_GEMM_F32     C [M][ldc] FP32 (tensor-parallel partial sums, logits)
+ *   RIB_GEMM_SWIGLU  W = [gate; up] (N = 2F rows, F a multiple of 128);
+ *                    C [M][ldc >= F] = bf16(bf16(g bf16(sigmoid g)) u),
+ *                    g = bf16(A Wg^T), u = bf16(A Wu^T) (engine.py:28-30)
+ * ------------------------------------------------------------------------ */
+#define RIB_GEMM_BF16 0
+#define RIB_GEMM_F32 1
+#define RIB_GEMM_SWIGLU 2
+int rib_gemm(const void *A, int M, int K, const void *W, int N, int epi,
+             void *C, long long ldc, void *stream);
+
+/* (cos, sin) FP32 pairs [count][64] of the RoPE angles of positions
+ * pos0 .. pos0 + count - 1 (theta as kernels.py:134-138 forms it), the
+ * table rib_gemm_qkv_rope reads.  16-byte aligned, count * 512 bytes. */
+int rib_rope_table(int pos0, int count, double base, void *table, void *stream);
+
+/* The QKV projection of M prompt tokens fused with the per-head QK-RMSNorm,
+ * RoPE and KV-cache append: replaces matmul(x, qkv) -> qk_norm_rope_prefill
+ * -> Cache.update (engine.py:111-113; kernels.py:169-224) without writing
+ * the qkv activations.  W [(nq + 2 nkv) * 128][K] in the engine's fused
+ * order (q heads, k heads, v heads); qw, kw [128]; rope_table from
+ * rib_rope_table(pos0, >= M, ...).  Writes Q [nq][Lp][128] (rows [M, Lp)
+ * zero) and cache rows pos0 .. pos0 + M - 1 of cache [2][nkv][cap][128]. */
+int rib_gemm_qkv_rope(const void *A, int M, int K, const void *W, int nq,
+                      int nkv, const void *qw, const void *kw,
+                      const void *rope_table, int pos0, void *q_out, int Lp,
+                      void *cache, int cap, void *stream);
 
 /* Greedy token of each row of x [rows, n] FP32 (the first index on ties). */
 int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out,

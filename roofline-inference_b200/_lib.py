@@ -108,7 +108,8 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_decode_attention": ([vp, vp, i, i, i, i, f, vp, vp, sz, vp], i),
         "rib_decode_attention_noalloc": ([vp, vp, i, i, i, i, f, vp, vp], i),
         "rib_decode_attention_batched": ([vp, vp, vp, i, i, i, i, i, f, vp, vp, sz, vp], i),
-        "rib_prefill_attention": ([vp, vp, vp, i, i, i, i, i, i, f, vp, vp], i),
+        "rib_prefill_workspace_bytes": ([i, i], sz),
+        "rib_prefill_attention": ([vp, vp, vp, i, i, i, i, i, i, f, vp, vp, sz, vp], i),
         "rib_qk_norm_rope_append_dev": ([vp, i, vp, vp, vp, i, i, d, i, vp, vp, i, vp], i),
         "rib_qk_norm_rope_prefill_dev": ([vp, i, vp, vp, vp, i, i, d, i, vp, vp, vp], i),
         "rib_gemv": ([vp, i, i, vp, vp, vp, i, i, vp, vp], i),

@@ -42,6 +42,23 @@ def decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
         return ws
 
 
+_prefill_workspaces: dict = {}
+
+
+def prefill_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Scratch of the prefill kernel (its FP16 copy of V), one buffer per
+    (device, stream), grown on demand; a separate buffer from the decode
+    workspace, whose counter region must stay zero."""
+    key = (device.index if device.index is not None else torch.cuda.current_device(),
+           stream_handle(device))
+    with _ws_lock:
+        ws = _prefill_workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _prefill_workspaces[key] = ws
+        return ws
+
+
 # --------------------------------------------------------------- decode
 def decode_attention(q, cache_layer, n: int, scale: float):
     """One query token against the first `n` keys of one cache layer.
@@ -219,8 +236,10 @@ def attention(Q, K, V, qL: int, kL: int, scale: float, nsg=4, bk=16, kt=False, v
         raise ValueError(f"need 1 <= qL <= qLp and qL <= kL <= cap (qL={qL}, qLp={qLp}, "
                          f"kL={kL}, cap={cap})")
     out = torch.empty((qL, H * HEAD_DIM), dtype=torch.bfloat16, device=Q.device)
-    st = _lib.load().rib_prefill_attention(Q.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), qL, kL, qLp,
-                                           cap, H, nkv, float(scale), out.data_ptr(),
-                                           stream_handle(Q.device))
+    L = _lib.load()
+    ws = prefill_workspace(Q.device, int(L.rib_prefill_workspace_bytes(kL, nkv)))
+    st = L.rib_prefill_attention(Q.data_ptr(), Kc.data_ptr(), Vc.data_ptr(), qL, kL, qLp, cap, H, nkv,
+                                 float(scale), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 stream_handle(Q.device))
     _lib.check(st, "attention")
     return out

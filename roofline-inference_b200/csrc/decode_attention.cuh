@@ -106,7 +106,7 @@ struct Params {
   const uint16_t *qkv;
   const uint16_t *qw, *kw;
   float inv_freq[64];   // rope_inv_freq
-  // early (decode_kernel only): lens, caps, cache_ptrs and every cache row
+  // early: lens, caps, cache_ptrs and every cache row
   // below lens[b] - 1 are complete when the kernel starts, so the producer
   // fills the ring with tiles below the new token's row before the
   // programmatic-launch wait; only qkv (and the appended row) come from the

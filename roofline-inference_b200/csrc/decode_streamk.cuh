@@ -134,7 +134,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
   StreamSmem &s =
       *reinterpret_cast<StreamSmem *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   pdl_launch_dependents();
-  pdl_wait();
+  // With early, lens, caps, cache_ptrs and every cache row below lens[b] - 1
+  // are complete when the kernel starts: the prefix scan and the producer's
+  // first ring of such tiles run before the programmatic-launch wait.
+  if (!p.early) pdl_wait();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   // ---- tiles per sequence (all heads), exclusive prefix over sequences.
@@ -201,7 +204,10 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
   const int tpc = max((T + G - 1) / G, kStreamMinTiles);
   const int t_begin = blockIdx.x * tpc;
   const int t_end = min(T, t_begin + tpc);
-  if (t_begin >= t_end) return;  // CTA-uniform
+  if (t_begin >= t_end) {  // CTA-uniform
+    if (p.early) pdl_wait();
+    return;
+  }
 
   if (tid == 0) {
 #pragma unroll
@@ -221,6 +227,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
     const uint16_t *Kh = nullptr, *Vh = nullptr;
     int n = 0;
     bool fresh = true;
+    bool waited = !p.early;
     for (int t = t_begin; t < t_end; ++t) {
       if (t >= u.uend) {
         u = locate(s, B, p.nkv, t);
@@ -236,8 +243,14 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
       }
       const int g = t - t_begin, k = g / NCW;
       const int slot = (g % NCW) * SPW + k % SPW;
-      if (k >= SPW && !mbar_wait(&s.empty[slot], ((k / SPW) - 1) & 1)) return;
       const int k0 = (t - u.ustart) * TK;
+      // early: a full ring, and only tiles that end below the new token's row,
+      // go out before the wait
+      if (!waited && (g >= STAGES || k0 + TK > n - 1)) {
+        pdl_wait();
+        waited = true;
+      }
+      if (k >= SPW && !mbar_wait(&s.empty[slot], ((k / SPW) - 1) & 1)) return;
       const uint32_t bytes = static_cast<uint32_t>(min(TK, n - k0)) * ROW_BYTES;
       mbar_arrive_expect_tx(&s.full[slot], 2 * bytes);
       bulk_g2s(s.k[slot], Kh + static_cast<size_t>(k0) * D, bytes, &s.full[slot], pol);
@@ -247,6 +260,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
   }
 
   // -------------------------------------------------------------- consumers
+  if (p.early) pdl_wait();  // q and the outputs' readers belong to the previous kernel
   const int ct = tid;  // 0 .. NCT-1
   int kw = 0;          // tiles this warp has consumed (ring position)
   bool dead = false;   // a wait gave up: skip the remaining waits

@@ -1,0 +1,429 @@
+// Persistent BF16 GEMM on sm_100a for the Qwen3 prefill projections:
+// C[M, N] = epi(A[M, K] * W[N, K]^T), tcgen05.mma with the FP32 accumulator
+// in TMEM, both operands staged by TMA.
+//
+// Replaces the library matmul the reference's engine calls for prompts of
+// more than 32 tokens (agent-test/v2/engine.py:95-99: mx.matmul; the
+// skinny_gemm of kernels.py:273-334 covers 8 < M <= 32), and fuses what
+// follows each projection in Engine.prefill (engine.py:110-135):
+//   kBF16    C = bf16(A W^T)                      (O and down projections)
+//   kF32     C = A W^T in FP32                    (tensor-parallel partials)
+//   kSwiGLU  W = [gate; up] (N = 2F rows); C[M, F] = bf16(bf16(g bf16(sigmoid g)) u)
+//            with g = bf16(A Wg^T), u = bf16(A Wu^T)  (engine.py:28-30, 133)
+//   kQKRope  W = the QKV projection; per (token, head) tile: per-head RMSNorm
+//            and RoPE of q and k with the arithmetic of rope::norm_rope8
+//            (kernels.py:116-146, 169-204), Q written to [nq][Lp][128] (pad
+//            rows zero), K and V appended to the cache rows pos0 + m
+//            (engine.py:111-113): the qkv activations never reach HBM.
+//
+// CTA (one per SM, persistent over output tiles of 128 x BN): 6 warps.
+//   warp 0      TMA producer: A and W k-blocks of 64 (128-byte swizzle) into
+//               an NS-stage ring (4 x 48 KB at BN = 256, 6 x 32 KB at 128).
+//   warp 1      TMEM owner and MMA issuer: per k-block 4 x tcgen05.mma
+//               (M = 128, N = BN, K = 16) into one of two accumulators, so
+//               the epilogue of tile i overlaps the main loop of tile i + 1.
+//   warps 2-5   epilogue: thread = accumulator row (TMEM lane quadrant
+//               warp % 4), tcgen05.ld of 32 columns at a time.
+// Every wait is bounded (common.cuh); on a timeout the CTA drains its copies,
+// frees TMEM and returns with RIB_ETIMEOUT recorded.  No TMA multicast.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "qk_norm_rope.cuh"
+
+namespace rib {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle panel of BF16
+constexpr int NWARPS = 6;
+constexpr int NTHREADS = NWARPS * 32;
+constexpr int kEpiThreads = 128;
+
+enum Epi : int { kBF16 = 0, kF32 = 1, kSwiGLU = 2, kQKRope = 3 };
+
+template <int BN>
+struct Cfg {
+  static_assert(BN == 128 || BN == 256, "BN is 128 or 256");
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int NS = BN == 256 ? 4 : 6;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  // kind::f16: D = F32 (bit 4), A = B = BF16 (bits 7, 10), both K-major,
+  // N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
+                                    (static_cast<uint32_t>(BN >> 3) << 17) |
+                                    (static_cast<uint32_t>(BM >> 4) << 24);
+};
+
+template <int BN>
+struct Smem {
+  alignas(1024) uint8_t stage[Cfg<BN>::NS][Cfg<BN>::STAGE];
+  uint64_t full[Cfg<BN>::NS], empty[Cfg<BN>::NS];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Params {
+  CUtensorMap tm_a;   // A [M][K], box (64, 128)
+  CUtensorMap tm_b;   // W [N][K], box (64, BN) (kSwiGLU: (64, BN / 2), two loads)
+  int M, N, K;
+  int num_m, num_tiles;
+  int epi;
+  void *c;            // kBF16 / kSwiGLU: BF16 [M][ldc]; kF32: FP32 [M][ldc]
+  long long ldc;
+  int swiglu_f;       // kSwiGLU: F (up rows start at F)
+  // kQKRope
+  const uint16_t *qw, *kw;  // [128] each
+  const float2 *rope;       // [>= num_m * 128][64] (cos, sin) of positions pos0 + m
+  int pos0, nq, nkv;
+  uint16_t *q_out;          // [nq][Lp][128]
+  int Lp;
+  uint16_t *cache;          // [2][nkv][cap][128]
+  int cap;
+};
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  // K-major, 128-byte swizzle (layout 2 at bits 61-63), sm100 version bit 46,
+  // LBO 16 B (unused), SBO 1024 B (8 rows of 128 B); addresses in 16-byte units.
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0, int c1, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int BN>
+__device__ __forceinline__ bool aborted(const Smem<BN> &s) {
+  return *reinterpret_cast<const volatile int *>(&s.abort_flag) != 0;
+}
+template <int BN>
+__device__ __forceinline__ void set_abort(Smem<BN> &s) {
+  *reinterpret_cast<volatile int *>(&s.abort_flag) = 1;
+}
+
+__device__ __forceinline__ float silu_bf16(float g) {
+  // s = bf16(sigmoid(g)), a = bf16(g s)  (agent-test/v2/kernels.py:86-93),
+  // the arithmetic of model::swiglu_kernel
+  // (__frcp_rn is the correctly rounded reciprocal: the same value as 1.0f / x)
+  const float s = round_bf16(__frcp_rn(1.0f + expf(-g)));
+  return round_bf16(g * s);
+}
+
+// ---------------------------------------------------------------- epilogues
+// Row `m` of the tile's accumulator at TMEM address `ta` (this thread's
+// lane, column 0).  All 32 lanes of the warp execute every tcgen05.ld.
+template <int BN>
+__device__ __forceinline__ void epi_store(const Params &p, uint32_t ta, int m, int n0) {
+  const bool row_ok = m < p.M;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld32(ta + c0, r);
+    tmem_wait_ld();
+    const int ncols = p.N - (n0 + c0);  // columns past N (a ragged last tile) are not stored
+    if (!row_ok || ncols <= 0) continue;
+    if (p.epi == kF32) {
+      float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.c) + m * p.ldc + n0 + c0);
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        if (4 * v < ncols)
+          dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+    } else {
+      uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.c) + m * p.ldc + n0 + c0);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        if (8 * v >= ncols) break;
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+        w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+        w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+        w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+        dst[v] = w;
+      }
+    }
+  }
+}
+
+// kSwiGLU (BN = 256): columns [0, 128) are gate rows f0 .. f0 + 127, columns
+// [128, 256) the matching up rows; writes C[m, f0 .. f0 + 127].
+__device__ __forceinline__ void epi_swiglu(const Params &p, uint32_t ta, int m, int f0) {
+  const bool row_ok = m < p.M;
+#pragma unroll 1
+  for (int c0 = 0; c0 < 128; c0 += 32) {
+    uint32_t g[32], u[32];
+    tmem_ld32(ta + c0, g);
+    tmem_ld32(ta + 128 + c0, u);
+    tmem_wait_ld();
+    if (!row_ok) continue;
+    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.c) + m * p.ldc + f0 + c0);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float gg = round_bf16(__uint_as_float(g[8 * v + e]));
+        const float uu = round_bf16(__uint_as_float(u[8 * v + e]));
+        y[e] = silu_bf16(gg) * uu;
+      }
+      uint4 w;
+      w.x = pack_bf16x2(y[0], y[1]);
+      w.y = pack_bf16x2(y[2], y[3]);
+      w.z = pack_bf16x2(y[4], y[5]);
+      w.w = pack_bf16x2(y[6], y[7]);
+      dst[v] = w;
+    }
+  }
+}
+
+// kQKRope: each 128 columns of the tile are one head `h` of the QKV
+// projection for 128 tokens (a 256-wide tile holds two heads, done one after
+// the other).  The sum of squares is combined in the order rope::norm_rope8 uses
+// (eight-element FMA chains per 16-lane group member, then an xor tree), so
+// for the same BF16 qkv values the outputs are bit-identical to the
+// two-kernel path (GEMM, then qk_norm_rope_append).
+__device__ __forceinline__ void epi_qk_rope(const Params &p, uint32_t ta, int m, int h) {
+  uint32_t r[128];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) tmem_ld32(ta + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
+  tmem_wait_ld();
+  const int nq = p.nq, nkv = p.nkv;
+  if (m >= p.M) {
+    // Q pad rows [M, Lp) are zero (kernels.py:223, init_value=0)
+    if (h < nq && m < p.Lp) {
+      uint4 *dst = reinterpret_cast<uint4 *>(p.q_out + (static_cast<size_t>(h) * p.Lp + m) * 128);
+#pragma unroll
+      for (int v = 0; v < 16; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  float x[128];
+#pragma unroll
+  for (int d = 0; d < 128; ++d) x[d] = round_bf16(__uint_as_float(r[d]));  // the BF16 qkv value
+  uint16_t *dst;
+  if (h >= nq + nkv) {  // V: copied into the cache
+    dst = p.cache + ((static_cast<size_t>(nkv + h - nq - nkv) * p.cap) + p.pos0 + m) * 128;
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+    for (int v = 0; v < 16; ++v) {
+      uint4 w;
+      w.x = pack_bf16x2(x[8 * v + 0], x[8 * v + 1]);
+      w.y = pack_bf16x2(x[8 * v + 2], x[8 * v + 3]);
+      w.z = pack_bf16x2(x[8 * v + 4], x[8 * v + 5]);
+      w.w = pack_bf16x2(x[8 * v + 6], x[8 * v + 7]);
+      d4[v] = w;
+    }
+    return;
+  }
+  // sum of squares: 16 chains of 8 (dims [8j, 8j+8)), then the xor tree 8, 4, 2, 1
+  float s16[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float a = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a = fmaf(x[8 * j + i], x[8 * j + i], a);
+    s16[j] = a;
+  }
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < o; ++j) s16[j] = s16[j] + s16[j + o];
+  const float inv = 1.0f / sqrtf(s16[0] / 128.0f + 1e-6f);
+  const uint16_t *w = h < nq ? p.qw : p.kw;
+  float n[128];
+#pragma unroll
+  for (int v = 0; v < 16; ++v) {
+    const uint4 wr = *reinterpret_cast<const uint4 *>(w + 8 * v);
+    const float wf[8] = {bf16lo(wr.x), bf16hi(wr.x), bf16lo(wr.y), bf16hi(wr.y),
+                         bf16lo(wr.z), bf16hi(wr.z), bf16lo(wr.w), bf16hi(wr.w)};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[8 * v + i] = round_bf16(wf[i] * round_bf16(x[8 * v + i] * inv));
+  }
+  const float2 *cs = p.rope + static_cast<size_t>(m) * 64;
+  float o[128];
+#pragma unroll
+  for (int d = 0; d < 64; ++d) {
+    const float2 t = cs[d];
+    o[d] = fmaf(n[d], t.x, -n[d + 64] * t.y);
+    o[d + 64] = fmaf(n[d], t.y, n[d + 64] * t.x);
+  }
+  dst = h < nq ? p.q_out + (static_cast<size_t>(h) * p.Lp + m) * 128
+               : p.cache + ((static_cast<size_t>(h - nq) * p.cap) + p.pos0 + m) * 128;
+  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+  for (int v = 0; v < 16; ++v) {
+    uint4 wv;
+    wv.x = pack_bf16x2(o[8 * v + 0], o[8 * v + 1]);
+    wv.y = pack_bf16x2(o[8 * v + 2], o[8 * v + 3]);
+    wv.z = pack_bf16x2(o[8 * v + 4], o[8 * v + 5]);
+    wv.w = pack_bf16x2(o[8 * v + 6], o[8 * v + 7]);
+    d4[v] = wv;
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int BN>
+__device__ __forceinline__ bool warp_wait(Smem<BN> &s, uint64_t *bar, uint32_t parity) {
+  bool ok = !aborted(s) && mbar_wait(bar, parity);
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok) set_abort(s);
+  return ok;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  Smem<BN> &s = *reinterpret_cast<Smem<BN> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kblocks = p.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NS; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s.acc_full[b], 1);
+      mbar_init(&s.acc_empty[b], kEpiThreads);
+    }
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tm_a);
+    prefetch_tmap(&p.tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  pdl_launch_dependents();
+  pdl_wait();  // A is the previous kernel's output; C may still be read by it
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        const int m0 = (tile % p.num_m) * BM, nb = tile / p.num_m;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int st = it % C::NS;
+          if (it >= C::NS && (aborted(s) || !mbar_wait(&s.empty[st], ((it / C::NS) - 1) & 1))) {
+            set_abort(s);
+            ok = false;
+            break;
+          }
+          uint8_t *a = s.stage[st];
+          uint8_t *b = a + C::A_BYTES;
+          mbar_arrive_expect_tx(&s.full[st], C::STAGE);
+          tma_load_2d(a, &p.tm_a, kb * BK, m0, &s.full[st]);
+          if (p.epi == kSwiGLU) {  // gate rows f0.., then up rows F + f0..
+            tma_load_2d(b, &p.tm_b, kb * BK, nb * (BN / 2), &s.full[st]);
+            tma_load_2d(b + C::B_BYTES / 2, &p.tm_b, kb * BK, p.swiglu_f + nb * (BN / 2), &s.full[st]);
+          } else {
+            tma_load_2d(b, &p.tm_b, kb * BK, nb * BN, &s.full[st]);
+          }
+        }
+      }
+      // drain: every copy issued must land before the CTA may exit
+      for (int t = max(0, it - C::NS); t < it; ++t) mbar_wait(&s.full[t % C::NS], (t / C::NS) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (lt >= 2 && (aborted(s) || !mbar_wait(&s.acc_empty[buf], ((lt >> 1) - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int st = it % C::NS;
+          if (aborted(s) || !mbar_wait(&s.full[st], (it / C::NS) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(s.stage[st]);
+          const uint32_t b = a + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_ss(d, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (kb | kk) != 0);
+          tc_commit(&s.empty[st]);
+        }
+        if (!ok) break;
+        tc_commit(&s.acc_full[buf]);
+      }
+      if (!ok) set_abort(s);
+      tc_commit(&s.mma_done);
+      mbar_wait(&s.mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (!warp_wait(s, &s.acc_full[buf], (lt >> 1) & 1)) break;
+      tc_fence_after();
+      const int m = (tile % p.num_m) * BM + row, nb = tile / p.num_m;
+      const uint32_t ta = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+      if (p.epi == kSwiGLU) {
+        if constexpr (BN == 256) epi_swiglu(p, ta, m, nb * 128);
+      } else if (p.epi == kQKRope) {
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 128; ++hh) epi_qk_rope(p, ta + 128 * hh, m, nb * (BN / 128) + hh);
+      } else {
+        epi_store<BN>(p, ta, m, nb * BN);
+      }
+      tc_fence_before();
+      mbar_arrive(&s.acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- RoPE table
+// (cos, sin) of the 64 angles of positions pos0 .. pos0 + count - 1, each as
+// rope::rope_angles forms it; one CTA of 64 threads per position.
+__global__ void rope_table_kernel(int pos0, int count, const __grid_constant__ rope::Params rp, float2 *table) {
+  __shared__ float c[64], sn[64];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int i = blockIdx.x;
+  rope::rope_angles(pos0 + i, rp.inv_freq, c, sn, threadIdx.x);
+  __syncthreads();
+  if (threadIdx.x < 64) table[static_cast<size_t>(i) * 64 + threadIdx.x] = make_float2(c[threadIdx.x], sn[threadIdx.x]);
+}
+
+}  // namespace gemm
+}  // namespace rib

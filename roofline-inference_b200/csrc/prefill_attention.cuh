@@ -12,13 +12,20 @@
 // CTA = 128 query rows x one KV head g (query heads 2g, 2g+1), 12 warps in
 // three warpgroups:
 //   warp 0      TMA producer: Q of both heads once, then K and V tiles of
-//               128 keys into a 2-stage ring (128B-swizzled panels).
+//               128 keys into 2-stage rings (128B-swizzled panels).
 //   warp 1      TMEM owner and MMA issuer (one thread):
 //                 S_h = Q_h K^T       SS-MMA, M=N=128, K=128 (8 x K16)
 //                 O_h += P_h V        TS-MMA, A = P_h from TMEM, B = V (MN-major)
 //               issue order PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), so the tensor
 //               pipe works on one head while the other head's softmax runs.
-//   warps 2-3   idle
+//   warps 2-3   idle (they complete the first warpgroup for the register split)
+// P.V runs as an FP16 MMA on FP16 P: P carries 11 significant bits instead of
+// BF16's 8, and the output error stays at the BF16 rounding floor, the
+// accuracy of the reference kernel's FP32 P (attention.py:6, 141-153).  A
+// kind::f16 MMA takes A and B of one type, so V is read from an FP16 copy
+// that v_half_kernel writes once per call (exact for |v| <= 65504; larger
+// values are flagged on the device status word as RIB_EINVAL): 2 bytes per
+// key and head each way, about 0.5% of a 32k prefill's time.
 //   warps 4-7   softmax of head 2g   (one thread per query row / TMEM lane)
 //   warps 8-11  softmax of head 2g+1
 // Registers: launched at 168 per thread; warpgroup 0 gives back to 40
@@ -28,15 +35,17 @@
 // lane, and 128*40 + 256*232 = 384*168, the launch allocation exactly; the
 // host refuses to launch unless the kernel really was built at 168.
 // TMEM (512 columns): S_0 [0,128), S_1 [128,256) as FP32; P_h is written as
-// packed BF16 over the first 64 columns of S_h; O_0 [256,384), O_1 [384,512).
+// packed FP16 over the first 64 columns of S_h; O_0 [256,384), O_1 [384,512).
 // The running max is only raised (and O rescaled) when it grows by more
 // than 8 in log2 units; until then exp2 arguments stay below 8 and P below
-// 256, which BF16 and the FP32 accumulators carry exactly enough.
+// 256, well inside FP16's range, with 11 significant bits.
 // Every wait is bounded (common.cuh); on a timeout the CTA sets a flag,
 // drains, frees TMEM and returns.
 #pragma once
 
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 
@@ -46,7 +55,8 @@ namespace prefill {
 constexpr int D = 128;
 constexpr int BM = 128;  // query rows per CTA
 constexpr int BN = 128;  // keys per tile
-constexpr int NS = 2;    // K/V pipeline stages
+constexpr int NS = 2;    // K pipeline stages
+constexpr int NSV = 2;   // V pipeline stages
 constexpr int NWARPS = 12;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int PANEL_BYTES = 128 * 128;          // [128 rows][64 dims] BF16, one swizzle panel
@@ -70,14 +80,16 @@ constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) |
                                 (static_cast<uint32_t>(BN >> 3) << 17) |
                                 (static_cast<uint32_t>(BM >> 4) << 24);
 constexpr uint32_t kIdescS = kIdescBase;              // A, B K-major
-constexpr uint32_t kIdescPV = kIdescBase | (1u << 16);  // B (= V) MN-major
+// P.V: A = P (TMEM) and B = V (MN-major) both FP16 (format 0 at bits 7-9, 10-12).
+constexpr uint32_t kIdescPV = ((kIdescBase & ~((7u << 7) | (7u << 10)))) | (1u << 16);
 
 struct Smem {
   alignas(1024) uint8_t q[2][TILE_BYTES];
   alignas(1024) uint8_t k[NS][TILE_BYTES];
-  alignas(1024) uint8_t v[NS][TILE_BYTES];
+  alignas(1024) uint8_t v[NSV][TILE_BYTES];
   uint64_t q_full;
-  uint64_t k_full[NS], v_full[NS], kv_empty[NS];
+  uint64_t k_full[NS], k_empty[NS];
+  uint64_t v_full[NSV], v_empty[NSV];
   uint64_t s_full[2], p_full[2], o_full[2];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -133,6 +145,15 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   return d;
 }
 
+// Two BF16 values -> two FP16 values (round to nearest; exact for normal
+// magnitudes up to 65504); `bad` collects results that overflowed to inf
+// (or NaN inputs).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w, uint32_t &bad) {
+  const uint32_t r = pack_f16x2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  bad |= static_cast<uint32_t>((r & 0x7C00u) == 0x7C00u) | static_cast<uint32_t>((r & 0x7C000000u) == 0x7C000000u);
+  return r;
+}
+
 // Causal / length mask of 32 score columns starting at key `key0`.
 __device__ __forceinline__ void mask_chunk(uint32_t (&r)[32], int key0, int my_last, int kL) {
 #pragma unroll
@@ -166,8 +187,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
     mbar_init(&s.q_full, 1);
     for (int i = 0; i < NS; ++i) {
       mbar_init(&s.k_full[i], 1);
+      mbar_init(&s.k_empty[i], 1);
+    }
+    for (int i = 0; i < NSV; ++i) {
       mbar_init(&s.v_full[i], 1);
-      mbar_init(&s.kv_empty[i], 1);
+      mbar_init(&s.v_empty[i], 1);
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&s.s_full[h], 1);
@@ -193,7 +217,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
   const uint32_t tmem = s.tmem_base;
 
   if (warp < 4) {
-    // warpgroup 0: producer, MMA issuer, two idle warps
+    // warpgroup 0: producer, MMA issuer, two V-converter warps
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -202,27 +226,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
       for (int h = 0; h < 2; ++h)
         for (int c = 0; c < 2; ++c)
           tma_load_3d(s.q[h] + c * PANEL_BYTES, &p.tm_q, c * 64, q0, 2 * g + h, &s.q_full);
-      int issued = 0;
+      // K tiles in a 2-stage ring, V tiles in a 3-stage ring: V runs a tile
+      // further ahead, so its FP16 conversion is done before P.V needs it.
+      int issued_k = 0, issued_v = 0;
       for (int t = 0; t < nt; ++t) {
-        const int st = t % NS;
-        if (t >= NS && (aborted(s) || !mbar_wait(&s.kv_empty[st], ((t / NS) - 1) & 1))) {
+        const int sk = t % NS, sv = t % NSV;
+        if (t >= NS && (aborted(s) || !mbar_wait(&s.k_empty[sk], ((t / NS) - 1) & 1))) {
           set_abort(s);
           break;
         }
-        mbar_arrive_expect_tx(&s.k_full[st], TILE_BYTES);
+        mbar_arrive_expect_tx(&s.k_full[sk], TILE_BYTES);
         for (int c = 0; c < 2; ++c)
-          tma_load_3d(s.k[st] + c * PANEL_BYTES, &p.tm_k, c * 64, t * BN, g, &s.k_full[st]);
-        mbar_arrive_expect_tx(&s.v_full[st], TILE_BYTES);
+          tma_load_3d(s.k[sk] + c * PANEL_BYTES, &p.tm_k, c * 64, t * BN, g, &s.k_full[sk]);
+        issued_k = t + 1;
+        if (t >= NSV && (aborted(s) || !mbar_wait(&s.v_empty[sv], ((t / NSV) - 1) & 1))) {
+          set_abort(s);
+          break;
+        }
+        mbar_arrive_expect_tx(&s.v_full[sv], TILE_BYTES);
         for (int c = 0; c < 2; ++c)
-          tma_load_3d(s.v[st] + c * PANEL_BYTES, &p.tm_v, c * 64, t * BN, g, &s.v_full[st]);
-        issued = t + 1;
+          tma_load_3d(s.v[sv] + c * PANEL_BYTES, &p.tm_v, c * 64, t * BN, g, &s.v_full[sv]);
+        issued_v = t + 1;
       }
       // drain: every copy issued must land before the CTA may exit
       mbar_wait(&s.q_full, 0);
-      for (int t = max(0, issued - NS); t < issued; ++t) {
-        mbar_wait(&s.k_full[t % NS], (t / NS) & 1);
-        mbar_wait(&s.v_full[t % NS], (t / NS) & 1);
-      }
+      for (int t = max(0, issued_k - NS); t < issued_k; ++t) mbar_wait(&s.k_full[t % NS], (t / NS) & 1);
+      for (int t = max(0, issued_v - NSV); t < issued_v; ++t) mbar_wait(&s.v_full[t % NSV], (t / NSV) & 1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -251,29 +280,31 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
         tc_commit(&s.s_full[0]);
         issue_s(1, 0);
         tc_commit(&s.s_full[1]);
+        tc_commit(&s.k_empty[0]);  // K stage free once both S MMAs have run
       }
       for (int j = 0; ok && j < nt; ++j) {
-        const int st = j % NS, st1 = (j + 1) % NS;
-        ok = !aborted(s) && mbar_wait(&s.v_full[st], (j / NS) & 1) &&
+        const int sv = j % NSV, sk1 = (j + 1) % NS;
+        ok = !aborted(s) && mbar_wait(&s.v_full[sv], (j / NSV) & 1) &&
              mbar_wait(&s.p_full[0], j & 1);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(0, st, j == 0);
+        issue_pv(0, sv, j == 0);
         tc_commit(&s.o_full[0]);
         if (j + 1 < nt) {
-          if (!(ok = mbar_wait(&s.k_full[st1], ((j + 1) / NS) & 1))) break;
+          if (!(ok = mbar_wait(&s.k_full[sk1], ((j + 1) / NS) & 1))) break;
           tc_fence_after();
-          issue_s(0, st1);
+          issue_s(0, sk1);
           tc_commit(&s.s_full[0]);
         }
         if (!(ok = !aborted(s) && mbar_wait(&s.p_full[1], j & 1))) break;
         tc_fence_after();
-        issue_pv(1, st, j == 0);
+        issue_pv(1, sv, j == 0);
         tc_commit(&s.o_full[1]);
-        tc_commit(&s.kv_empty[st]);
+        tc_commit(&s.v_empty[sv]);
         if (j + 1 < nt) {
-          issue_s(1, st1);
+          issue_s(1, sk1);
           tc_commit(&s.s_full[1]);
+          tc_commit(&s.k_empty[sk1]);
         }
       }
       if (!ok) set_abort(s);
@@ -351,7 +382,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
           b = fast_exp2(b);
           if (e & 1) acc1 = fadd2(acc1, pack2f(a, b));
           else acc0 = fadd2(acc0, pack2f(a, b));
-          pk[e] = pack_bf16x2(a, b);
+          pk[e] = pack_f16x2(a, b);
         }
         tmem_st32(tS + half * 32, pk);
       }
@@ -390,6 +421,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// V [nkv][cap][128] BF16 rows [0, kL) -> v16 [nkv][kL][128] FP16 (round to
+// nearest: exact for |v| <= 65504; values past the FP16 range become inf and
+// are recorded as RIB_EINVAL on the device status word).
+__global__ void __launch_bounds__(256) v_half_kernel(const uint16_t *__restrict__ V, int cap, int kL, int nkv,
+                                                     uint16_t *__restrict__ v16) {
+  const long long per_head = static_cast<long long>(kL) * (D / 8);
+  const long long total = per_head * nkv;
+  uint32_t bad = 0;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long h = i / per_head, r = i - h * per_head;  // r: 16-byte chunk within the head
+    uint4 w = *reinterpret_cast<const uint4 *>(V + h * cap * D + r * 8);
+    w.x = bf16x2_to_f16x2(w.x, bad);
+    w.y = bf16x2_to_f16x2(w.y, bad);
+    w.z = bf16x2_to_f16x2(w.z, bad);
+    w.w = bf16x2_to_f16x2(w.w, bad);
+    *reinterpret_cast<uint4 *>(v16 + h * kL * D + r * 8) = w;
+  }
+  if (bad) atomicExch(&g_device_status, RIB_EINVAL);
 }
 
 // ---------------------------------------------------------------- host side
@@ -438,18 +490,36 @@ inline bool make_map(CUtensorMap *m, const void *base, int rows, int heads, long
 
 inline bool g_smem_done[64];
 
+// Bytes of the FP16 copy of V a prefill call needs: [nkv][kL][128].
+inline size_t workspace_bytes(int kL, int nkv) {
+  return (static_cast<size_t>(nkv) * kL * D * 2 + 255) / 256 * 256;
+}
+
 inline int launch(const void *Q, const void *K, const void *V, int qL, int kL, int qLp, int cap,
-                  int H, int nkv, float scale, void *O, void *stream, bool (*bind)(void *)) {
-  if (!Q || !K || !V || !O) return RIB_EINVAL;
+                  int H, int nkv, float scale, void *O, void *workspace, size_t workspace_bytes_,
+                  void *stream, bool (*bind)(void *)) {
+  if (!Q || !K || !V || !O || !workspace) return RIB_EINVAL;
   if (nkv < 1 || H != 2 * nkv || qL < 1 || qLp < qL || kL < qL || cap < 1 || !(scale > 0.f))
     return RIB_EINVAL;
   if (kL > cap) return RIB_ECAPACITY;
+  if (workspace_bytes_ < workspace_bytes(kL, nkv)) return RIB_EINVAL;
   auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
-  if (!a16(Q) || !a16(K) || !a16(V) || !a16(O)) return RIB_EALIGN;
+  if (!a16(Q) || !a16(K) || !a16(V) || !a16(O) || !a16(workspace)) return RIB_EALIGN;
   if (!bind(stream)) return host_fail(RIB_ECUDA, "bind stream device", 0);
+  // V -> FP16 copy [nkv][kL][128]
+  uint16_t *v16 = static_cast<uint16_t *>(workspace);
+  {
+    const long long chunks = static_cast<long long>(nkv) * kL * (D / 8);
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::min<long long>((chunks + threads - 1) / threads, 148LL * 16));
+    v_half_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t *>(V), cap, kL, nkv, v16);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return host_fail_cuda("v_half_kernel launch", e);
+  }
   Params p;
   if (!make_map(&p.tm_q, Q, qLp, H, qLp) || !make_map(&p.tm_k, K, kL, nkv, cap) ||
-      !make_map(&p.tm_v, V, kL, nkv, cap))
+      !make_map(&p.tm_v, v16, kL, nkv, kL))
     return RIB_ECUDA;
   p.out = static_cast<uint16_t *>(O);
   p.qL = qL;

@@ -13,6 +13,7 @@
 #include "decode_step.cuh"
 #include "prefill_attention.cuh"
 #include "decode_streamk.cuh"
+#include "gemm.cuh"
 #include "model_kernels.cuh"
 #include "qk_norm_rope.cuh"
 
@@ -447,6 +448,61 @@ int step_launch(const rib::step::Params &p, int which, cudaStream_t st) {
   return e == cudaSuccess ? RIB_OK : rib::host_fail_cuda("decode_step_kernel launch", e);
 }
 
+// ------------------------------------------------------------------ GEMM (prefill projections)
+// 2-D BF16 map of a row-major [rows][cols] matrix (row stride ld elements),
+// box (64 columns, box_rows rows), 128-byte swizzle; rows past `rows` read
+// as zero.
+bool gemm_map(CUtensorMap *m, const void *base, long long rows, long long cols, long long ld, int box_rows) {
+  rib::prefill::EncodeTiledFn enc = rib::prefill::encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    rib::host_fail(RIB_ECUDA, "cuTensorMapEncodeTiled (gemm)", static_cast<int>(r));
+    return false;
+  }
+  return true;
+}
+
+bool g_gemm_smem_done[2][kMaxDevices];
+
+template <int BN>
+int gemm_launch_bn(rib::gemm::Params &p, const void *A, const void *W, int w_box_rows, cudaStream_t st) {
+  using namespace rib::gemm;
+  if (!gemm_map(&p.tm_a, A, p.M, p.K, p.K, BM) || !gemm_map(&p.tm_b, W, p.N, p.K, p.K, w_box_rows))
+    return RIB_ECUDA;
+  const int smem = static_cast<int>(sizeof(Smem<BN>)) + 1024;
+  if (!set_smem_once(gemm_kernel<BN>, smem, g_gemm_smem_done[BN == 256]))
+    return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(gemm smem)", smem);
+  const int grid = std::min(p.num_tiles, sm_count());
+  return launch_pdl("gemm_kernel launch", gemm_kernel<BN>, dim3(grid), dim3(NTHREADS), smem, st, p);
+}
+
+// Shared checks and launch of every GEMM entry point.
+int gemm_run(const void *A, int M, int K, const void *W, int N, int epi, int bn, rib::gemm::Params &p,
+             void *stream) {
+  using namespace rib::gemm;
+  if (!A || !W || M < 1 || N < 1 || K < BK || K % BK) return RIB_EINVAL;
+  if (epi == kSwiGLU || epi == kQKRope ? N % bn : N % 8) return RIB_EINVAL;
+  if (!aligned16(A) || !aligned16(W)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.epi = epi;
+  p.num_m = ceil_div(M, BM);
+  const int out_cols = epi == kSwiGLU ? N / 2 : N;
+  p.num_tiles = p.num_m * (epi == kSwiGLU ? out_cols / 128 : ceil_div(N, bn));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bn == 256) return gemm_launch_bn<256>(p, A, W, epi == kSwiGLU ? 128 : 256, st);
+  return gemm_launch_bn<128>(p, A, W, 128, st);
+}
+
 }  // namespace
 
 extern "C" {
@@ -662,6 +718,10 @@ int rib_decode_attention_gather(const void *q, const uint64_t *cache_ptrs, const
   p.nq_total = g->world * nq;
   p.epoch = epoch;
   p.total_units = batch * nkv;
+  // Early ring fill (header: lens, cache_ptrs and the cache rows below the
+  // new token's are complete at launch): a call's first tiles stream while
+  // the previous call finishes its exchange with the peers.
+  p.early = 1;
   return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream);
 }
 
@@ -759,10 +819,16 @@ int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw, do
   return decode_launch(p, batch, max_n, workspace, workspace_bytes, stream, false);
 }
 
+size_t rib_prefill_workspace_bytes(int kL, int nkv) {
+  if (kL < 1 || nkv < 1) return 0;
+  return rib::prefill::workspace_bytes(kL, nkv);
+}
+
 int rib_prefill_attention(const void *Q, const void *K, const void *V, int qL, int kL, int qLp,
-                          int cap, int H, int nkv, float scale, void *O, void *stream) {
-  return rib::prefill::launch(Q, K, V, qL, kL, qLp, cap, H, nkv, scale, O, stream,
-                              bind_stream_device);
+                          int cap, int H, int nkv, float scale, void *O, void *workspace,
+                          size_t workspace_bytes, void *stream) {
+  return rib::prefill::launch(Q, K, V, qL, kL, qLp, cap, H, nkv, scale, O, workspace, workspace_bytes,
+                              stream, bind_stream_device);
 }
 
 
@@ -1109,6 +1175,63 @@ int rib_qk_norm_rope_append_batched(const void *qkv, const void *qw, const void 
   const int threads = ((nq + 2 * nkv + 1) / 2) * 32;
   return launch_pdl("qk_norm_rope_batched_kernel launch", rib::rope::qk_norm_rope_batched_kernel, dim3(batch),
                     dim3(threads), 0, static_cast<cudaStream_t>(stream), p);
+}
+
+int rib_gemm(const void *A, int M, int K, const void *W, int N, int epi, void *C, long long ldc,
+             void *stream) {
+  using namespace rib::gemm;
+  if (!C || (epi != RIB_GEMM_BF16 && epi != RIB_GEMM_F32 && epi != RIB_GEMM_SWIGLU)) return RIB_EINVAL;
+  Params p = {};
+  p.c = C;
+  p.ldc = ldc;
+  int bn;
+  if (epi == RIB_GEMM_SWIGLU) {
+    if (N % 256 || ldc < N / 2) return RIB_EINVAL;
+    bn = 256;
+    p.swiglu_f = N / 2;
+  } else {
+    if (ldc < N || N % 8) return RIB_EINVAL;
+    bn = N % 256 == 0 ? 256 : 128;  // a last tile past N is computed and not stored
+  }
+  if (!aligned16(C) || (ldc * (epi == RIB_GEMM_F32 ? 4 : 2)) % 16) return RIB_EALIGN;
+  const int e = epi == RIB_GEMM_BF16 ? kBF16 : epi == RIB_GEMM_F32 ? kF32 : kSwiGLU;
+  return gemm_run(A, M, K, W, N, e, bn, p, stream);
+}
+
+int rib_rope_table(int pos0, int count, double base, void *table, void *stream) {
+  if (!table || pos0 < 0 || count < 1 || !(base > 0.0)) return RIB_EINVAL;
+  if (!aligned16(table)) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  rib::rope::Params rp = {};
+  rib::rope::rope_inv_freq(rp.inv_freq, base);
+  return launch_pdl("rope_table_kernel launch", rib::gemm::rope_table_kernel, dim3(count), dim3(64), 0,
+                    static_cast<cudaStream_t>(stream), pos0, count, rp, static_cast<float2 *>(table));
+}
+
+int rib_gemm_qkv_rope(const void *A, int M, int K, const void *W, int nq, int nkv, const void *qw,
+                      const void *kw, const void *rope_table, int pos0, void *q_out, int Lp, void *cache,
+                      int cap, void *stream) {
+  using namespace rib::gemm;
+  if (!qw || !kw || !rope_table || !q_out || !cache || nq < 1 || nkv < 1 || pos0 < 0 || Lp < M || cap < 1)
+    return RIB_EINVAL;
+  if (static_cast<long long>(pos0) + M > cap) return RIB_ECAPACITY;
+  if (!aligned16(qw) || !aligned16(kw) || !aligned16(rope_table) || !aligned16(q_out) || !aligned16(cache))
+    return RIB_EALIGN;
+  Params p = {};
+  p.qw = static_cast<const uint16_t *>(qw);
+  p.kw = static_cast<const uint16_t *>(kw);
+  p.rope = static_cast<const float2 *>(rope_table);
+  p.pos0 = pos0;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.q_out = static_cast<uint16_t *>(q_out);
+  p.Lp = Lp;
+  p.cache = static_cast<uint16_t *>(cache);
+  p.cap = cap;
+  // tiles of 128 rows cover Lp (Q pad rows are written as zero)
+  // two heads per 256-wide tile ((nq + 2 nkv) = 4 nkv heads: always even)
+  const int status = gemm_run(A, M, K, W, (nq + 2 * nkv) * 128, kQKRope, 256, p, stream);
+  return status;
 }
 
 int rib_argmax_rows_f32(const float *x, int rows, int n, int32_t *out, void *stream) {

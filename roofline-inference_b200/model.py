@@ -14,8 +14,9 @@ Per decode step and layer the engine launches the reference's seven kernels
 with two of them fused: norm + QKV GEMV, qk-norm + RoPE + KV append (one
 kernel), split-KV decode attention, O GEMV + residual, norm + gate/up GEMV +
 SwiGLU, down GEMV + residual; then the final norm + LM-head GEMV and argmax.
-Prefill uses cuBLAS GEMMs (torch.matmul) for the projections, the tcgen05
-prefill kernel for attention and this library's add_rms / SwiGLU kernels; as
+Prefill runs the projections on this library's tcgen05 GEMM (gemm.py) with
+the QKV norm + RoPE + KV append and the SwiGLU fused into its epilogues, the
+tcgen05 prefill kernel for attention and the add_rms kernel; as
 in the reference, the last layer runs attention and MLP for the final row only
 and the logits cover the final row only.
 """
@@ -34,6 +35,7 @@ from .cache import Cache
 from .kernels import (add_rms, argmax, embedding, gemv, qk_norm_rope_append, qk_norm_rope_append_at,
                       rms_norm, swiglu)
 from ._tensors import HEAD_DIM, stream_handle
+from .gemm import gemm, gemm_qkv_rope, rope_table
 
 
 @dataclass(frozen=True)
@@ -116,9 +118,14 @@ def random_weights(config: Qwen3Config = QWEN3_0_6B, seed: int = 0, device="cpu"
     return Qwen3Weights(config, embed, norm(d), layers)
 
 
-def _linear(x, W):
-    """x [m, k] @ W[n, k]^T: a plain cuBLAS BF16 GEMM (FP32 accumulate, BF16 out)."""
-    return torch.matmul(x, W.t())
+def _linear(x, W, epi: str = "bf16"):
+    """epi(x [m, k] @ W[n, k]^T) on this library's kernels (the reference's
+    Engine.matmul, agent-test/v2/engine.py:95-99): the GEMV for one row, the
+    tcgen05 GEMM (gemm.py) for more.  epi "bf16", "f32" or "swiglu"
+    (W = [gate; up])."""
+    if x.shape[0] == 1:
+        return gemv(W, x.reshape(-1), swiglu=epi == "swiglu", out_float=epi == "f32").reshape(1, -1)
+    return gemm(x, W, epi=epi)
 
 
 def _shard_qkv_rows(W: torch.Tensor, h0: int, h1: int, nq: int, nkv: int) -> torch.Tensor:
@@ -239,7 +246,7 @@ class Engine:
         """Row-parallel projection: the full output under tensor parallelism
         (FP32 partials summed over ranks), else a plain BF16 GEMM."""
         if self.tp:
-            return self._all_reduce_bf16(torch.mm(x, W.t(), out_dtype=torch.float32))
+            return self._all_reduce_bf16(_linear(x, W, "f32"))
         return _linear(x, W)
 
     def _gather_rows(self, o_local):
@@ -267,9 +274,11 @@ class Engine:
         nl = len(self.layers)
         h = embedding(self.embed, tokens)                                   # [n, hidden]
         x = rms_norm(h, self.layers[0]["in_norm"])
+        table = rope_table(off, n, self.base, self.device)                 # shared by every layer
         for i, w in enumerate(self.layers):
-            q = qk_norm_rope_append(_linear(x, w["qkv"]), w["q_norm"], w["k_norm"], off, self.nq_local,
-                                    self.n_kv, self.base, cache.kv[i], Lp)    # [nq_local, Lp, 128]
+            # QKV projection + qk-norm + RoPE + KV append in one GEMM (engine.py:111-113)
+            q = gemm_qkv_rope(x, w["qkv"], w["q_norm"], w["k_norm"], table, off, self.nq_local, self.n_kv,
+                              cache.kv[i], Lp)                                # [nq_local, Lp, 128]
             final = i == nl - 1
             if final and not last:
                 break        # a middle chunk only needs the final layer's cache rows, now written
@@ -283,7 +292,7 @@ class Engine:
                 o = attention(q, kvl[0], kvl[1], n, off + n, self.scale)       # [n, nq_local*128]
                 o = o if self.tp else self._gather_rows(o)                     # [n, H*128]
             h, x = add_rms(h, self._proj_out(o, w["o"]), w["post_norm"])
-            r = self._proj_out(swiglu(_linear(x, w["gu"])), w["down"])
+            r = self._proj_out(_linear(x, w["gu"], "swiglu"), w["down"])
             if final:
                 h = h + r
             else:
@@ -293,7 +302,7 @@ class Engine:
             return None
         if all_logits:
             hn = rms_norm(h, self.final_norm)
-            lg = torch.matmul(hn.float(), self.lm_head.float().t())
+            lg = _linear(hn, self.lm_head, "f32")
             return (self._gather_vocab(lg) if self.tp else lg)[None]
         lg = gemv(self.lm_head, h.reshape(-1), nw=self.final_norm, out_float=True)
         return (self._gather_vocab(lg) if self.tp else lg)[None, None]

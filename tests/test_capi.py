@@ -93,15 +93,50 @@ def test_rope_rejects_bad_arguments(rib):
 
 def test_prefill_rejects_bad_arguments(rib):
     L = rib.load_library()
+    ws = L.rib_prefill_workspace_bytes(64, 8)
+    assert ws == 8 * 64 * 128 * 2 and L.rib_prefill_workspace_bytes(0, 8) == 0
     # H != 2 * nkv
     assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 64, 64, 256, 12, 8, 0.088, FAKE,
-                                   None) == 1
+                                   FAKE, ws, None) == 1
     # kL < qL
     assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 32, 64, 256, 16, 8, 0.088, FAKE,
-                                   None) == 1
+                                   FAKE, ws, None) == 1
     # kL beyond cap
     assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 300, 64, 256, 16, 8, 0.088, FAKE,
-                                   None) == 2
+                                   FAKE, ws, None) == 2
+    # workspace too small, or missing
+    assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 64, 64, 256, 16, 8, 0.088, FAKE,
+                                   FAKE, ws - 16, None) == 1
+    assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 64, 64, 256, 16, 8, 0.088, FAKE,
+                                   None, ws, None) == 1
     # misaligned
     assert L.rib_prefill_attention(MISALIGNED, FAKE, FAKE, 64, 64, 64, 256, 16, 8, 0.088, FAKE,
-                                   None) == 3
+                                   FAKE, ws, None) == 3
+    assert L.rib_prefill_attention(FAKE, FAKE, FAKE, 64, 64, 64, 256, 16, 8, 0.088, FAKE,
+                                   MISALIGNED, ws, None) == 3
+
+
+def test_gemm_rejects_bad_arguments(rib):
+    import importlib
+    G = importlib.import_module("roofline-inference_b200.gemm")
+    L = G._L()
+    # K not a multiple of 64, N not a multiple of 8, unknown epilogue
+    assert L.rib_gemm(FAKE, 64, 96, FAKE, 128, 0, FAKE, 128, None) == 1
+    assert L.rib_gemm(FAKE, 64, 128, FAKE, 100, 0, FAKE, 100, None) == 1
+    assert L.rib_gemm(FAKE, 64, 128, FAKE, 128, 7, FAKE, 128, None) == 1
+    # SwiGLU needs F = N / 2 a multiple of 128
+    assert L.rib_gemm(FAKE, 64, 128, FAKE, 192, 2, FAKE, 96, None) == 1
+    # misaligned operands
+    assert L.rib_gemm(MISALIGNED, 64, 128, FAKE, 128, 0, FAKE, 128, None) == 3
+    assert L.rib_gemm(FAKE, 64, 128, FAKE, 128, 0, MISALIGNED, 128, None) == 3
+    # QKV + RoPE + append beyond the cache capacity (engine.py:45-46)
+    assert L.rib_gemm_qkv_rope(FAKE, 64, 128, FAKE, 16, 8, FAKE, FAKE, FAKE, 250, FAKE, 64, FAKE, 256,
+                               None) == 2
+    assert L.rib_rope_table(0, 0, 1e6, FAKE, None) == 1
+
+
+def test_wait_limit_range_checked_on_host(rib):
+    L = rib.load_library()
+    assert L.rib_set_wait_limit_ns(10) == 1
+    assert L.rib_set_wait_limit_ns(61_000_000_000) == 1
+    assert L.rib_get_wait_limit_ns(None) == 1

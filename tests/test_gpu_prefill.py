@@ -1,31 +1,57 @@
 """GPU parity of the tcgen05/TMEM causal prefill attention kernel against the
-oracle and the golden fixtures.
+oracle, the reference's own kernel (golden fixtures) and the reference's own
+tolerance rule.
 
 Shapes: the reference test's (qL, kL) pairs (agent-test/v2/test_engine.py:81-99,
 q scaled by 1.5, cap rounded to 256), the prefill sweep L in {16, 64, 256,
 1024, 4096, 32768} and ragged sizes that are not multiples of the 128-row tile.
-Tolerance: contract max-abs <= 2e-2 and mean-abs <= 2e-3 against the FP32
-oracle; in addition the error may exceed the error of rounding the exact
-result to BF16 only by the BF16 rounding of P (P.V runs on BF16 P)."""
+
+Tolerances, all against the FP32 oracle:
+  - contract: max-abs <= 2e-2 and mean-abs <= 2e-3;
+  - the reference's rule (test_engine.py:97-99): e_kernel <= 1.1 e_mlx + 1e-6,
+    where e_mlx is the max error of MLX's BF16 SDPA, here its restatement
+    (oracle/reference_np.prefill_attention_mlx_bf16: Q scaled in BF16, FP32
+    softmax and P V);
+  - stricter, MLX-independent: e_kernel <= 1.1 e_p16 + 1e-6, where e_p16 is the
+    max error of a plain BF16-P SDPA (exact row max, P rounded to BF16,
+    FP32 sums; oracle/reference_np.prefill_attention_bf16p).
+The kernel runs P V on BF16 P (a kind::f16 MMA takes BF16 operands); the
+reference kernel keeps P in FP32 and sits at the BF16 rounding floor; each
+test prints e_kernel against that floor as well."""
 from __future__ import annotations
+
+import importlib
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import from_u16, load_golden, parity_errors, u16
+from conftest import bf16f, from_u16, load_golden, parity_errors, u16
 
 pytestmark = pytest.mark.gpu
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+RULE = 1.1  # test_engine.py:99
 
 
-def _assert_parity(out, exact, rows=None):
+def _assert_parity(out, exact, Q=None, K=None, V=None, qL=None, kL=None, rows=None, scale=128 ** -0.5):
+    from oracle import reference_np as rn
     o = out if rows is None else out[rows[0]:rows[1]]
     e = exact if rows is None else exact[rows[0]:rows[1]]
     err = parity_errors(o, e)
-    print(f"prefill parity: {err}")
     assert err["max"] <= MAX_ABS and err["mean"] <= MEAN_ABS, err
-    assert err["max"] <= 2.0 * err["floor_max"] + 1e-6, err
+    if Q is not None:
+        ex = np.asarray(e, np.float64)
+        e_mlx = float(np.abs(bf16f(rn.prefill_attention_mlx_bf16(Q, K, V, qL, kL, scale, rows)) - ex).max())
+        e_p16 = float(np.abs(bf16f(rn.prefill_attention_bf16p(Q, K, V, qL, kL, scale, rows)) - ex).max())
+        tiny = 1e-30  # a single visible key gives exact outputs: zero errors
+        err.update(e_mlx=e_mlx, e_p16=e_p16, vs_mlx=err["max"] / max(e_mlx, tiny),
+                   vs_p16=err["max"] / max(e_p16, tiny), vs_floor=err["max"] / max(err["floor_max"], tiny))
+        print(f"prefill parity qL={qL} kL={kL} rows={rows}: {err}")
+        assert err["max"] <= RULE * e_mlx + 1e-6, err
+        assert err["max"] <= RULE * e_p16 + 1e-6, err
+    else:
+        print(f"prefill parity: {err}")
+    return err
 
 
 def _case(wl, qL, kL, seed, qscale=1.0):
@@ -38,26 +64,59 @@ def _case(wl, qL, kL, seed, qscale=1.0):
     return Q, buf
 
 
-@pytest.mark.parametrize("name", ["prefill_37x37", "prefill_128x300"])
+@pytest.mark.parametrize("name", ["prefill_37x37", "prefill_128x300", "prefill_1000x1000",
+                                  "prefill_512x2600"])
 def test_prefill_golden(rib, name):
+    """The reference test's four shapes: against the FP32 oracle with the
+    reference's rule, and against the reference kernel's own BF16 output."""
     z = load_golden(name)
     qL, kL = int(z["qL"]), int(z["kL"])
-    Q, K, V = (from_u16(z[k], "cuda") for k in ("Q", "K", "V"))
-    out = rib.attention(Q, K[None], V[None], qL, kL, 128 ** -0.5)
+    if "Q" in z:
+        Q, K, V, rows = z["Q"], z["K"], z["V"], None
+    else:
+        mg = importlib.import_module("golden.make_golden")
+        Q, K, V = mg.prefill_inputs(qL, kL, int(z["seed"]))
+        assert mg.sha(Q, K, V) == str(z["inputs_sha256"]), "seeded generator changed"
+        rows = z["rows"]
+    cap = (kL + 255) // 256 * 256
+    buf = np.zeros((2, 8, cap, 128), np.uint16)
+    buf[0, :, :kL], buf[1, :, :kL] = K, V
+    bd = from_u16(buf, "cuda")
+    out = rib.attention(from_u16(Q, "cuda"), bd[0:1], bd[1:2], qL, kL, 128 ** -0.5)
     torch.cuda.synchronize()
     assert tuple(out.shape) == (qL, 16 * 128)
-    _assert_parity(out, z["out"])
+    got = u16(out)
+    if rows is None:
+        err = _assert_parity(got, z["out"], Q, K, V, qL, kL)
+        ref_k = z["out_ref"]
+    else:
+        # sampled rows: contiguous runs of the fixture's row list
+        runs = np.split(rows, np.where(np.diff(rows) != 1)[0] + 1)
+        at = 0
+        for r in runs:
+            sub = z["out"][at:at + len(r)]
+            full = np.full((qL, 16 * 128), np.nan, np.float32)
+            full[r[0]:r[-1] + 1] = sub
+            _assert_parity(got, full, Q, K, V, qL, kL, rows=(int(r[0]), int(r[-1]) + 1))
+            at += len(r)
+        got = got[rows]
+        ref_k = z["out_ref"]
+    d = np.abs(bf16f(got) - bf16f(ref_k))
+    print(f"{name}: kernel vs the reference kernel's BF16 output: max {d.max():.3e} mean {d.mean():.3e}")
+    assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS
 
 
 @pytest.mark.parametrize("qL,kL", [(37, 37), (128, 300), (1000, 1000), (512, 2600), (1, 1),
                                    (1, 700), (129, 129), (200, 4000)])
 def test_prefill_reference_shapes(rib, wl, oracle, qL, kL):
-    """agent-test/v2/test_engine.py:81-99 shapes plus single-row and ragged ones."""
+    """agent-test/v2/test_engine.py:81-99 shapes plus single-row and ragged
+    ones, on other seeds, under the reference's rule."""
     Q, buf = _case(wl, qL, kL, seed=qL * 7 + kL, qscale=1.5)
     out = rib.attention(Q, buf[0:1], buf[1:2], qL, kL, wl.SCALE)
     torch.cuda.synchronize()
-    ref = oracle.prefill_attention(u16(Q), u16(buf[0]), u16(buf[1]), qL, kL, wl.SCALE)
-    _assert_parity(out, ref)
+    Qh, Kh, Vh = u16(Q), u16(buf[0]), u16(buf[1])
+    ref = oracle.prefill_attention(Qh, Kh, Vh, qL, kL, wl.SCALE)
+    _assert_parity(u16(out), ref, Qh, Kh, Vh, qL, kL)
 
 
 @pytest.mark.parametrize("L", [16, 64, 256, 1024, 4096])
@@ -66,8 +125,9 @@ def test_prefill_sweep(rib, wl, oracle, L):
     Q, buf = _case(wl, L, L, seed=L)
     out = rib.attention(Q, buf[0:1], buf[1:2], L, L, wl.SCALE)
     torch.cuda.synchronize()
-    ref = oracle.prefill_attention(u16(Q), u16(buf[0]), u16(buf[1]), L, L, wl.SCALE)
-    _assert_parity(out, ref)
+    Qh, Kh, Vh = u16(Q), u16(buf[0]), u16(buf[1])
+    ref = oracle.prefill_attention(Qh, Kh, Vh, L, L, wl.SCALE)
+    _assert_parity(u16(out), ref, Qh, Kh, Vh, L, L)
 
 
 def test_prefill_32k_sampled_rows(rib, wl, oracle):
@@ -81,7 +141,7 @@ def test_prefill_32k_sampled_rows(rib, wl, oracle):
     Qh, Kh, Vh = u16(Q), u16(buf[0]), u16(buf[1])
     for r0 in (0, 16384 - 64, L - 128):
         ref = oracle.prefill_attention(Qh, Kh, Vh, L, L, wl.SCALE, rows=(r0, r0 + 128))
-        _assert_parity(out, ref, rows=(r0, r0 + 128))
+        _assert_parity(u16(out), ref, Qh, Kh, Vh, L, L, rows=(r0, r0 + 128))
 
 
 def test_prefill_fused_pipeline(rib, wl, oracle):

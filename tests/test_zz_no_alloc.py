@@ -4,48 +4,96 @@ rib_decode_attention_noalloc serves callers that cannot call cudaMalloc or
 lend device scratch -- a host whose device memory belongs to another
 allocator or to a fixed budget, or a language binding with no device
 allocator of its own.  It keeps its split-KV scratch in a fixed 2 MiB array
-inside the library.  This test calls it through the C ABI and checks it
-against the workspace-taking entry point, twice in a row (the array keeps
-the previous call's contents), and checks that a size beyond the array is
-refused.  The file is named so that pytest collects it last."""
+inside the library.  These tests call it through the C ABI and check it
+against the oracle and against the workspace-taking entry point, on calls in
+a row (the array keeps the previous call's contents): at the largest size
+the array takes at 8 KV heads (n = 909312) and on a launch whose split merge
+takes two levels (its group counters live in the same array); and they check
+that one key more is refused.  The file is named so that pytest collects it
+last."""
 from __future__ import annotations
 
 import numpy as np
 import pytest
 import torch
 
-from conftest import bf16f
+from conftest import bf16f, u16
 
 pytestmark = pytest.mark.gpu
 
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+N_MAX_8_HEADS = 909312  # largest n whose scratch fits the 2 MiB array at 8 KV heads
 
 
-def test_noalloc_decode_matches_workspace_entry_point(rib, wl):
+def _noalloc(L, q, cache, n, nq, nkv, scale):
+    got = torch.full((nq, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+    status = L.rib_decode_attention_noalloc(q.data_ptr(), cache.data_ptr(), cache.shape[2], n, nq, nkv,
+                                            scale, got.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert status == 0, L.rib_last_error_string()
+    torch.cuda.synchronize()
+    return got
+
+
+def _check(got, want_bf16, ref_f32):
+    d = np.abs(bf16f(got).astype(np.float64) - bf16f(want_bf16).astype(np.float64))
+    assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS, (d.max(), d.mean())
+    e = np.abs(bf16f(got).astype(np.float64) - ref_f32)
+    assert e.max() <= MAX_ABS and e.mean() <= MEAN_ABS, (e.max(), e.mean())
+
+
+def test_noalloc_decode_matches_oracle_and_workspace_entry_point(rib, wl, oracle):
     L = rib.load_library()
     n = 8193
     st = wl.decode_step(n - 1, seed=21, device="cuda")
-    cap = st.cache.shape[2]
-    stream = torch.cuda.current_stream().cuda_stream
+    cache_h = u16(st.cache)
     outs = []
     for call in range(2):
         q = wl.randn_bf16((16, 128), seed=40 + call, device="cuda")
         want = rib.decode_attention(q, st.cache, n, wl.SCALE).reshape(16, 128)
-        got = torch.full((16, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
-        status = L.rib_decode_attention_noalloc(q.data_ptr(), st.cache.data_ptr(), cap, n, 16, 8,
-                                                wl.SCALE, got.data_ptr(), stream)
-        assert status == 0, L.rib_last_error_string()
-        torch.cuda.synchronize()
-        d = np.abs(bf16f(got).astype(np.float64) - bf16f(want).astype(np.float64))
-        assert d.max() <= MAX_ABS and d.mean() <= MEAN_ABS, (call, d.max(), d.mean())
+        got = _noalloc(L, q, st.cache, n, 16, 8, wl.SCALE)
+        ref, _ = oracle.decode_attention(u16(q), cache_h, n, wl.SCALE)
+        _check(got, want, ref)
         outs.append(got.clone())
     assert not torch.equal(outs[0], outs[1])  # two different queries, two answers
+    assert rib._lib.take_device_status() == 0
 
 
-def test_noalloc_decode_rejects_sizes_beyond_static_scratch(rib):
+def test_noalloc_two_level_merge_twice(rib, wl, oracle):
+    """One KV head at 32769 keys runs hundreds of splits, so the split merge
+    takes two levels and uses the group counters kept in the array; a second
+    call must find them back at zero."""
     L = rib.load_library()
+    n = 32769
+    st = wl.decode_step(n - 1, seed=23, device="cuda", nkv=1)
+    cache_h = u16(st.cache)
+    for call in range(2):
+        q = wl.randn_bf16((2, 128), seed=60 + call, device="cuda")
+        want = rib.decode_attention(q, st.cache, n, wl.SCALE).reshape(2, 128)
+        got = _noalloc(L, q, st.cache, n, 2, 1, wl.SCALE)
+        ref, _ = oracle.decode_attention(u16(q), cache_h, n, wl.SCALE)
+        _check(got, want, ref)
+    assert rib._lib.take_device_status() == 0
+
+
+def test_noalloc_largest_size_fits(rib, wl, oracle):
+    L = rib.load_library()
+    n = N_MAX_8_HEADS
+    assert L.rib_decode_workspace_bytes(1, n, 8) <= 2 << 20
+    cache = torch.randn((2, 8, n, 128), device="cuda").to(torch.bfloat16)
+    q = wl.randn_bf16((16, 128), seed=70, device="cuda")
+    want = rib.decode_attention(q, cache, n, wl.SCALE).reshape(16, 128)
+    got = _noalloc(L, q, cache, n, 16, 8, wl.SCALE)
+    ref, _ = oracle.decode_attention(u16(q), u16(cache), n, wl.SCALE)
+    _check(got, want, ref)
+    del cache
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("n", [N_MAX_8_HEADS + 1, 2000000])
+def test_noalloc_decode_rejects_sizes_beyond_static_scratch(rib, n):
+    L = rib.load_library()
+    assert L.rib_decode_workspace_bytes(1, n, 8) > 2 << 20
     fake = 0x10000  # aligned dummy address; the size check runs before any launch
-    n = 2000000  # needs about 4 MiB of scratch at 8 KV heads
     status = L.rib_decode_attention_noalloc(fake, fake, n, n, 16, 8, 0.088, fake,
                                             torch.cuda.current_stream().cuda_stream)
     assert status == 1
