@@ -1239,8 +1239,9 @@ def run_case(case: str):
     """Bounded workloads for ncu captures: decode-small is the layer-batched
     decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
     prefill-small is causal prefill at L = 16384 (128 MB of Q/K/V, above L2;
-    3 launches); decode-4k is the 28-layer sweep at ctx 4096 (470 MB of
-    KV, the stream-K decode kernel; 3 launches); model-decode is the
+    3 launches), prefill-32k the same at L = 32768 (the bench's launch);
+    decode-4k is the 28-layer sweep at ctx 4096 (470 MB of KV, the stream-K
+    decode kernel; 3 launches); model-decode is the
     Qwen3-0.6B decode step at context 4096 (1.19 GB of weights and 0.47 GB of
     K/V, above L2): the graph's eager
     warm-up step and 3 replays of 143 launches each (the append fused into
@@ -1299,7 +1300,7 @@ def run_case(case: str):
         for _ in range(3):
             tok = dec.step(tok)
     else:
-        L = 16384
+        L = 32768 if case == "prefill-32k" else 16384
         Q = wl.randn_bf16((16, L, 128), seed=71, device=device)
         K = wl.randn_bf16((1, 8, L, 128), seed=72, device=device)
         V = wl.randn_bf16((1, 8, L, 128), seed=73, device=device)
@@ -1318,7 +1319,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "model-decode", "model-prefill", "gemm",
+    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "prefill-32k", "model-decode",
+                                       "model-prefill", "gemm",
                              "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()
