@@ -16,12 +16,15 @@
 //            rows zero), K and V appended to the cache rows pos0 + m
 //            (engine.py:111-113): the qkv activations never reach HBM.
 //
-// CTA (one per SM, persistent over output tiles of 128 x BN): 6 warps.
+// CTA (one per SM, persistent over output tiles of 128 x BN, or 256 x 256 as
+// two halves when there are enough such tiles to fill the GPU): 6 warps.
 //   warp 0      TMA producer: A and W k-blocks of 64 (128-byte swizzle) into
-//               an NS-stage ring (4 x 48 KB at BN = 256, 6 x 32 KB at 128).
+//               an NS-stage ring (4 x 48 KB at BN = 256, 6 x 32 KB at 128,
+//               3 x 64 KB for 256-row tiles).
 //   warp 1      TMEM owner and MMA issuer: per k-block 4 x tcgen05.mma
-//               (M = 128, N = BN, K = 16) into one of two accumulators, so
-//               the epilogue of tile i overlaps the main loop of tile i + 1.
+//               (M = 128, N = BN, K = 16) per 128-row half, into one of two
+//               accumulators for 128-row tiles, so the epilogue of tile i
+//               overlaps the main loop of tile i + 1.
 //   warps 2-5   epilogue: thread = accumulator row (TMEM lane quadrant
 //               warp % 4), tcgen05.ld of 32 columns at a time.
 // Every wait is bounded (common.cuh); on a timeout the CTA drains its copies,
@@ -31,6 +34,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "model_kernels.cuh"
 #include "qk_norm_rope.cuh"
 
 namespace rib {
@@ -44,14 +48,22 @@ constexpr int kEpiThreads = 128;
 
 enum Epi : int { kBF16 = 0, kF32 = 1, kSwiGLU = 2, kQKRope = 3 };
 
-template <int BN>
+// MH = 1: 128-row tiles, two accumulators (the epilogue of one tile overlaps
+// the next tile's MMAs).  MH = 2: 256-row tiles as two M = 128 halves that
+// share every W stage -- 64 KB per k-block for twice the FLOPs of the 48 KB
+// of a 128 x 256 tile -- with one accumulator pair filling all 512 TMEM
+// columns, so the epilogue does not overlap the next tile's MMAs.
+template <int BN, int MH = 1>
 struct Cfg {
   static_assert(BN == 128 || BN == 256, "BN is 128 or 256");
-  static constexpr int A_BYTES = BM * BK * 2;
+  static_assert(MH == 1 || (MH == 2 && BN == 256), "256-row tiles take BN = 256");
+  static constexpr int A_HALF = BM * BK * 2;
+  static constexpr int A_BYTES = MH * A_HALF;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int NS = BN == 256 ? 4 : 6;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int NS = MH == 2 ? 3 : (BN == 256 ? 4 : 6);
+  static constexpr int NBUF = MH == 2 ? 1 : 2;  // accumulator buffers
+  static constexpr uint32_t TMEM_COLS = NBUF * MH * BN;
   // kind::f16: D = F32 (bit 4), A = B = BF16 (bits 7, 10), both K-major,
   // N >> 3 at bits 17-22, M >> 4 at bits 24-28.
   static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) |
@@ -59,10 +71,10 @@ struct Cfg {
                                     (static_cast<uint32_t>(BM >> 4) << 24);
 };
 
-template <int BN>
+template <int BN, int MH>
 struct Smem {
-  alignas(1024) uint8_t stage[Cfg<BN>::NS][Cfg<BN>::STAGE];
-  uint64_t full[Cfg<BN>::NS], empty[Cfg<BN>::NS];
+  alignas(1024) uint8_t stage[Cfg<BN, MH>::NS][Cfg<BN, MH>::STAGE];
+  uint64_t full[Cfg<BN, MH>::NS], empty[Cfg<BN, MH>::NS];
   uint64_t acc_full[2], acc_empty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -103,21 +115,19 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int c0,
       : "memory");
 }
 
-template <int BN>
-__device__ __forceinline__ bool aborted(const Smem<BN> &s) {
+template <class S>
+__device__ __forceinline__ bool aborted(const S &s) {
   return *reinterpret_cast<const volatile int *>(&s.abort_flag) != 0;
 }
-template <int BN>
-__device__ __forceinline__ void set_abort(Smem<BN> &s) {
+template <class S>
+__device__ __forceinline__ void set_abort(S &s) {
   *reinterpret_cast<volatile int *>(&s.abort_flag) = 1;
 }
 
 __device__ __forceinline__ float silu_bf16(float g) {
   // s = bf16(sigmoid(g)), a = bf16(g s)  (agent-test/v2/kernels.py:86-93),
   // the arithmetic of model::swiglu_kernel
-  // (__frcp_rn is the correctly rounded reciprocal: the same value as 1.0f / x)
-  const float s = round_bf16(__frcp_rn(1.0f + expf(-g)));
-  return round_bf16(g * s);
+  return round_bf16(g * model::sigmoid_bf16(g));
 }
 
 // ---------------------------------------------------------------- epilogues
@@ -250,13 +260,16 @@ __device__ __forceinline__ void epi_qk_rope(const Params &p, uint32_t ta, int m,
 #pragma unroll
     for (int i = 0; i < 8; ++i) n[8 * v + i] = round_bf16(wf[i] * round_bf16(x[8 * v + i] * inv));
   }
-  const float2 *cs = p.rope + static_cast<size_t>(m) * 64;
+  const float4 *cs = reinterpret_cast<const float4 *>(p.rope + static_cast<size_t>(m) * 64);
   float o[128];
 #pragma unroll
-  for (int d = 0; d < 64; ++d) {
-    const float2 t = cs[d];
+  for (int d2 = 0; d2 < 32; ++d2) {  // (cos, sin) of angles 2 d2 and 2 d2 + 1
+    const float4 t = __ldg(cs + d2);
+    const int d = 2 * d2;
     o[d] = fmaf(n[d], t.x, -n[d + 64] * t.y);
     o[d + 64] = fmaf(n[d], t.y, n[d + 64] * t.x);
+    o[d + 1] = fmaf(n[d + 1], t.z, -n[d + 65] * t.w);
+    o[d + 65] = fmaf(n[d + 1], t.w, n[d + 65] * t.z);
   }
   dst = h < nq ? p.q_out + (static_cast<size_t>(h) * p.Lp + m) * 128
                : p.cache + ((static_cast<size_t>(h - nq) * p.cap) + p.pos0 + m) * 128;
@@ -273,19 +286,21 @@ __device__ __forceinline__ void epi_qk_rope(const Params &p, uint32_t ta, int m,
 }
 
 // ---------------------------------------------------------------- kernel
-template <int BN>
-__device__ __forceinline__ bool warp_wait(Smem<BN> &s, uint64_t *bar, uint32_t parity) {
+template <class S>
+__device__ __forceinline__ bool warp_wait(S &s, uint64_t *bar, uint32_t parity) {
   bool ok = !aborted(s) && mbar_wait(bar, parity);
   ok = __all_sync(0xffffffffu, ok);
   if (!ok) set_abort(s);
   return ok;
 }
 
-template <int BN>
+template <int BN, int MH>
 __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MH>;
+  using S = Smem<BN, MH>;
   extern __shared__ uint8_t smem_raw[];
-  Smem<BN> &s = *reinterpret_cast<Smem<BN> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  S &s = *reinterpret_cast<S *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int TM = BM * MH;  // rows per tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kblocks = p.K / BK;
 
@@ -323,7 +338,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        const int m0 = (tile % p.num_m) * BM, nb = tile / p.num_m;
+        const int m0 = (tile % p.num_m) * TM, nb = tile / p.num_m;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int st = it % C::NS;
           if (it >= C::NS && (aborted(s) || !mbar_wait(&s.empty[st], ((it / C::NS) - 1) & 1))) {
@@ -353,13 +368,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant
       int it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++lt) {
-        const int buf = lt & 1;
-        if (lt >= 2 && (aborted(s) || !mbar_wait(&s.acc_empty[buf], ((lt >> 1) - 1) & 1))) {
+        const int buf = lt % C::NBUF;
+        if (lt >= C::NBUF && (aborted(s) || !mbar_wait(&s.acc_empty[buf], ((lt / C::NBUF) - 1) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
+        const uint32_t d = tmem + buf * MH * BN;
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
           const int st = it % C::NS;
           if (aborted(s) || !mbar_wait(&s.full[st], (it / C::NS) & 1)) {
@@ -371,7 +386,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant
           const uint32_t b = a + C::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc_mma_ss(d, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), C::IDESC, (kb | kk) != 0);
+#pragma unroll
+            for (int h = 0; h < MH; ++h)  // the halves share the W stage
+              tc_mma_ss(d + h * BN, sw128_desc(a + h * C::A_HALF + kk * 32), sw128_desc(b + kk * 32), C::IDESC,
+                        (kb | kk) != 0);
           tc_commit(&s.empty[st]);
         }
         if (!ok) break;
@@ -388,18 +406,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant
     const int row = quad * 32 + lane;
     int lt = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
-      const int buf = lt & 1;
-      if (!warp_wait(s, &s.acc_full[buf], (lt >> 1) & 1)) break;
+      const int buf = lt % C::NBUF;
+      if (!warp_wait(s, &s.acc_full[buf], (lt / C::NBUF) & 1)) break;
       tc_fence_after();
-      const int m = (tile % p.num_m) * BM + row, nb = tile / p.num_m;
-      const uint32_t ta = tmem + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
-      if (p.epi == kSwiGLU) {
-        if constexpr (BN == 256) epi_swiglu(p, ta, m, nb * 128);
-      } else if (p.epi == kQKRope) {
+      const int nb = tile / p.num_m;
 #pragma unroll 1
-        for (int hh = 0; hh < BN / 128; ++hh) epi_qk_rope(p, ta + 128 * hh, m, nb * (BN / 128) + hh);
-      } else {
-        epi_store<BN>(p, ta, m, nb * BN);
+      for (int h = 0; h < MH; ++h) {
+        const int m = (tile % p.num_m) * TM + h * BM + row;
+        const uint32_t ta = tmem + (static_cast<uint32_t>(quad * 32) << 16) + (buf * MH + h) * BN;
+        if (p.epi == kSwiGLU) {
+          if constexpr (BN == 256) epi_swiglu(p, ta, m, nb * 128);
+        } else if (p.epi == kQKRope) {
+#pragma unroll 1
+          for (int hh = 0; hh < BN / 128; ++hh) epi_qk_rope(p, ta + 128 * hh, m, nb * (BN / 128) + hh);
+        } else {
+          epi_store<BN>(p, ta, m, nb * BN);
+        }
       }
       tc_fence_before();
       mbar_arrive(&s.acc_empty[buf]);

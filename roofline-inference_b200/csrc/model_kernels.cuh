@@ -124,8 +124,14 @@ __device__ __forceinline__ float dot8(const uint4 w, const float4 xa, const floa
   return acc;
 }
 
-// (__frcp_rn is the correctly rounded reciprocal: the same value as 1.0f / x, fewer instructions)
-__device__ __forceinline__ float sigmoid_bf16(float g) { return round_bf16(__frcp_rn(1.0f + expf(-g))); }
+// bf16(1 / (1 + exp(-g))) (agent-test/v2/kernels.py:89).  __fdividef is the
+// branch-free approximate quotient (within 2 ulp of 1.0f / x for x below 2^126,
+// 0 above, where the sigmoid is below 2^-126 anyway): the result is rounded to
+// BF16 straight after, so it differs from the correctly rounded quotient's only
+// when that lies within 2 FP32 ulp of a BF16 rounding boundary, and without the
+// IEEE reciprocal's special-case branch the epilogues keep their elements in
+// flight together.
+__device__ __forceinline__ float sigmoid_bf16(float g) { return round_bf16(__fdividef(1.0f, 1.0f + expf(-g))); }
 
 // ------------------------------------------------------------------ GEMV
 struct GemvParams {

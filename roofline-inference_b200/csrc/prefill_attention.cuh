@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) prefill_kernel(const __grid_const
         }
         m = mn;
       }
-      // P = exp2(S * scale*log2e - m), packed BF16 over S's first 64 columns
+      // P = exp2(S * scale*log2e - m), packed FP16 over S's first 64 columns
       // (the whole row is already in registers).
       const uint64_t nm2 = pack2f(-m, -m);
       uint64_t acc0 = pack2f(0.f, 0.f), acc1 = acc0;

@@ -469,21 +469,26 @@ bool gemm_map(CUtensorMap *m, const void *base, long long rows, long long cols, 
   return true;
 }
 
-bool g_gemm_smem_done[2][kMaxDevices];
+bool g_gemm_smem_done[3][kMaxDevices];
 
-template <int BN>
+template <int BN, int MH>
 int gemm_launch_bn(rib::gemm::Params &p, const void *A, const void *W, int w_box_rows, cudaStream_t st) {
   using namespace rib::gemm;
-  if (!gemm_map(&p.tm_a, A, p.M, p.K, p.K, BM) || !gemm_map(&p.tm_b, W, p.N, p.K, p.K, w_box_rows))
+  if (!gemm_map(&p.tm_a, A, p.M, p.K, p.K, BM * MH) || !gemm_map(&p.tm_b, W, p.N, p.K, p.K, w_box_rows))
     return RIB_ECUDA;
-  const int smem = static_cast<int>(sizeof(Smem<BN>)) + 1024;
-  if (!set_smem_once(gemm_kernel<BN>, smem, g_gemm_smem_done[BN == 256]))
+  const int smem = static_cast<int>(sizeof(Smem<BN, MH>)) + 1024;
+  if (!set_smem_once(gemm_kernel<BN, MH>, smem, g_gemm_smem_done[MH == 2 ? 2 : BN == 256]))
     return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(gemm smem)", smem);
   const int grid = std::min(p.num_tiles, sm_count());
-  return launch_pdl("gemm_kernel launch", gemm_kernel<BN>, dim3(grid), dim3(NTHREADS), smem, st, p);
+  return launch_pdl("gemm_kernel launch", gemm_kernel<BN, MH>, dim3(grid), dim3(NTHREADS), smem, st, p);
 }
 
-// Shared checks and launch of every GEMM entry point.
+// Shared checks and launch of every GEMM entry point.  256-row tiles (two
+// accumulator halves sharing each W stage) for the plain BF16 / FP32 stores
+// when N takes 256-wide tiles and there are at least as many such tiles as
+// SMs; else 128-row tiles, whose two accumulators let the epilogue of one
+// tile run under the next tile's MMAs (the SwiGLU and QK-norm + RoPE
+// epilogues take about as long as a tile's MMAs).
 int gemm_run(const void *A, int M, int K, const void *W, int N, int epi, int bn, rib::gemm::Params &p,
              void *stream) {
   using namespace rib::gemm;
@@ -495,12 +500,16 @@ int gemm_run(const void *A, int M, int K, const void *W, int N, int epi, int bn,
   p.N = N;
   p.K = K;
   p.epi = epi;
-  p.num_m = ceil_div(M, BM);
   const int out_cols = epi == kSwiGLU ? N / 2 : N;
-  p.num_tiles = p.num_m * (epi == kSwiGLU ? out_cols / 128 : ceil_div(N, bn));
+  const int ntiles_n = epi == kSwiGLU ? out_cols / 128 : ceil_div(N, bn);
+  const bool two_halves = bn == 256 && (epi == kBF16 || epi == kF32) && ceil_div(M, 2 * BM) * ntiles_n >= sm_count();
+  p.num_m = ceil_div(M, two_halves ? 2 * BM : BM);
+  p.num_tiles = p.num_m * ntiles_n;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bn == 256) return gemm_launch_bn<256>(p, A, W, epi == kSwiGLU ? 128 : 256, st);
-  return gemm_launch_bn<128>(p, A, W, 128, st);
+  const int w_rows = epi == kSwiGLU ? 128 : bn;
+  if (two_halves) return gemm_launch_bn<256, 2>(p, A, W, w_rows, st);
+  if (bn == 256) return gemm_launch_bn<256, 1>(p, A, W, w_rows, st);
+  return gemm_launch_bn<128, 1>(p, A, W, w_rows, st);
 }
 
 }  // namespace
