@@ -329,18 +329,30 @@ constexpr int kMergeGroup = 16;  // splits per first-level merge group
 
 // Merges `count` partials (m, l, o) of `unit` held at split slots first,
 // first + stride, ...: per head the largest m (M), and l and o weighted by
-// exp2(m - M), summed (L, O); thread tid < D computes dim tid.  The (m, l)
-// pairs are staged in shared memory by parallel loads (count <=
-// kMergeSplits); the o loads are issued in independent batches.
+// exp2(m - M), summed in split order (L, O); thread tid < D computes dim tid.
+// The o loads of the first kMergeBatch partials of both heads are issued
+// before the (m, l) pairs are staged in shared memory (count <=
+// kMergeSplits), so the merge costs one L2 round trip per kMergeBatch
+// partials instead of one per head and per unrolled chunk.
+constexpr int kMergeBatch = 16;
 __device__ __forceinline__ void merge_partials(const Params &p, Smem &s, size_t unit, int first, int stride,
                                                int count, int tid, float (&M)[2], float (&L)[2], float (&O)[2]) {
   const float *ml = p.part_ml + unit * p.max_splits * 4;  // [split][head][m, l]
   const float *po = p.part_o + unit * p.max_splits * 2 * D;
+  float v[2][kMergeBatch];
+  auto load_batch = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < kMergeBatch; ++u)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        v[hh][u] = (tid < D && k0 + u < count) ? __ldcg(&po[((first + (k0 + u) * stride) * 2 + hh) * D + tid]) : 0.f;
+  };
+  load_batch(0);  // in flight while the (m, l) pairs are staged
   for (int i = tid; i < 2 * count; i += NTHREADS) {
     const int k = i >> 1, hh = i & 1;
-    const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + (first + k * stride) * 2 + hh);
-    s.merge_m[hh][k] = v.x;
-    s.merge_l[hh][k] = v.y;
+    const float2 w = __ldcg(reinterpret_cast<const float2 *>(ml) + (first + k * stride) * 2 + hh);
+    s.merge_m[hh][k] = w.x;
+    s.merge_l[hh][k] = w.y;
   }
   __syncthreads();
   if (tid < D) {
@@ -348,16 +360,23 @@ __device__ __forceinline__ void merge_partials(const Params &p, Smem &s, size_t 
     for (int hh = 0; hh < 2; ++hh) {
       float m = -INFINITY;
       for (int k = 0; k < count; ++k) m = fmaxf(m, s.merge_m[hh][k]);
-      float l = 0.f, o = 0.f;
-#pragma unroll 16
-      for (int k = 0; k < count; ++k) {
-        const float f = fast_exp2(s.merge_m[hh][k] - m);
-        l = fmaf(s.merge_l[hh][k], f, l);
-        o = fmaf(__ldcg(&po[((first + k * stride) * 2 + hh) * D + tid]), f, o);
-      }
       M[hh] = m;
-      L[hh] = l;
-      O[hh] = o;
+      L[hh] = 0.f;
+      O[hh] = 0.f;
+    }
+    for (int k0 = 0; k0 < count; k0 += kMergeBatch) {
+      if (k0 > 0) load_batch(k0);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+          const int k = k0 + u;
+          if (k < count) {
+            const float f = fast_exp2(s.merge_m[hh][k] - M[hh]);
+            L[hh] = fmaf(s.merge_l[hh][k], f, L[hh]);
+            O[hh] = fmaf(v[hh][u], f, O[hh]);
+          }
+        }
     }
   }
 }
@@ -413,7 +432,13 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
   // Early start: tiles that end below the new token's row do not depend on the
   // kernel before this one; one ring's worth is in flight before the wait.
   const int pre = early ? max(0, min(min(STAGES, ntiles), (n - 1 - k_begin) / TK)) : 0;
+  // Fused prologue: the merge buffers are free until the merge, so they hold
+  // the RoPE angles and the staged q meanwhile.  The angles depend only on
+  // the position n - 1, so with early they are formed before the wait.
+  float *cos_t = &s.merge_m[0][0], *sin_t = &s.merge_m[0][64];
+  uint16_t *qstage = reinterpret_cast<uint16_t *>(&s.merge_m[1][0]);
   if (early) {
+    if (p.qkv) rope::rope_angles(n - 1, p.inv_freq, cos_t, sin_t, tid);
     __syncthreads();  // barriers initialised
     if (warp == NCW && lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
@@ -428,12 +453,8 @@ __device__ __forceinline__ void decode_cta(const Params &p, Smem &s, int split, 
     }
     pdl_wait();
   }
-  // Fused prologue: the merge buffers are free until the merge, so they hold
-  // the RoPE angles and the staged q meanwhile.
-  float *cos_t = &s.merge_m[0][0], *sin_t = &s.merge_m[0][64];
-  uint16_t *qstage = reinterpret_cast<uint16_t *>(&s.merge_m[1][0]);
   if (p.qkv) {
-    rope::rope_angles(n - 1, p.inv_freq, cos_t, sin_t, tid);
+    if (!early) rope::rope_angles(n - 1, p.inv_freq, cos_t, sin_t, tid);
     __syncthreads();
     const int j = lane & 15, half = lane >> 4;
     const unsigned half_mask = 0xffffu << (lane & 16);

@@ -26,6 +26,7 @@ constexpr int kStreamMinTiles = 16;    // fewest tiles per CTA (bounds segments 
 constexpr int kStreamMaxSeqs = 256;    // sequences per launch (tile prefix kept in shared memory)
 constexpr int kStreamMaxSegs = 320;    // segments per unit: at most one wave of CTAs (2 x 148) + 1
 constexpr int NCT = NCW * 32;          // consumer threads
+constexpr int kStreamMergeBatch = 16;  // segments whose partial outputs one merge round trip loads
 
 struct StreamSmem {
   alignas(128) uint8_t k[STAGES][TILE_BYTES];
@@ -350,27 +351,53 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
       emit = s.is_last;
       if (emit) {
         __threadfence();
+        // The o loads of the first kStreamMergeBatch segments of all three
+        // outputs go out before the (m, l) pairs are staged; each output is
+        // summed in segment order.
+        float v[3][kStreamMergeBatch];
+        auto load_batch = [&](int k0) {
+#pragma unroll
+          for (int u = 0; u < kStreamMergeBatch; ++u)
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+              const int i = ct + q * NCT;
+              v[q][u] = (i < 2 * D && k0 + u < nseg) ? __ldcg(&po[((k0 + u) * 2 + (i >> 7)) * D + (i & 127)]) : 0.f;
+            }
+        };
+        load_batch(0);
         for (int i = ct; i < 2 * nseg; i += NCT) {
-          const float2 v = __ldcg(reinterpret_cast<const float2 *>(ml) + i);
-          s.merge_m[i & 1][i >> 1] = v.x;
-          s.merge_l[i & 1][i >> 1] = v.y;
+          const float2 w = __ldcg(reinterpret_cast<const float2 *>(ml) + i);
+          s.merge_m[i & 1][i >> 1] = w.x;
+          s.merge_l[i & 1][i >> 1] = w.y;
         }
         consumer_sync();
+        float M[3], L[3] = {0.f, 0.f, 0.f}, O[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+          const int hh = ((ct + q * NCT) >> 7) & 1;
+          M[q] = -INFINITY;
+          for (int sp = 0; sp < nseg; ++sp) M[q] = fmaxf(M[q], s.merge_m[hh][sp]);
+        }
+        for (int k0 = 0; k0 < nseg; k0 += kStreamMergeBatch) {
+          if (k0 > 0) load_batch(k0);
+#pragma unroll
+          for (int q = 0; q < 3; ++q) {
+            const int hh = ((ct + q * NCT) >> 7) & 1;
+#pragma unroll
+            for (int u = 0; u < kStreamMergeBatch; ++u) {
+              const int sp = k0 + u;
+              if (sp < nseg) {
+                const float f = fast_exp2(s.merge_m[hh][sp] - M[q]);
+                L[q] = fmaf(s.merge_l[hh][sp], f, L[q]);
+                O[q] = fmaf(v[q][u], f, O[q]);
+              }
+            }
+          }
+        }
 #pragma unroll
         for (int q = 0; q < 3; ++q) {
           const int i = ct + q * NCT;
-          if (i >= 2 * D) continue;
-          const int hh = i >> 7, d = i & 127;
-          float M = -INFINITY;
-          for (int sp = 0; sp < nseg; ++sp) M = fmaxf(M, s.merge_m[hh][sp]);
-          float L = 0.f, O = 0.f;
-#pragma unroll 8
-          for (int sp = 0; sp < nseg; ++sp) {
-            const float f = fast_exp2(s.merge_m[hh][sp] - M);
-            L = fmaf(s.merge_l[hh][sp], f, L);
-            O = fmaf(__ldcg(&po[(sp * 2 + hh) * D + d]), f, O);
-          }
-          s.red_o[0][hh][d] = O / L;
+          if (i < 2 * D) s.red_o[0][i >> 7][i & 127] = O[q] / L[q];
         }
         if (ct == 0) p.counters[unit] = 0;  // leave the workspace ready for the next call
       }

@@ -181,7 +181,28 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
 #pragma unroll
       for (int r = 0; r < NR; ++r) wreg[r][c] = ldg_stream(wrow[r] + (c * 32 + lane) * 8);
   }
+  // The norm weight is a model constant too: this thread's chunks of it (the
+  // x chunks it stages below, at most kNwChunks of them) come in before the
+  // wait as well.
+  constexpr int kNwChunks = 2;
+  const bool nw_pre = p.nw && K <= kNwChunks * static_cast<int>(kGemvWarps * 32) * 8;
+  uint4 nwreg[kNwChunks];
+  if (nw_pre) {
+#pragma unroll
+    for (int c = 0; c < kNwChunks; ++c) {
+      const int i = (tid + c * kGemvWarps * 32) * 8;
+      if (i < K) nwreg[c] = *reinterpret_cast<const uint4 *>(p.nw + i);
+    }
+  }
   pdl_wait();
+  // The residual rows (written by an earlier kernel of the chain, complete
+  // once the wait returns) are read now, so their latency overlaps x's.
+  float resv[R];
+  if (!SW && p.epi == kResidual && lane == 0 && active) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      resv[r] = row0 + r < p.rows_out ? __uint_as_float(static_cast<uint32_t>(p.res[row0 + r]) << 16) : 0.f;
+  }
 
   // ---- x into shared memory (normalised when nw is given)
   const unsigned long long *part = nullptr;
@@ -192,8 +213,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   }
   uint64_t t0 = 0;
   float ss = 0.f;
-  for (int i = tid * 8; i < K; i += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4 *>(p.x + i);
+  auto stage8 = [&](int i, const uint4 v) {
     float f[8] = {bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y),
                   bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w)};
     if (TP && part) {
@@ -202,9 +222,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
         const unsigned long long *src = part + static_cast<size_t>(r) * p.ex.slot + i;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const ulonglong2 v = tp_read2(src + 2 * j, ex_e, t0);
-          sum[2 * j] += __uint_as_float(static_cast<uint32_t>(v.x));
-          sum[2 * j + 1] += __uint_as_float(static_cast<uint32_t>(v.y));
+          const ulonglong2 w = tp_read2(src + 2 * j, ex_e, t0);
+          sum[2 * j] += __uint_as_float(static_cast<uint32_t>(w.x));
+          sum[2 * j + 1] += __uint_as_float(static_cast<uint32_t>(w.y));
         }
       }
 #pragma unroll
@@ -223,15 +243,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
       xs[i + e] = f[e];
       ss = fmaf(f[e], f[e], ss);
     }
-  }
+  };
+  for (int i = tid * 8; i < K; i += blockDim.x * 8) stage8(i, *reinterpret_cast<const uint4 *>(p.x + i));
   if (p.nw) {
     const float inv = 1.0f / sqrtf(block_sum(ss, red) / static_cast<float>(K) + kEps);
-    for (int i = tid * 8; i < K; i += blockDim.x * 8) {
-      const uint4 w = *reinterpret_cast<const uint4 *>(p.nw + i);
+    auto norm8 = [&](int i, const uint4 w) {
       const float wf[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
                            bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
 #pragma unroll
       for (int e = 0; e < 8; ++e) xs[i + e] = round_bf16(wf[e] * round_bf16(xs[i + e] * inv));
+    };
+    if (nw_pre) {
+#pragma unroll
+      for (int c = 0; c < kNwChunks; ++c) {
+        const int i = (tid + c * kGemvWarps * 32) * 8;
+        if (i < K) norm8(i, nwreg[c]);
+      }
+    } else {
+      for (int i = tid * 8; i < K; i += blockDim.x * 8) norm8(i, *reinterpret_cast<const uint4 *>(p.nw + i));
     }
   }
   __syncthreads();
@@ -305,7 +334,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
       const float a = round_bf16(g * sigmoid_bf16(g));
       v = a * u;
     } else if (p.epi == kResidual) {
-      v = __uint_as_float(static_cast<uint32_t>(p.res[row]) << 16) + round_bf16(acc[r]);
+      v = resv[r] + round_bf16(acc[r]);
     } else {
       v = acc[r];
     }
