@@ -56,12 +56,14 @@ def profile_traffic(name: str) -> dict | None:
     return json.loads(p.read_text()) if p.exists() else None
 
 
-def decode_traffic_ratio() -> float | None:
-    """DRAM bytes (read + write) per algorithmic KV byte of the decode kernel
-    from a 4-layer capture; traffic grows with the keys processed, so it
-    scales to any launch of the same kernel."""
+def decode_traffic_ratio(kernel: str) -> float | None:
+    """DRAM bytes (read + write) per algorithmic KV byte of `kernel` from a
+    4-layer capture; traffic grows with the keys processed, so it scales to
+    any launch of the same kernel.  None when the record is of another kernel."""
     rec = profile_traffic("decode_kernel_traffic")
-    return None if rec is None else float(rec["traffic_per_algorithmic_byte"])
+    if rec is None or rec.get("kernel") != kernel:
+        return None
+    return float(rec["traffic_per_algorithmic_byte"])
 
 
 def peaks() -> dict:
@@ -543,7 +545,9 @@ def run_ours(args):
     value = bytes_step_total / (ms * 1e-3) / 1e9
     achieved = bytes_launch_local / (launch_ms * 1e-3) / 1e9
     clk = clocks.summary()
-    ratio = decode_traffic_ratio()
+    choice = int(rib.load_library().rib_decode_kernel_choice(N_LAYERS, w["n"], w["nkv"]))
+    kernel = "rib::decode::decode_streamk_kernel" if choice == 1 else "rib::decode::decode_kernel"
+    ratio = decode_traffic_ratio(kernel)
 
     # ---- N > 1 baseline: the same step as decode + a separate NCCL all-gather
     nccl = None
@@ -630,9 +634,9 @@ def run_ours(args):
                      "frac": achieved / pk["hbm_gbs"],
                      "traffic": None if ratio is None else bytes_launch_local * ratio,
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
-                                       "4-layer capture (profiles/decode_kernel_traffic.json), "
-                                       "scaled by keys",
-                     "kernel": "rib::decode::decode_kernel",
+                                       "4-layer capture of the same kernel "
+                                       "(profiles/decode_kernel_traffic.json), scaled by keys",
+                     "kernel": kernel,
                      "peak_source": pk["source"] + " hbm_gbs (copy, burst)",
                      "bytes_per_launch": bytes_launch_local, "launch_ms": launch_ms},
         "nccl_allgather_baseline": nccl,
@@ -840,6 +844,12 @@ def run_prefill(rib, device, args, pk):
     ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
     flops = wl.prefill_flops(L)
     tf = flops / (ms * 1e-3) / 1e12
+    # DRAM traffic of this very launch (L = 32768) from one ncu capture; K and V
+    # re-reads depend on L and L2 residency, so no other L is scaled from it.
+    rec = profile_traffic("prefill_kernel_traffic")
+    traffic = None
+    if rec is not None and int(rec["L"]) == L:
+        traffic = float(rec["dram_bytes_read_per_launch"]) + float(rec["dram_bytes_write_per_launch"])
     # The loop runs back to back for reps * ms, long enough for the 1000 W cap to
     # lower the SM clock, so the sustained cuBLAS figure is reported beside the burst one.
     return {"value": tf, "unit": "TFLOP/s", "L": L, "ms": ms, "flops": flops, "launches": reps,
@@ -849,6 +859,10 @@ def run_prefill(rib, device, args, pk):
                          "peak_source": pk["source"] + " bf16_tflops (burst)",
                          "peak_sustained": pk["bf16_tflops_sustained"],
                          "frac_of_sustained": tf / pk["bf16_tflops_sustained"],
+                         "traffic": traffic,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of this launch "
+                                           "(profiles/prefill_kernel_traffic.json)" if traffic else None,
+                         "algorithmic_bytes": (2 * 16 + 2 * 8) * L * 128 * 2,  # Q, O, K, FP16 V once each
                          "kernel": "rib::prefill::prefill_kernel"}}
 
 

@@ -144,6 +144,14 @@ int rib_qk_norm_rope_append(const void *qkv, int L, const void *qw,
  * ------------------------------------------------------------------------ */
 size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv);
 
+/* Which decode kernel rib_decode_attention / _batched / _ragged / _gather
+ * launch for `batch` sequences of at most max_n keys over nkv KV heads on
+ * the current device: 0 the fixed-split kernel (decode_kernel), 1 the
+ * stream-K kernel (decode_streamk_kernel), -RIB_EINVAL for a bad size.
+ * (rib_decode_attention_qkv and the no-allocation entry point always take
+ * the split kernel.)  For reporting and profiling; no call needs it. */
+int rib_decode_kernel_choice(int batch, int max_n, int nkv);
+
 /* Zeroes the counter region of a decode workspace (an enqueued memset on
  * `stream`); workspace_bytes >= 16384. */
 int rib_decode_workspace_init(void *workspace, size_t workspace_bytes,

@@ -104,6 +104,7 @@ def _bind(L: ctypes.CDLL) -> None:
         "rib_qk_norm_rope_prefill": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, vp], i),
         "rib_qk_norm_rope_append": ([vp, i, vp, vp, i, i, i, d, i, vp, vp, i, vp], i),
         "rib_decode_workspace_bytes": ([i, i, i], sz),
+        "rib_decode_kernel_choice": ([i, i, i], i),
         "rib_decode_workspace_init": ([vp, sz, vp], i),
         "rib_decode_attention": ([vp, vp, i, i, i, i, f, vp, vp, sz, vp], i),
         "rib_decode_attention_noalloc": ([vp, vp, i, i, i, i, f, vp, vp], i),

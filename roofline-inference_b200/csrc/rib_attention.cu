@@ -584,6 +584,11 @@ size_t rib_decode_workspace_bytes(int batch, int max_n, int nkv) {
                   decode_geometry(batch, max_n, nkv, use_streamk(batch, max_n, nkv)).total);
 }
 
+int rib_decode_kernel_choice(int batch, int max_n, int nkv) {
+  if (batch < 1 || max_n < 1 || nkv < 1) return -RIB_EINVAL;
+  return use_streamk(batch, max_n, nkv) ? 1 : 0;
+}
+
 int rib_decode_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
   if (!workspace || workspace_bytes < kCounterRegionBytes) return RIB_EINVAL;
   if (!aligned16(workspace)) return RIB_EALIGN;
