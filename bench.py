@@ -57,9 +57,10 @@ def profile_traffic(name: str) -> dict | None:
 
 
 def decode_traffic_ratio(kernel: str) -> float | None:
-    """DRAM bytes (read + write) per algorithmic KV byte of `kernel` from a
-    4-layer capture; traffic grows with the keys processed, so it scales to
-    any launch of the same kernel.  None when the record is of another kernel."""
+    """DRAM bytes (read + write) per algorithmic KV byte of `kernel` from one
+    ncu capture of the one-GPU launch; traffic grows with the keys processed,
+    so it scales to a rank's share at N > 1.  None when the record is of
+    another kernel."""
     rec = profile_traffic("decode_kernel_traffic")
     if rec is None or rec.get("kernel") != kernel:
         return None
@@ -569,6 +570,22 @@ def run_ours(args):
         nccl = {"value": bytes_step_total / (nccl_ms * 1e-3) / 1e9, "unit": "GB/s",
                 "ms_per_step": nccl_ms,
                 "path": "decode kernel + torch.distributed.all_gather_into_tensor (NCCL)"}
+        # the same decode with no exchange at all: what the gather adds is the
+        # difference (every rank still times its own launches, max over ranks)
+        for _ in range(args.warmup):
+            plan.launch()
+        torch.cuda.synchronize()
+        barrier(world)
+        a1, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a1.record(stream)
+        for _ in range(args.steps):
+            plan.launch()
+        b1.record(stream)
+        torch.cuda.synchronize()
+        local_ms = max_over_ranks(a1.elapsed_time(b1) / args.steps, world, device)
+        nccl["decode_only_ms_per_step"] = local_ms
+        nccl["fused_exchange_us"] = (ms - local_ms) * 1e3
+        nccl["nccl_exchange_us"] = (nccl_ms - local_ms) * 1e3
 
     # ---- engine-style: 28 per-layer launches of the same sweep
     for i in range(N_LAYERS):
@@ -633,8 +650,8 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"],
                      "traffic": None if ratio is None else bytes_launch_local * ratio,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
-                                       "4-layer capture of the same kernel "
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                       "one-GPU launch of the same kernel "
                                        "(profiles/decode_kernel_traffic.json), scaled by keys",
                      "kernel": kernel,
                      "peak_source": pk["source"] + " hbm_gbs (copy, burst)",
@@ -1251,7 +1268,9 @@ def batch_workload(eng, device, extra: int):
 
 def run_case(case: str):
     """Bounded workloads for ncu captures: decode-small is the layer-batched
-    decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches);
+    decode over 4 layers at ctx 32768 (537 MB of KV, above L2, 3 launches;
+    the stream-K kernel); decode-28 is the bench's own launch (28 layers,
+    3.76 GB of KV, the split kernel; 3 launches, for one-pass metrics only);
     prefill-small is causal prefill at L = 16384 (128 MB of Q/K/V, above L2;
     3 launches), prefill-32k the same at L = 32768 (the bench's launch);
     decode-4k is the 28-layer sweep at ctx 4096 (470 MB of KV, the stream-K
@@ -1270,9 +1289,10 @@ def run_case(case: str):
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    if case in ("decode-small", "decode-4k"):
+    if case in ("decode-small", "decode-4k", "decode-28"):
         w = make_decode_workload(0, 1, device, layers=4) if case == "decode-small" else \
-            make_decode_workload(0, 1, device, ctx=4096)
+            make_decode_workload(0, 1, device, ctx=4096) if case == "decode-4k" else \
+            make_decode_workload(0, 1, device)
         plan = DecodePlan(rib, w, device)
         for _ in range(3):
             plan.launch()
@@ -1333,7 +1353,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
-    ap.add_argument("--case", choices=["decode-small", "decode-4k", "prefill-small", "prefill-32k", "model-decode",
+    ap.add_argument("--case", choices=["decode-small", "decode-4k", "decode-28", "prefill-small", "prefill-32k",
+                                       "model-decode",
                                        "model-prefill", "gemm",
                              "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
