@@ -76,8 +76,13 @@ __device__ __forceinline__ UnitPos locate(const StreamSmem &s, int B, int nkv, i
   return u;
 }
 
-// Output of one finished unit (s.res) for the 96 consumer threads: plain
-// stores, or the NVLink all-gather of finalize_unit (decode_attention.cuh).
+// Output of one finished unit (s.red_o[0]) for the 96 consumer threads:
+// plain stores, or the NVLink all-gather of finalize_unit
+// (decode_attention.cuh) without its completion step.  A CTA may finish a
+// unit in the middle of its run of tiles, so the system-scope fence that
+// makes the peer stores visible, the count of finished units and the last
+// unit's signal and wait are deferred to stream_gather_done at the CTA's end:
+// one fence per CTA, and none in the middle of its streaming.
 __device__ __forceinline__ void stream_finalize(const Params &p, StreamSmem &s, int b, int h, int ct) {
   if (p.world == 0) {
     uint16_t *outp = p.out + (static_cast<size_t>(b) * p.nq + 2 * h) * D;
@@ -94,16 +99,27 @@ __device__ __forceinline__ void stream_finalize(const Params &p, StreamSmem &s, 
     const int r = k >> 5, i = k & 31;
     *reinterpret_cast<uint4 *>(p.gout[r] + region + row * D + 8 * i) = *reinterpret_cast<const uint4 *>(ostage + 8 * i);
   }
+}
+
+// End of a gathering CTA that finished `fin` units: one system-scope fence
+// after the barrier orders every thread's peer stores, then the units count
+// towards the rank's total; the CTA that completes it signals every peer and
+// waits, bounded, for every peer's signal, so when the kernel ends this
+// rank's buffer holds the outputs of all ranks.
+__device__ __forceinline__ void stream_gather_done(const Params &p, StreamSmem &s, int ct, int fin) {
   consumer_sync();
-  if (ct == 0) {  // one fence after the barrier orders every thread's peer stores
-    __threadfence_system();
-    s.is_last = (atomicAdd(p.done, 1) == p.total_units - 1);
+  if (ct == 0) {
+    bool last = false;
+    if (fin > 0) {
+      __threadfence_system();
+      last = atomicAdd(p.done, fin) + fin == p.total_units;
+    }
+    s.is_last = last;
   }
   consumer_sync();
-  const bool last = s.is_last;
-  consumer_sync();  // is_last is reused by the next segment
-  if (!last) return;
-  // last unit of this rank: signal every peer, then wait for every peer
+  if (!s.is_last) return;
+  const unsigned long long epoch = p.epoch_dev ? __ldcg(p.epoch_dev) + 1 : p.epoch;
+  const size_t region = p.epoch_dev ? (epoch & 1ull) * p.region_elems : 0;
   if (ct == 0) __threadfence_system();
   consumer_sync();
   if (ct < p.world) st_release_sys(p.gsig[ct] + p.rank, epoch);
@@ -265,6 +281,7 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
   const int ct = tid;  // 0 .. NCT-1
   int kw = 0;          // tiles this warp has consumed (ring position)
   bool dead = false;   // a wait gave up: skip the remaining waits
+  int fin = 0;         // units this CTA finished (all-gather count)
   for (int seg = t_begin; seg < t_end;) {
     const UnitPos u = locate(s, B, p.nkv, seg);
     const int seg_end = min(t_end, u.uend);
@@ -403,10 +420,14 @@ __global__ void __launch_bounds__(NTHREADS, 2) decode_streamk_kernel(const __gri
       }
     }
     consumer_sync();
-    if (emit) stream_finalize(p, s, u.b, u.h, ct);
+    if (emit) {
+      stream_finalize(p, s, u.b, u.h, ct);
+      ++fin;
+    }
     consumer_sync();  // s.res, s.red_* and s.merge_* are reused by the next segment
     seg = seg_end;
   }
+  if (p.world > 0) stream_gather_done(p, s, ct, fin);
 }
 
 }  // namespace decode
