@@ -517,12 +517,13 @@ def run_ours(args):
         else:
             plan.launch()
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        # The sampler's start-up leaves the GPU idle for 0.3 s; the warm-up
+        # steps run after it, right before the timed ones, so that the timed
+        # steps start at the clocks of a busy GPU.
+        for _ in range(args.warmup):
+            step()
         torch.cuda.synchronize()
         barrier(world)
         start.record(stream)
