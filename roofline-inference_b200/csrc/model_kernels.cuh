@@ -24,7 +24,11 @@ namespace rib {
 namespace model {
 
 constexpr float kEps = 1e-6f;
-constexpr int kGemvWarps = 8;
+// Warps per GEMV CTA (a build-time tuning constant).
+#ifndef RIB_GEMV_WARPS
+#define RIB_GEMV_WARPS 8
+#endif
+constexpr int kGemvWarps = RIB_GEMV_WARPS;
 constexpr int kMaxK = 8192;
 
 enum Epilogue { kNone = 0, kResidual = 1, kSwiGLU = 2, kPeerPartial = 3 };
