@@ -325,6 +325,15 @@ int rib_qk_norm_rope_prefill_dev(const void *qkv, int L, const void *qw,
                               g = bf16(W_g x), u = bf16(W_u x),
                               y = bf16(bf16(g * bf16(sigmoid(g))) * u)     */
 
+/* Launch hint OR-ed into rib_gemv's epi: 16 warps per CTA instead of 8, so
+ * half as many CTAs each stage and normalise x once for twice the rows.
+ * Results are identical.  It pays when the launch follows another GEMV; right
+ * after a decode-attention launch the narrow form is faster (its CTAs fit
+ * beside the attention's and start their weight loads before it ends).
+ * Honoured for one row per warp, K in {256, 512, 768, 1024, 1536, 2048,
+ * 3072}; otherwise ignored.  No counterpart in the reference. */
+#define RIB_GEMV_WIDE 0x100
+
 /* Batch-1 GEMV with fused input RMSNorm and epilogue.  Replaces
  * gemv(W, x, nw=, res=, swiglu=, out_float=) (agent-test/v2/kernels.py
  * :103-113, Metal source :19-97).

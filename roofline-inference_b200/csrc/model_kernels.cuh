@@ -29,6 +29,11 @@ constexpr float kEps = 1e-6f;
 #define RIB_GEMV_WARPS 8
 #endif
 constexpr int kGemvWarps = RIB_GEMV_WARPS;
+// Warps per CTA of the wide form (RIB_GEMV_WIDE): half as many CTAs, each
+// staging and normalising x once for twice the rows.  It pays after another
+// GEMV; right after the decode attention the narrow CTAs fit beside the
+// attention's and start their weight loads before it ends.
+constexpr int kGemvWideWarps = 16;
 constexpr int kMaxK = 8192;
 
 enum Epilogue { kNone = 0, kResidual = 1, kSwiGLU = 2, kPeerPartial = 3 };
@@ -161,15 +166,16 @@ struct GemvParams {
 // wait; x (and the residual) are read after it.
 // TP: the tensor-parallel forms (in_sum input, kPeerPartial epilogue) are
 // compiled in; without it those fields are ignored.
-template <int R, int C, bool SW, bool TP>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
+// W: warps per CTA (kGemvWarps, or kGemvWideWarps for the wide form).
+template <int R, int C, bool SW, bool TP, int W = kGemvWarps>
+__global__ void __launch_bounds__(W * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ float xs[];  // [K]
   __shared__ float red[32];
   pdl_launch_dependents();
   constexpr int NR = SW ? 2 * R : R;  // weight rows per warp
   const int K = p.K;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int row0 = (blockIdx.x * kGemvWarps + warp) * R;
+  const int row0 = (blockIdx.x * W + warp) * R;
   const bool active = row0 < p.rows_out;
   const int F = p.rows_out;  // up rows start at F in the SwiGLU case
   const uint16_t *wrow[NR];
@@ -189,12 +195,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   // x chunks it stages below, at most kNwChunks of them) come in before the
   // wait as well.
   constexpr int kNwChunks = 2;
-  const bool nw_pre = p.nw && K <= kNwChunks * static_cast<int>(kGemvWarps * 32) * 8;
+  const bool nw_pre = p.nw && K <= kNwChunks * static_cast<int>(W * 32) * 8;
   uint4 nwreg[kNwChunks];
   if (nw_pre) {
 #pragma unroll
     for (int c = 0; c < kNwChunks; ++c) {
-      const int i = (tid + c * kGemvWarps * 32) * 8;
+      const int i = (tid + c * W * 32) * 8;
       if (i < K) nwreg[c] = *reinterpret_cast<const uint4 *>(p.nw + i);
     }
   }
@@ -260,7 +266,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     if (nw_pre) {
 #pragma unroll
       for (int c = 0; c < kNwChunks; ++c) {
-        const int i = (tid + c * kGemvWarps * 32) * 8;
+        const int i = (tid + c * W * 32) * 8;
         if (i < K) norm8(i, nwreg[c]);
       }
     } else {

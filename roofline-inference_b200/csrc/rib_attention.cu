@@ -344,35 +344,43 @@ void *noalloc_scratch(int dev) {
 
 // ------------------------------------------------------------------ model kernels
 template <int R, int C, bool SW, bool TP>
-int gemv_launch_rc(const rib::model::GemvParams &p, cudaStream_t st) {
-  const int rows_per_cta = rib::model::kGemvWarps * R;
-  const int grid = ceil_div(p.rows_out, rows_per_cta);
+int gemv_launch_rc(const rib::model::GemvParams &p, cudaStream_t st, bool wide) {
+  using rib::model::kGemvWarps;
+  using rib::model::kGemvWideWarps;
+  if constexpr (R == 1 && C > 0 && !TP) {
+    if (wide) {
+      const int grid = ceil_div(p.rows_out, kGemvWideWarps * R);
+      return launch_pdl("gemv_kernel launch", rib::model::gemv_kernel<R, C, SW, TP, kGemvWideWarps>,
+                        dim3(grid), dim3(kGemvWideWarps * 32), p.K * sizeof(float), st, p);
+    }
+  }
+  const int grid = ceil_div(p.rows_out, kGemvWarps * R);
   return launch_pdl("gemv_kernel launch", rib::model::gemv_kernel<R, C, SW, TP>, dim3(grid),
-                    dim3(rib::model::kGemvWarps * 32), p.K * sizeof(float), st, p);
+                    dim3(kGemvWarps * 32), p.K * sizeof(float), st, p);
 }
 
 // Compile-time chunk counts for the K of Qwen3 projections, whole and split
 // over 2, 4 or 8 ranks; other K take the runtime loop.
 template <int R, bool SW, bool TP>
-int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
+int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st, bool wide) {
   switch (p.K) {
-    case 256: return gemv_launch_rc<R, 1, SW, TP>(p, st);
-    case 512: return gemv_launch_rc<R, 2, SW, TP>(p, st);
-    case 768: return gemv_launch_rc<R, 3, SW, TP>(p, st);
-    case 1024: return gemv_launch_rc<R, 4, SW, TP>(p, st);
-    case 1536: return gemv_launch_rc<R, 6, SW, TP>(p, st);
-    case 2048: return gemv_launch_rc<R, 8, SW, TP>(p, st);
-    case 3072: return gemv_launch_rc<R, 12, SW, TP>(p, st);
-    default: return gemv_launch_rc<R, 0, SW, TP>(p, st);
+    case 256: return gemv_launch_rc<R, 1, SW, TP>(p, st, wide);
+    case 512: return gemv_launch_rc<R, 2, SW, TP>(p, st, wide);
+    case 768: return gemv_launch_rc<R, 3, SW, TP>(p, st, wide);
+    case 1024: return gemv_launch_rc<R, 4, SW, TP>(p, st, wide);
+    case 1536: return gemv_launch_rc<R, 6, SW, TP>(p, st, wide);
+    case 2048: return gemv_launch_rc<R, 8, SW, TP>(p, st, wide);
+    case 3072: return gemv_launch_rc<R, 12, SW, TP>(p, st, wide);
+    default: return gemv_launch_rc<R, 0, SW, TP>(p, st, wide);
   }
 }
 
 template <int R>
-int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st) {
+int gemv_launch_r(const rib::model::GemvParams &p, cudaStream_t st, bool wide) {
   const bool tp = p.in_sum || p.epi == rib::model::kPeerPartial;
   if (p.epi == rib::model::kSwiGLU)
-    return tp ? gemv_launch_r<R, true, true>(p, st) : gemv_launch_r<R, true, false>(p, st);
-  return tp ? gemv_launch_r<R, false, true>(p, st) : gemv_launch_r<R, false, false>(p, st);
+    return tp ? gemv_launch_r<R, true, true>(p, st, wide) : gemv_launch_r<R, true, false>(p, st, wide);
+  return tp ? gemv_launch_r<R, false, true>(p, st, wide) : gemv_launch_r<R, false, false>(p, st, wide);
 }
 
 // ------------------------------------------------------------------ persistent decode step
@@ -866,17 +874,21 @@ int rib_qk_norm_rope_append_dev(const void *qkv, int L, const void *qw, const vo
 // Rows per warp: one while that still gives at least 4 CTAs per SM, more for
 // tall matrices (the LM head) so that each CTA's x load and norm are
 // amortised over more weight bytes.
-static int gemv_dispatch(const rib::model::GemvParams &p, cudaStream_t st) {
+// wide: the RIB_GEMV_WIDE hint, honoured for one-row-per-warp shapes with a
+// compile-time chunk count outside tensor parallelism.
+static int gemv_dispatch(const rib::model::GemvParams &p, cudaStream_t st, bool wide = false) {
   using rib::model::kGemvWarps;
   const int target_ctas = 4 * sm_count();
-  if (p.rows_out >= target_ctas * kGemvWarps * 4) return gemv_launch_r<4>(p, st);
-  if (p.rows_out >= target_ctas * kGemvWarps * 2) return gemv_launch_r<2>(p, st);
-  return gemv_launch_r<1>(p, st);
+  if (p.rows_out >= target_ctas * kGemvWarps * 4) return gemv_launch_r<4>(p, st, false);
+  if (p.rows_out >= target_ctas * kGemvWarps * 2) return gemv_launch_r<2>(p, st, false);
+  return gemv_launch_r<1>(p, st, wide);
 }
 
 int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const void *res, int epi,
              int out_f32, void *y, void *stream) {
   using namespace rib::model;
+  const bool wide = (epi & RIB_GEMV_WIDE) != 0;
+  epi &= ~RIB_GEMV_WIDE;
   if (!W || !x || !y || N < 1 || K < 8 || K % 8 || K > kMaxK) return RIB_EINVAL;
   if (epi != kNone && epi != kResidual && epi != kSwiGLU) return RIB_EINVAL;
   if ((epi == kResidual) != (res != nullptr)) return RIB_EINVAL;
@@ -897,7 +909,7 @@ int rib_gemv(const void *W, int N, int K, const void *x, const void *nw, const v
   p.rows_out = epi == kSwiGLU ? N / 2 : N;
   p.epi = epi;
   p.out_f32 = out_f32 ? 1 : 0;
-  return gemv_dispatch(p, static_cast<cudaStream_t>(stream));
+  return gemv_dispatch(p, static_cast<cudaStream_t>(stream), wide);
 }
 
 size_t rib_tp_buffer_bytes(int world, int slot) {

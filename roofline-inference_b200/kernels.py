@@ -182,6 +182,7 @@ def qk_norm_rope_append_batched(qkv, qw, kw, pos, cache_ptrs, caps, nq: int, nkv
 # and greedy argmax, each one kernel of csrc/model_kernels.cuh.
 
 EPI_NONE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
+GEMV_WIDE = 0x100  # RIB_GEMV_WIDE launch hint
 
 
 def _require_i32_scalar(name, t, device):
@@ -200,14 +201,15 @@ def _out_or_new(out, shape, dtype, device, name):
     return out
 
 
-def gemv(W, x, *, nw=None, res=None, swiglu=False, out_float=False, cfg=None, out=None):
+def gemv(W, x, *, nw=None, res=None, swiglu=False, out_float=False, cfg=None, out=None, wide=False):
     """y = epi(W @ pre(x)) for one token (agent-test/v2/kernels.py:103-113).
 
     W [N, K] BF16 (K a multiple of 8); x [K]; nw: fuse the input RMSNorm
     (eps 1e-6) with this weight; res: y = bf16(res + bf16(W x)); swiglu: W is
     [gate; up] and y[N/2] = bf16(bf16(g * bf16(sigmoid(g))) * u); out_float:
-    FP32 output (the logits).  `cfg` (Metal launch tuning) is accepted and
-    ignored."""
+    FP32 output (the logits).  wide: the RIB_GEMV_WIDE launch form (same
+    results; faster after another GEMV, slower right after the decode
+    attention).  `cfg` (Metal launch tuning) is accepted and ignored."""
     del cfg
     require_bf16_cuda("W", W)
     require_bf16_cuda("x", x)
@@ -229,6 +231,8 @@ def gemv(W, x, *, nw=None, res=None, swiglu=False, out_float=False, cfg=None, ou
     if res is not None and out_float:
         raise ValueError("res and out_float do not combine")
     epi = EPI_SWIGLU if swiglu else (EPI_RESIDUAL if res is not None else EPI_NONE)
+    if wide:
+        epi |= GEMV_WIDE
     n_out = N // 2 if swiglu else N
     if res is not None:
         require_bf16_cuda("res", res)

@@ -324,8 +324,8 @@ class Engine:
                                     self.base, cache.kv[i])
             o = self._attend_one(q, cache.kv[i], n)
             h = gemv(w["o"], o.reshape(-1), res=h)
-            a = gemv(w["gu"], h, nw=w["post_norm"], swiglu=True)
-            h = gemv(w["down"], a, res=h)
+            a = gemv(w["gu"], h, nw=w["post_norm"], swiglu=True, wide=True)
+            h = gemv(w["down"], a, res=h, wide=True)
         cache.offset += 1
         logits = gemv(self.embed, h, nw=self.final_norm, out_float=True)
         if return_logits:
@@ -523,8 +523,10 @@ class DecodeGraph:
             else:             # norm + RoPE + append inside the attention launch
                 self._attend_fused(L, st, w, i)
             h1 = gemv(w["o"], self.o.view(-1), res=h, out=self.h[1])
-            gemv(w["gu"], h1, nw=w["post_norm"], swiglu=True, out=self.a)
-            h = gemv(w["down"], self.a, res=h1, out=self.h[2 if h is not self.h[2] else 0])
+            # (the wide GEMV form after another GEMV; the O GEMV, right after the
+            # attention, keeps the narrow one)
+            gemv(w["gu"], h1, nw=w["post_norm"], swiglu=True, out=self.a, wide=True)
+            h = gemv(w["down"], self.a, res=h1, out=self.h[2 if h is not self.h[2] else 0], wide=True)
             launches += 5
         gemv(e.embed, h, nw=e.final_norm, out_float=True, out=self.logits)
         argmax(self.logits, out=self.tok, workspace=self.argmax_ws)

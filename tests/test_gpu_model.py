@@ -58,6 +58,22 @@ def gemv_abs_tol(mnp, W, x, nw):
 
 
 # ------------------------------------------------------------------ GEMV
+@pytest.mark.parametrize("N,K,epi", [(6144, 1024, "swiglu"), (1024, 3072, "res"), (4096, 1024, "norm"),
+                                     (1000, 512, "none"), (40, 256, "norm"), (72, 136, "none")])
+def test_gemv_wide_same_results(rib, N, K, epi):
+    """The RIB_GEMV_WIDE launch form (16 warps per CTA) gives the same bits as
+    the default form; shapes it does not cover (K without a compile-time
+    chunk count) fall back to the default form."""
+    W = rand_bf16((N, K), 11, 0.05)
+    x = rand_bf16((K,), 12)
+    nw = rand_bf16((K,), 13, 0.1) + 1 if epi in ("norm", "swiglu") else None
+    res = rand_bf16((N,), 14) if epi == "res" else None
+    a = rib.gemv(W, x, nw=nw, res=res, swiglu=epi == "swiglu")
+    b = rib.gemv(W, x, nw=nw, res=res, swiglu=epi == "swiglu", wide=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("N,K", [(4096, 1024), (1024, 2048), (1024, 3072), (1000, 512), (40, 256),
                                  (1024, 384), (64, 1536), (72, 136)])
 @pytest.mark.parametrize("epi", ["none", "norm", "res", "swiglu"])

@@ -213,6 +213,16 @@ def test_tp_entry_points_reject_bad_arguments(rib):
     assert L.rib_gemv_tp(FAKE, 64, 256, FAKE, None, 1, 0, FAKE, ctypes.byref(ex), 0, None, None) == 1
 
 
+def test_gemv_wide_flag_keeps_the_argument_checks(rib):
+    """RIB_GEMV_WIDE is a launch hint OR-ed into epi: the epilogue under it is
+    checked as without it."""
+    L = rib.load_library()
+    wide = 0x100
+    assert L.rib_gemv(FAKE, 64, 256, FAKE, None, None, 7 | wide, 0, FAKE, None) == 1   # unknown epilogue
+    assert L.rib_gemv(FAKE, 64, 256, FAKE, None, None, 1 | wide, 0, FAKE, None) == 1   # residual without res
+    assert L.rib_gemv(FAKE, 63, 256, FAKE, None, None, 2 | wide, 0, FAKE, None) == 1   # odd N for SwiGLU
+
+
 def test_fused_decode_entry_rejects_bad_arguments(rib):
     """rib_decode_attention_qkv argument checks (no launch): GQA factor, null
     pointers, non-positive base, misaligned qkv, capacity below max_n."""
