@@ -334,7 +334,10 @@ constexpr int kMergeGroup = 16;  // splits per first-level merge group
 // before the (m, l) pairs are staged in shared memory (count <=
 // kMergeSplits), so the merge costs one L2 round trip per kMergeBatch
 // partials instead of one per head and per unrolled chunk.
-constexpr int kMergeBatch = 16;
+#ifndef RIB_DECODE_MERGE_BATCH
+#define RIB_DECODE_MERGE_BATCH 40  // partials per merge round trip (build-time tuning)
+#endif
+constexpr int kMergeBatch = RIB_DECODE_MERGE_BATCH;
 __device__ __forceinline__ void merge_partials(const Params &p, Smem &s, size_t unit, int first, int stride,
                                                int count, int tid, float (&M)[2], float (&L)[2], float (&O)[2]) {
   const float *ml = p.part_ml + unit * p.max_splits * 4;  // [split][head][m, l]
