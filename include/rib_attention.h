@@ -499,6 +499,24 @@ int rib_decode_attention_qkv(const void *qkv, const void *qw, const void *kw,
 int rib_gemm(const void *A, int M, int K, const void *W, int N, int epi,
              void *C, long long ldc, void *stream);
 
+/* The same product for at most 64 rows of A (a batched decode step over up
+ * to 64 sequences, a short prompt), where the weights are what has to
+ * stream: the tcgen05 tile is 128 weight rows x 64 tokens (the operands swap
+ * roles) and K is split over enough CTAs to cover the GPU, each writing an
+ * FP32 partial to `workspace`; a second launch sums the partials of each
+ * output in split order and applies the epilogue.  Every weight byte is read
+ * once.  Replaces the reference's skinny / library GEMM for few rows
+ * (agent-test/v2/kernels.py:273-334, engine.py:95-99).
+ *   1 <= M <= 64, K a multiple of 64, N a multiple of 128;
+ *   epi RIB_GEMM_BF16 or RIB_GEMM_SWIGLU;
+ *   workspace: rib_gemm_small_workspace_bytes(M, N, K) bytes (16-byte
+ *   aligned, no initial contents); calls sharing it must not overlap on the
+ *   device. */
+size_t rib_gemm_small_workspace_bytes(int M, int N, int K);
+int rib_gemm_small(const void *A, int M, int K, const void *W, int N, int epi,
+                   void *C, long long ldc, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
 /* (cos, sin) FP32 pairs [count][64] of the RoPE angles of positions
  * pos0 .. pos0 + count - 1 (theta as kernels.py:134-138 forms it), the
  * table rib_gemm_qkv_rope reads.  16-byte aligned, count * 512 bytes. */

@@ -434,6 +434,213 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- few rows
+// C = epi(X W^T) for X of M <= 64 rows (a batched decode step, a short
+// prompt): the weights are the operand that has to stream, so the roles swap
+// (the tcgen05 tile is 128 weight rows x 64 tokens, D^T = W X^T) and K is
+// split so that the launch fills the GPU: CTA (r, s) multiplies weight rows
+// [128 r, 128 r + 128) by X over k-blocks [s kps, (s + 1) kps) and stores
+// its FP32 partial [128][64] to part[s]; gemm_small_reduce_kernel then sums
+// the partials of each output in split order (deterministic) and applies the
+// epilogue.  Every weight byte is read once; the weight k-blocks of the
+// first stages are requested before the programmatic-launch wait (model
+// constants), X's after it.
+constexpr int kSmallTok = 64;  // token rows per tile (MMA N), X rows >= M zero-filled by TMA
+constexpr int kSmallNS = 4;    // pipeline stages
+constexpr uint32_t kSmallIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                 (static_cast<uint32_t>(kSmallTok >> 3) << 17) |
+                                 (static_cast<uint32_t>(BM >> 4) << 24);
+constexpr int kSmallWBytes = BM * BK * 2;         // 16 KB
+constexpr int kSmallXBytes = kSmallTok * BK * 2;  // 8 KB
+
+struct SmallParams {
+  CUtensorMap tm_w;  // W [N][K], box (64, 128)
+  CUtensorMap tm_x;  // X [M][K], box (64, 64)
+  int M, N, K;
+  int kps;           // k-blocks per split
+  float *part;       // [splits][N][64] FP32 partials
+};
+
+struct SmallSmem {
+  alignas(1024) uint8_t w[kSmallNS][kSmallWBytes];
+  alignas(1024) uint8_t x[kSmallNS][kSmallXBytes];
+  uint64_t full[kSmallNS], empty[kSmallNS];
+  uint64_t acc_full, mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(NTHREADS, 2) gemm_small_kernel(const __grid_constant__ SmallParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  SmallSmem &s = *reinterpret_cast<SmallSmem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int kb0 = split * p.kps, nkb = min(p.K / BK, kb0 + p.kps) - kb0;  // >= 1 (host)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSmallNS; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    mbar_init(&s.acc_full, 1);
+    mbar_init(&s.mma_done, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&p.tm_w);
+    prefetch_tmap(&p.tm_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, kSmallTok);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int pre = min(nkb, kSmallNS);
+      for (int i = 0; i < pre; ++i) {  // weights: no dependence on the previous kernel
+        mbar_arrive_expect_tx(&s.full[i], kSmallWBytes + kSmallXBytes);
+        tma_load_2d(s.w[i], &p.tm_w, (kb0 + i) * BK, tile * BM, &s.full[i]);
+      }
+      pdl_wait();  // X is the previous kernel's output
+      for (int i = 0; i < pre; ++i) tma_load_2d(s.x[i], &p.tm_x, (kb0 + i) * BK, 0, &s.full[i]);
+      int issued = pre;
+      for (int i = pre; i < nkb; ++i) {
+        const int st = i % kSmallNS;
+        if (aborted(s) || !mbar_wait(&s.empty[st], ((i / kSmallNS) - 1) & 1)) {
+          set_abort(s);
+          break;
+        }
+        mbar_arrive_expect_tx(&s.full[st], kSmallWBytes + kSmallXBytes);
+        tma_load_2d(s.w[st], &p.tm_w, (kb0 + i) * BK, tile * BM, &s.full[st]);
+        tma_load_2d(s.x[st], &p.tm_x, (kb0 + i) * BK, 0, &s.full[st]);
+        issued = i + 1;
+      }
+      // drain: every copy issued must land before the CTA may exit
+      for (int t = max(0, issued - kSmallNS); t < issued; ++t) mbar_wait(&s.full[t % kSmallNS], (t / kSmallNS) & 1);
+    } else {
+      pdl_wait();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    pdl_wait();
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        const int st = i % kSmallNS;
+        if (aborted(s) || !mbar_wait(&s.full[st], (i / kSmallNS) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(s.w[st]), b = smem_u32(s.x[st]);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_ss(tmem, sw128_desc(a + kk * 32), sw128_desc(b + kk * 32), kSmallIdesc, (i | kk) != 0);
+        tc_commit(&s.empty[st]);
+      }
+      if (ok) tc_commit(&s.acc_full);
+      else set_abort(s);
+      tc_commit(&s.mma_done);
+      mbar_wait(&s.mma_done, 0);
+    }
+    __syncwarp();
+  } else {
+    pdl_wait();  // the partials may still be read by the previous call's reduction
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int n = tile * BM + quad * 32 + lane;  // weight row = output column
+    if (warp_wait(s, &s.acc_full, 0)) {
+      tc_fence_after();
+      uint32_t r0[32], r1[32];
+      const uint32_t ta = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+      tmem_ld32(ta, r0);
+      tmem_ld32(ta + 32, r1);
+      tmem_wait_ld();
+      float4 *dst = reinterpret_cast<float4 *>(p.part + (static_cast<size_t>(split) * p.N + n) * kSmallTok);
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        dst[v] = make_float4(__uint_as_float(r0[4 * v]), __uint_as_float(r0[4 * v + 1]),
+                             __uint_as_float(r0[4 * v + 2]), __uint_as_float(r0[4 * v + 3]));
+#pragma unroll
+      for (int v = 0; v < 8; ++v)
+        dst[8 + v] = make_float4(__uint_as_float(r1[4 * v]), __uint_as_float(r1[4 * v + 1]),
+                                 __uint_as_float(r1[4 * v + 2]), __uint_as_float(r1[4 * v + 3]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kSmallTok);
+}
+
+struct SmallReduceParams {
+  const float *part;  // [splits][N][64]
+  int splits, N, M;
+  int swiglu_f;       // > 0: SwiGLU over gate rows [0, F) and up rows [F, 2F)
+  uint16_t *c;        // BF16 [M][ldc]
+  long long ldc;
+};
+
+// Sums the partials of 8 output columns x 64 tokens in split order
+// (thread = token m and columns c, c + 4; the loads of 8 splits are in
+// flight at once), applies the epilogue (BF16 store, or SwiGLU with the
+// rounding points of epi_swiglu) and writes the M valid token rows, 16 bytes
+// per row.
+constexpr int kReduceCols = 8;
+__global__ void __launch_bounds__(256) gemm_small_reduce_kernel(const __grid_constant__ SmallReduceParams p) {
+  __shared__ float t[kSmallTok][kReduceCols + 1];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int n0 = blockIdx.x * kReduceCols;
+  const int m = threadIdx.x & 63, c = threadIdx.x >> 6;
+  const size_t ss = static_cast<size_t>(p.N) * kSmallTok;  // split stride
+  const int nsrc = p.swiglu_f > 0 ? 4 : 2;
+  const float *src[4];
+  src[0] = p.part + static_cast<size_t>(n0 + c) * kSmallTok + m;
+  src[1] = src[0] + 4 * kSmallTok;
+  src[2] = src[0] + static_cast<size_t>(p.swiglu_f) * kSmallTok;  // up rows (SwiGLU)
+  src[3] = src[2] + 4 * kSmallTok;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s0 = 0; s0 < p.splits; s0 += 8) {
+    float v[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[k][u] = (k < nsrc && s0 + u < p.splits) ? __ldcg(src[k] + (s0 + u) * ss) : 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < p.splits) acc[k] += v[k][u];
+  }
+  if (p.swiglu_f > 0) {
+    acc[0] = silu_bf16(round_bf16(acc[0])) * round_bf16(acc[2]);
+    acc[1] = silu_bf16(round_bf16(acc[1])) * round_bf16(acc[3]);
+  }
+  t[m][c] = acc[0];
+  t[m][c + 4] = acc[1];
+  __syncthreads();
+  if (threadIdx.x < p.M) {
+    const float *r = t[threadIdx.x];
+    uint4 w;
+    w.x = pack_bf16x2(r[0], r[1]);
+    w.y = pack_bf16x2(r[2], r[3]);
+    w.z = pack_bf16x2(r[4], r[5]);
+    w.w = pack_bf16x2(r[6], r[7]);
+    *reinterpret_cast<uint4 *>(p.c + static_cast<size_t>(threadIdx.x) * p.ldc + n0) = w;
+  }
+}
+
 // ---------------------------------------------------------------- RoPE table
 // (cos, sin) of the 64 angles of positions pos0 .. pos0 + count - 1, each as
 // rope::rope_angles forms it; one CTA of 64 threads per position.

@@ -1224,6 +1224,67 @@ int rib_gemm(const void *A, int M, int K, const void *W, int N, int epi, void *C
   return gemm_run(A, M, K, W, N, e, bn, p, stream);
 }
 
+// Few-row GEMM: weight row tiles x K splits, enough CTAs to cover the SMs.
+struct SmallGeom {
+  int row_tiles, splits, kps;
+};
+SmallGeom small_geometry(int N, int K) {
+  SmallGeom g;
+  const int kb = K / rib::gemm::BK;
+  g.row_tiles = N / rib::gemm::BM;
+  const int want = std::max(1, std::min(kb, ceil_div(sm_count(), g.row_tiles)));
+  g.kps = ceil_div(kb, want);
+  g.splits = ceil_div(kb, g.kps);
+  return g;
+}
+
+bool g_gemm_small_smem_done[kMaxDevices];
+
+size_t rib_gemm_small_workspace_bytes(int M, int N, int K) {
+  if (M < 1 || M > rib::gemm::kSmallTok || N < 128 || N % 128 || K < 64 || K % 64) return 0;
+  const SmallGeom g = small_geometry(N, K);
+  return static_cast<size_t>(g.splits) * N * rib::gemm::kSmallTok * sizeof(float);
+}
+
+int rib_gemm_small(const void *A, int M, int K, const void *W, int N, int epi, void *C, long long ldc,
+                   void *workspace, size_t workspace_bytes, void *stream) {
+  using namespace rib::gemm;
+  if (!A || !W || !C || !workspace) return RIB_EINVAL;
+  if (M < 1 || M > kSmallTok || N < 128 || N % 128 || K < 64 || K % 64) return RIB_EINVAL;
+  if (epi != RIB_GEMM_BF16 && epi != RIB_GEMM_SWIGLU) return RIB_EINVAL;
+  const int n_out = epi == RIB_GEMM_SWIGLU ? N / 2 : N;
+  if (n_out % kReduceCols || ldc < n_out) return RIB_EINVAL;
+  if (workspace_bytes < rib_gemm_small_workspace_bytes(M, N, K)) return RIB_EINVAL;
+  if (!aligned16(A) || !aligned16(W) || !aligned16(C) || !aligned16(workspace) || (ldc * 2) % 16)
+    return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  const SmallGeom g = small_geometry(N, K);
+  SmallParams p = {};
+  if (!gemm_map(&p.tm_w, W, N, K, K, BM) || !gemm_map(&p.tm_x, A, M, K, K, kSmallTok)) return RIB_ECUDA;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.kps = g.kps;
+  p.part = static_cast<float *>(workspace);
+  const int smem = static_cast<int>(sizeof(SmallSmem)) + 1024;
+  if (!set_smem_once(gemm_small_kernel, smem, g_gemm_small_smem_done))
+    return rib::host_fail(RIB_ECUDA, "cudaFuncSetAttribute(gemm small smem)", smem);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rc = launch_pdl("gemm_small_kernel launch", gemm_small_kernel, dim3(g.row_tiles, g.splits),
+                            dim3(NTHREADS), smem, st, p);
+  if (rc != RIB_OK) return rc;
+  SmallReduceParams r = {};
+  r.part = p.part;
+  r.splits = g.splits;
+  r.N = N;
+  r.M = M;
+  r.swiglu_f = epi == RIB_GEMM_SWIGLU ? N / 2 : 0;
+  r.c = static_cast<uint16_t *>(C);
+  r.ldc = ldc;
+  return launch_pdl("gemm_small_reduce_kernel launch", gemm_small_reduce_kernel, dim3(n_out / kReduceCols),
+                    dim3(256), 0, st, r);
+}
+
 int rib_rope_table(int pos0, int count, double base, void *table, void *stream) {
   if (!table || pos0 < 0 || count < 1 || !(base > 0.0)) return RIB_EINVAL;
   if (!aligned16(table)) return RIB_EALIGN;

@@ -34,6 +34,10 @@ def _bind(L) -> None:
     L.rib_rope_table.restype = i
     L.rib_gemm_qkv_rope.argtypes = [vp, i, i, vp, i, i, vp, vp, vp, i, vp, i, vp, i, vp]
     L.rib_gemm_qkv_rope.restype = i
+    L.rib_gemm_small_workspace_bytes.argtypes = [i, i, i]
+    L.rib_gemm_small_workspace_bytes.restype = ctypes.c_size_t
+    L.rib_gemm_small.argtypes = [vp, i, i, vp, i, i, vp, ll, vp, ctypes.c_size_t, vp]
+    L.rib_gemm_small.restype = i
 
 
 _bound = None
@@ -58,12 +62,38 @@ def _check_operands(A, W):
         raise ValueError(f"K ({A.shape[1]}) must be a multiple of 64")
 
 
-def gemm(A: torch.Tensor, W: torch.Tensor, *, epi: str = "bf16", out: torch.Tensor | None = None) -> torch.Tensor:
+SMALL_M = 64  # rows up to which gemm() takes the few-row kernel
+
+_small_ws: dict[int, torch.Tensor] = {}
+
+
+def _small_workspace(device, nbytes: int) -> torch.Tensor:
+    """One partials buffer per device, grown on demand (a CUDA graph that
+    captures gemm() must have run it once at its largest shape first)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _small_ws.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _small_ws[idx] = ws
+    return ws
+
+
+def small_ok(M: int, N: int, K: int, epi: str) -> bool:
+    """Whether rib_gemm_small takes this shape."""
+    cols = N // 2 if epi == "swiglu" else N
+    return (1 <= M <= SMALL_M and epi in ("bf16", "swiglu") and N % 128 == 0 and K % 64 == 0
+            and cols % 8 == 0)
+
+
+def gemm(A: torch.Tensor, W: torch.Tensor, *, epi: str = "bf16", out: torch.Tensor | None = None,
+         small: bool | None = None) -> torch.Tensor:
     """epi(A W^T) for A [M, K], W [N, K] (K a multiple of 64).
 
     epi "bf16": [M, N] BF16 (N a multiple of 8); "f32": [M, N] FP32;
     "swiglu": W = [gate; up] with N = 2F rows (F a multiple of 128), returns
-    [M, F] = bf16(bf16(g bf16(sigmoid(g))) u), g and u the BF16 products."""
+    [M, F] = bf16(bf16(g bf16(sigmoid(g))) u), g and u the BF16 products.
+    small: the few-row kernel (rib_gemm_small: weights as the 128-row
+    operand, K split over the GPU); by default for M <= 64 where it applies."""
     _check_operands(A, W)
     if epi not in _EPI:
         raise ValueError(f"unknown epilogue {epi!r}")
@@ -75,8 +105,20 @@ def gemm(A: torch.Tensor, W: torch.Tensor, *, epi: str = "bf16", out: torch.Tens
         out = torch.empty((M, cols), dtype=dtype, device=A.device)
     elif out.dtype != dtype or out.shape != (M, cols) or not out.is_contiguous() or out.device != A.device:
         raise ValueError(f"out must be a contiguous {dtype} tensor [{M}, {cols}] on {A.device}")
-    st = _L().rib_gemm(A.data_ptr(), M, K, W.data_ptr(), N, _EPI[epi], out.data_ptr(), cols,
-                       stream_handle(A.device))
+    if small is None:
+        small = small_ok(M, N, K, epi)
+    L = _L()
+    if small:
+        if not small_ok(M, N, K, epi):
+            raise ValueError(f"the few-row GEMM does not take M={M}, N={N}, K={K}, epi={epi!r}")
+        nbytes = int(L.rib_gemm_small_workspace_bytes(M, N, K))
+        ws = _small_workspace(A.device, nbytes)
+        st = L.rib_gemm_small(A.data_ptr(), M, K, W.data_ptr(), N, _EPI[epi], out.data_ptr(), cols,
+                              ws.data_ptr(), ws.numel(), stream_handle(A.device))
+        _lib.check(st, "gemm_small")
+        return out
+    st = L.rib_gemm(A.data_ptr(), M, K, W.data_ptr(), N, _EPI[epi], out.data_ptr(), cols,
+                    stream_handle(A.device))
     _lib.check(st, "gemm")
     return out
 

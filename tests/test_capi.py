@@ -135,6 +135,31 @@ def test_gemm_rejects_bad_arguments(rib):
     assert L.rib_rope_table(0, 0, 1e6, FAKE, None) == 1
 
 
+def test_gemm_few_rows_rejects_bad_arguments(rib):
+    """rib_gemm_small: 1-64 rows, K a multiple of 64, N of 128, BF16 or SwiGLU
+    epilogue, a workspace of the stated size; checked before any launch."""
+    import importlib
+    G = importlib.import_module("roofline-inference_b200.gemm")
+    L = G._L()
+    ws = int(L.rib_gemm_small_workspace_bytes(64, 4096, 1024))
+    assert ws > 0
+    assert L.rib_gemm_small_workspace_bytes(65, 4096, 1024) == 0
+    assert L.rib_gemm_small_workspace_bytes(64, 4000, 1024) == 0
+
+    def call(M=64, K=1024, N=4096, epi=0, ldc=4096, nbytes=ws, A=FAKE, C=FAKE, wsp=FAKE):
+        return L.rib_gemm_small(A, M, K, FAKE, N, epi, C, ldc, wsp, nbytes, None)
+    assert call(M=0) == 1
+    assert call(M=65) == 1
+    assert call(K=96) == 1
+    assert call(N=4000, ldc=4000) == 1
+    assert call(epi=1) == 1               # FP32 output is not offered
+    assert call(ldc=100) == 1
+    assert call(nbytes=ws - 16) == 1
+    assert call(wsp=None) == 1
+    assert call(A=MISALIGNED) == 3
+    assert call(C=MISALIGNED) == 3
+
+
 def test_wait_limit_range_checked_on_host(rib):
     L = rib.load_library()
     assert L.rib_set_wait_limit_ns(10) == 1

@@ -66,6 +66,43 @@ def test_gemm_qwen3_shapes_4096(G, wl):
         _ulp_close(u16(C)[rows], model_np.matmul(u16(A)[rows], u16(W)))
 
 
+@pytest.mark.parametrize("M", [1, 16, 37, 64])
+@pytest.mark.parametrize("N,K,epi", [(4096, 1024, "bf16"), (1024, 2048, "bf16"), (1024, 3072, "bf16"),
+                                     (6144, 1024, "swiglu"), (256, 64, "bf16"), (512, 128, "swiglu")])
+def test_gemm_few_rows_matches_oracle(G, wl, M, N, K, epi):
+    """The few-row GEMM (rib_gemm_small: weights as the 128-row operand, K
+    split over the GPU, partials summed in split order) against the oracle,
+    at the Qwen3 projection shapes of a 64-sequence batched decode step; two
+    calls in a row on the shared partials buffer give the same bits."""
+    from oracle import model_np
+    A, W = _inputs(wl, M, N, K, seed=M * 7 + N + K)
+    y = G.gemm(A, W, epi=epi, small=True)
+    y2 = G.gemm(A, W, epi=epi, small=True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    want = model_np.matmul(u16(A), u16(W))
+    if epi == "swiglu":
+        want = model_np.swiglu(want)
+        d = np.abs(bf16f(u16(y)) - bf16f(want))
+        assert d.max() <= 6.25e-2, d.max()
+        assert (u16(y) != want).mean() <= 0.02
+        assert torch.equal(y, importlib.import_module("roofline-inference_b200").swiglu(G.gemm(A, W, small=True)))
+    else:
+        _ulp_close(u16(y), want)
+
+
+def test_gemm_few_rows_routing(G, wl):
+    """gemm() takes the few-row kernel by default up to 64 rows where its
+    shape rules hold, and refuses it explicitly where they do not."""
+    assert G.small_ok(64, 4096, 1024, "bf16") and G.small_ok(1, 6144, 1024, "swiglu")
+    assert not G.small_ok(65, 4096, 1024, "bf16")
+    assert not G.small_ok(16, 1000, 1024, "bf16")
+    assert not G.small_ok(16, 4096, 1024, "f32")
+    A, W = _inputs(wl, 16, 1000, 256, seed=3)
+    with pytest.raises(ValueError):
+        G.gemm(A, W, small=True)
+
+
 @pytest.mark.parametrize("M,N,K", [(200, 512, 3072), (33, 1000, 256)])
 def test_gemm_f32(G, wl, M, N, K):
     A, W = _inputs(wl, M, N, K, seed=5)
@@ -113,8 +150,9 @@ def test_gemm_qkv_rope(G, rib, wl, oracle, M, pos0, nkv):
     keep[pos0:pos0 + M] = False
     assert np.array_equal(u16(cache)[:, :, keep], u16(before)[:, :, keep])
     assert not Q[:, M:].any()
-    # bit-identical to the two-kernel path on the same BF16 projection
-    qkv = G.gemm(A, W)
+    # bit-identical to the two-kernel path on the same BF16 projection (the
+    # tiled GEMM's: the few-row kernel sums K in another order)
+    qkv = G.gemm(A, W, small=False)
     cache2 = before.clone()
     Q2 = rib.qk_norm_rope_append(qkv, qw, kw, pos0, nq, nkv, 1e6, cache2, Lp)
     torch.cuda.synchronize()
@@ -161,4 +199,4 @@ def test_gemm_argument_checks(G, wl):
     with pytest.raises(ValueError):
         G.gemm(A, wl.randn_bf16((100, 64), seed=2, device="cuda"))  # N not a multiple of 8
     with pytest.raises(ValueError):
-        G.gemm(A, W, epi="swiglu")                 # F = 64 is not a multiple of 128
+        G.gemm(A, W, epi="swiglu", small=False)    # F = 64 is not a multiple of 128 (tiled GEMM)
