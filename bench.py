@@ -1203,10 +1203,10 @@ def run_model_batch(rib, eng, device, args):
            "reference_line_ms": line["time_s"] * 1e3, "reference_bottleneck": line["bottleneck"],
            "fraction_of_line": line["time_s"] * 1e3 / ms,
            "launches_per_step": dec.launches_per_step,
-           "path": "BatchDecoder.step replayed from one CUDA graph: few-row tcgen05 GEMMs for the projections "
-                   "(rib_gemm_small, SwiGLU fused), rib_qk_norm_rope_append_batched, "
-                   "rib_decode_attention_ragged, add_rms kernels, cuBLAS FP32-output LM-head GEMM, "
-                   "rib_argmax_rows_f32"}
+           "path": "BatchDecoder.step replayed from one CUDA graph: cuBLAS GEMMs for the projections at 64 rows "
+                   "(faster there than this package's few-row and tiled GEMMs), SwiGLU kernel, "
+                   "rib_qk_norm_rope_append_batched, rib_decode_attention_ragged, add_rms kernels, "
+                   "cuBLAS FP32-output LM-head GEMM, rib_argmax_rows_f32"}
     del dec
     torch.cuda.empty_cache()
     return res

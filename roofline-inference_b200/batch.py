@@ -3,7 +3,7 @@ each in its own contiguous cache of its own capacity, decoding one token each
 per step (engine.py:33-40 and :145-163 generalised to many sequences; the
 reference engine is single-stream).
 
-Per step and layer: norm + QKV GEMM over the S rows (gemm.py), the batched
+Per step and layer: norm + QKV GEMM over the S rows (cuBLAS up to 64 rows), the batched
 qk-norm + RoPE + append (each sequence at its own position, into its own
 cache), split-KV decode attention over the per-sequence caches (lengths on
 the device), O GEMM + residual/RMSNorm (add_rms), gate/up GEMM + SwiGLU, down
@@ -26,13 +26,19 @@ from . import _lib
 from ._tensors import HEAD_DIM, stream_handle
 from .cache import Cache
 from .gemm import gemm
-from .kernels import add_rms, embedding, rms_norm
+from .kernels import add_rms, embedding, rms_norm, swiglu
 
 
 def _linear(x, W, epi: str = "bf16"):
-    """x W^T on this package's GEMM: the few-row kernel (weights as the
-    128-row operand, K split over the GPU) up to 64 rows, the tiled one above."""
-    return gemm(x, W, epi=epi)
+    """x W^T for the S rows of a step.  Up to 64 rows cuBLAS (a plain library
+    GEMM) is faster than both of this package's GEMMs: timed as CUDA graphs
+    of 28 calls at M = 16-64 it takes 3.5-8.3 us per Qwen3 projection, the
+    few-row tcgen05 GEMM (gemm.py) 7.7-8.1 us (two launches), the tiled one
+    9-21 us.  Above 64 rows the tiled tcgen05 GEMM, SwiGLU fused."""
+    if x.shape[0] > 64:
+        return gemm(x, W, epi=epi)
+    y = torch.matmul(x, W.t())
+    return swiglu(y) if epi == "swiglu" else y
 
 
 class SlotDecoder:
@@ -64,9 +70,9 @@ class SlotDecoder:
         self.next = torch.empty(slots, dtype=torch.int32, device=dev)
         self.graph = None
         self.graph_logits = None
-        # per layer: 4 projections (2 launches each on the few-row GEMM, 1 on the
-        # tiled one, the SwiGLU in its epilogue), append, attention, 2 add_rms
-        per_layer = 4 * (2 if slots <= 64 else 1) + 4
+        # per layer: 4 projections (+ a SwiGLU launch up to 64 rows; above, the
+        # tiled GEMM fuses it), append, attention, 2 add_rms
+        per_layer = 4 + (1 if slots <= 64 else 0) + 4
         self.launches_per_step = per_layer * cfg.num_layers + 8
 
     # ---------------------------------------------------------------- membership
@@ -153,8 +159,8 @@ class SlotDecoder:
                                               stream_handle(self.device)), "argmax_rows")
 
     def capture(self):
-        """Records one whole step (forward, row argmax, next inputs: 12 launches
-        per layer on the few-row GEMM, 8 more per step) in a CUDA graph;
+        """Records one whole step (forward, row argmax, next inputs: 9 launches
+        per layer, 8 more per step; cuBLAS may add split-K reductions) in a CUDA graph;
         later steps replay it, so a step costs one host launch.  Every input
         of the step lives in a fixed device buffer, and the GEMM shapes
         depend only on the slot count, so one graph serves every position and
@@ -166,8 +172,8 @@ class SlotDecoder:
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(self.stream)
         with torch.cuda.stream(side):
-            # Warm-up outside the graph (first-call set-up of every launch, and
-            # the few-row GEMM's partials buffer at its largest size).  It appends K/V at each active slot's next position,
+            # Warm-up outside the graph (first-call set-up of cuBLAS and every
+            # launch).  It appends K/V at each active slot's next position,
             # which the next real step overwrites before any attention reads
             # it; the device positions are then wound back.
             self._argmax(self._forward())
