@@ -798,16 +798,17 @@ def run_e2e(rib, w, rank, world, device, args, gather, plan):
     caps = torch.full((N_LAYERS,), w["cap"], dtype=torch.int32, device=device)
     caches = w["caches"]
     stream = torch.cuda.current_stream(device)
-    launches = 2
+    launches = 2 if gather is not None else 1
 
     def step():
         qkv_dev.copy_(qkv_host, non_blocking=True)
-        # every layer's norm + RoPE + append in one launch (the layers as a batch of caches)
-        q = rib.qk_norm_rope_append_batched(qkv_dev, qw, kw, pos_dev, plan.ptrs, caps, nq, nkv, 1e6)
         if gather is not None:
+            # every layer's norm + RoPE + append in one launch (the layers as a batch of caches)
+            q = rib.qk_norm_rope_append_batched(qkv_dev, qw, kw, pos_dev, plan.ptrs, caps, nq, nkv, 1e6)
             full = gather.decode(q, plan.ptrs, lens, w["n"], w["cap"], 128 ** -0.5, plan.ws)
         else:
-            full = rib.decode_attention_batched(q, caches, lens, 128 ** -0.5, max_n=w["n"])
+            # the norm + RoPE + append of all 28 layers inside the decode launch
+            full = rib.decode_attention_qkv(qkv_dev, qw, kw, 1e6, caches, lens, 128 ** -0.5, max_n=w["n"])
         out_host.copy_(full, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -826,8 +827,9 @@ def run_e2e(rib, w, rank, world, device, args, gather, plan):
             "h2d_bytes_per_step": qkv_host.numel() * 2,
             "d2h_bytes_per_step": out_host.numel() * 2,
             "gpu_launches_per_step": launches,
-            "path": "qk_norm_rope_append_batched (28 layers, one launch) + decode_attention_batched (public API)"
-                    + ("; NVLinkGather.decode (fused all-gather) at N > 1" if world > 1 else "")}
+            "path": ("qk_norm_rope_append_batched (28 layers, one launch) + NVLinkGather.decode (fused all-gather)"
+                     if world > 1 else
+                     "decode_attention_qkv (public API: the 28 layers' norm + RoPE + append fused into the decode launch)")}
 
 
 def run_prefill(rib, device, args, pk):
