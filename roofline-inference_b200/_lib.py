@@ -1,7 +1,7 @@
 """Loader of the C-ABI library librib_attention.so (CUDA kernels for sm_100a).
 
 The library is built in-tree from csrc/ with nvcc.  `load()` rebuilds it when
-the sources changed (content hash, not mtimes, so a copied tree is judged
+the sources changed (content hash, not mtimes, so a copied tree is recognised
 correctly) and then binds the entry points declared in
 include/rib_attention.h with ctypes.  There is no fallback: if the library
 cannot be built or loaded, every call raises.
