@@ -591,6 +591,51 @@ int rib_argmax_f32_tp(const float *x, int n, int index_offset, int32_t *out,
                       void *workspace, const rib_tp_exchange *ex,
                       void *stream);
 
+/* ------------------------------------------------------------------------ *
+ * Tensor parallelism of the prefill projections: the exchange after the
+ * row-parallel O and down GEMMs of Engine.prefill
+ * (agent-test/v2/engine.py:111-116, the add_rms after each projection,
+ * agent-test/v2/kernels.py:227-268), fused over NVLink peer memory in place
+ * of an NCCL all-reduce.  Rows [o rpo, (o + 1) rpo) belong to rank o,
+ * rpo = ceil(M / world).
+ *
+ *   rib_gemm_tp_partial    FP32 A W^T, each row stored straight into its
+ *                          owner rank's receive slot for this rank (a
+ *                          reduce-scatter inside the tcgen05 GEMM).
+ *   rib_tp_reduce_add_rms  every rank's owned rows summed in rank order,
+ *                          rounded to BF16 and stored into every rank's
+ *                          gather buffer; then on every rank, for all M
+ *                          rows, residual = bf16(residual + r) and, when
+ *                          norm_w is given, out = the RMSNorm of it (the
+ *                          rounding of rib_add_rms).
+ *
+ * Call them in pairs, with the same M, on every rank in the same order.
+ * Exchange buffer of one rank: rib_tp_prefill_buffer_bytes(world,
+ * rows_cap, hidden) bytes, zeroed, shared through rib_peer_buffer_alloc /
+ * _open.  epoch: the pair's number, larger than every epoch used before on
+ * these buffers and the same on every rank.  Waits for other ranks are
+ * bounded (rib_set_wait_limit_ns); after one runs out
+ * (rib_take_device_status() == RIB_ETIMEOUT) the buffers must be freed and
+ * new ones made. */
+typedef struct rib_tp_prefill_exchange {
+  int world, rank;
+  uint64_t buf[RIB_TP_MAX_RANKS]; /* per rank: its exchange buffer (peer mapping) */
+  int rows_cap;                    /* rows the buffers hold (M <= rows_cap)        */
+  int hidden;                      /* N of the projections: 256, 512, 1024, 2048   */
+} rib_tp_prefill_exchange;
+
+size_t rib_tp_prefill_buffer_bytes(int world, int rows_cap, int hidden);
+
+/* A [M][K] BF16 (K % 64 == 0), W [hidden][K] BF16 (this rank's columns). */
+int rib_gemm_tp_partial(const void *A, int M, int K, const void *W,
+                        const rib_tp_prefill_exchange *ex, void *stream);
+
+/* residual [M][hidden] BF16 in/out; norm_w [hidden] BF16 or NULL; out
+ * [M][hidden] BF16 (unused when norm_w is NULL). */
+int rib_tp_reduce_add_rms(const rib_tp_prefill_exchange *ex, int M,
+                          unsigned long long epoch, void *residual,
+                          const void *norm_w, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

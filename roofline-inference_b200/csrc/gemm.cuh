@@ -46,7 +46,9 @@ constexpr int NWARPS = 6;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int kEpiThreads = 128;
 
-enum Epi : int { kBF16 = 0, kF32 = 1, kSwiGLU = 2, kQKRope = 3 };
+enum Epi : int { kBF16 = 0, kF32 = 1, kSwiGLU = 2, kQKRope = 3, kF32Owner = 4 };
+
+constexpr int kMaxRanks = 8;
 
 // MH = 1: 128-row tiles, two accumulators (the epilogue of one tile overlaps
 // the next tile's MMAs).  MH = 2: 256-row tiles as two M = 128 halves that
@@ -79,6 +81,9 @@ struct Smem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
+  // kF32Owner: each epilogue warp's 32 rows x 32 columns, rows padded to 36
+  // floats (16-byte stores and loads without bank conflicts)
+  alignas(16) float ostage[4][32 * 36];
 };
 
 struct Params {
@@ -98,6 +103,12 @@ struct Params {
   int Lp;
   uint16_t *cache;          // [2][nkv][cap][128]
   int cap;
+  // kF32Owner (tensor-parallel prefill): row m's FP32 partial goes to rank
+  // o = m / rpo's receive buffer, slot `rank`, row m - o rpo (a plain store
+  // when o is this rank, else a store over NVLink); ldc = N.
+  float *owner_recv[kMaxRanks];  // each rank's receive slots [world][rpo_cap][N], as seen from here
+  int rpo, rank;
+  long long slot_floats;         // rpo_cap * N
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -163,6 +174,41 @@ __device__ __forceinline__ void epi_store(const Params &p, uint32_t ta, int m, i
         dst[v] = w;
       }
     }
+  }
+}
+
+// kF32Owner: the rows of this warp (m_base + lane) go to their owner ranks.
+// A thread holds one row of 32 columns after tcgen05.ld; staged through
+// shared memory, each store instruction then writes four rows' 128-byte
+// segments (eight lanes per row) instead of 32 scattered 16-byte pieces, the
+// form that moves well over NVLink.
+template <int BN>
+__device__ __forceinline__ void epi_store_owner(const Params &p, uint32_t ta, int m_base, int n0, float *stage) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane & 7;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld32(ta + c0, r);
+    tmem_wait_ld();
+    float4 *srow = reinterpret_cast<float4 *>(stage + lane * 36);
+#pragma unroll
+    for (int v = 0; v < 8; ++v)
+      srow[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                            __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+    __syncwarp();
+    const int ncols = p.N - (n0 + c0);  // columns past N (a ragged last tile) are not stored
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int i = it * 4 + (lane >> 3);
+      const int m = m_base + i;
+      if (m < p.M && 4 * j < ncols) {
+        const float4 v = *reinterpret_cast<const float4 *>(stage + i * 36 + 4 * j);
+        float *row = p.owner_recv[m / p.rpo] + p.rank * p.slot_floats + (m % p.rpo) * p.ldc;
+        *reinterpret_cast<float4 *>(row + n0 + c0 + 4 * j) = v;
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -420,12 +466,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemm_kernel(const __grid_constant
 #pragma unroll 1
           for (int hh = 0; hh < BN / 128; ++hh) epi_qk_rope(p, ta + 128 * hh, m, nb * (BN / 128) + hh);
         } else {
-          epi_store<BN>(p, ta, m, nb * BN);
+          if (p.epi == kF32Owner)
+            epi_store_owner<BN>(p, ta, m - lane, nb * BN, s.ostage[quad]);
+          else
+            epi_store<BN>(p, ta, m, nb * BN);
         }
       }
       tc_fence_before();
       mbar_arrive(&s.acc_empty[buf]);
     }
+    // Partials stored to other GPUs are visible system-wide before the
+    // kernel ends; the exchange's next kernel publishes them with a flag.
+    if (p.epi == kF32Owner) __threadfence_system();
   }
 
   tc_fence_before();

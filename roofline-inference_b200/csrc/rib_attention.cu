@@ -16,6 +16,7 @@
 #include "gemm.cuh"
 #include "model_kernels.cuh"
 #include "qk_norm_rope.cuh"
+#include "tp_prefill.cuh"
 
 // Largest split of the decode kernel, in keys (a build-time tuning constant).
 #ifndef RIB_DECODE_MAX_CHUNK
@@ -985,6 +986,81 @@ int rib_argmax_f32_tp(const float *x, int n, int index_offset, int32_t *out, voi
   const int grid = std::max(1, std::min(ceil_div(n, 1024 * 4), sm_count()));
   return launch_pdl("argmax_tp_kernel launch", rib::model::argmax_tp_kernel, dim3(grid), dim3(1024), 0, st, x,
                     n, index_offset, static_cast<rib::model::ArgmaxWs *>(workspace), out, d);
+}
+
+// ------------------------------------------------------------------ tensor-parallel prefill exchange
+size_t rib_tp_prefill_buffer_bytes(int world, int rows_cap, int hidden) {
+  if (world < 1 || world > RIB_TP_MAX_RANKS || rows_cap < 1 || hidden < 256 || hidden > 2048 || hidden % 256 ||
+      (hidden / 256) & (hidden / 256 - 1))
+    return 0;
+  return round256(rib::tpp::buffer_bytes(world, rows_cap, hidden));
+}
+
+// Checks a rib_tp_prefill_exchange against M rows.
+static int tpp_check(const rib_tp_prefill_exchange *ex, int M) {
+  if (!ex || rib_tp_prefill_buffer_bytes(ex->world, ex->rows_cap, ex->hidden) == 0 || ex->rank < 0 ||
+      ex->rank >= ex->world || M < 1 || M > ex->rows_cap)
+    return RIB_EINVAL;
+  for (int q = 0; q < ex->world; ++q) {
+    if (!ex->buf[q]) return RIB_EINVAL;
+    if (ex->buf[q] & 255u) return RIB_EALIGN;
+  }
+  return RIB_OK;
+}
+
+int rib_gemm_tp_partial(const void *A, int M, int K, const void *W, const rib_tp_prefill_exchange *ex,
+                        void *stream) {
+  using namespace rib::gemm;
+  const int st = tpp_check(ex, M);
+  if (st != RIB_OK) return st;
+  Params p = {};
+  const int H = ex->hidden;
+  p.ldc = H;
+  p.rpo = rib::tpp::rows_per_owner(M, ex->world);
+  p.rank = ex->rank;
+  p.slot_floats = static_cast<long long>(rib::tpp::rows_per_owner(ex->rows_cap, ex->world)) * H;
+  for (int q = 0; q < ex->world; ++q)
+    p.owner_recv[q] = reinterpret_cast<float *>(ex->buf[q] + rib::tpp::kRecvOffset);
+  return gemm_run(A, M, K, W, H, kF32Owner, 256, p, stream);
+}
+
+int rib_tp_reduce_add_rms(const rib_tp_prefill_exchange *ex, int M, unsigned long long epoch, void *residual,
+                          const void *norm_w, void *out, void *stream) {
+  using namespace rib::tpp;
+  const int st = tpp_check(ex, M);
+  if (st != RIB_OK) return st;
+  if (!residual || epoch == 0 || (norm_w && !out)) return RIB_EINVAL;
+  if (!aligned16(residual) || (norm_w && (!aligned16(norm_w) || !aligned16(out)))) return RIB_EALIGN;
+  if (!bind_stream_device(stream)) return rib::host_fail(RIB_ECUDA, "bind stream device", 0);
+  ReduceParams p = {};
+  const int H = ex->hidden;
+  const size_t goff = gather_offset(ex->world, ex->rows_cap, H);
+  for (int q = 0; q < ex->world; ++q) {
+    p.flags[q] = reinterpret_cast<unsigned long long *>(ex->buf[q] + kFlagsOffset);
+    p.gather[q] = reinterpret_cast<uint16_t *>(ex->buf[q] + goff);
+  }
+  const uintptr_t own = static_cast<uintptr_t>(ex->buf[ex->rank]);
+  p.recv = reinterpret_cast<const float *>(own + kRecvOffset);
+  p.counter = reinterpret_cast<int *>(own + kCounterOffset);
+  p.epoch = epoch;
+  p.slot_floats = static_cast<long long>(rows_per_owner(ex->rows_cap, ex->world)) * H;
+  p.world = ex->world;
+  p.rank = ex->rank;
+  p.M = M;
+  p.H = H;
+  p.rpo = rows_per_owner(M, ex->world);
+  p.residual = static_cast<uint16_t *>(residual);
+  p.w = static_cast<const uint16_t *>(norm_w);
+  p.out = static_cast<uint16_t *>(out);
+  // at most one CTA per SM, so every CTA of the grid is resident while they wait for one another
+  const dim3 grid(std::max(1, std::min(ceil_div(M, kThreads / 32), sm_count()))), block(kThreads);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (H) {
+    case 256: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<1>, grid, block, 0, s, p);
+    case 512: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<2>, grid, block, 0, s, p);
+    case 1024: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<4>, grid, block, 0, s, p);
+    default: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<8>, grid, block, 0, s, p);
+  }
 }
 
 // add_rms / rms_norm launch: warp per row for the common widths, else CTA per row.

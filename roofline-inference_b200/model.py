@@ -151,7 +151,9 @@ class Engine:
     of the gate/up rows and down columns and a slice of the LM-head rows;
     attention outputs stay local, and the O / down partial sums and the argmax
     keys are exchanged over NVLink inside the GEMV and argmax kernels (prefill:
-    NCCL all-reduce of FP32 partials)."""
+    the tcgen05 GEMM stores each row's FP32 partial to its owner rank, which
+    reduces it and stores the BF16 row to every rank before the residual add
+    and RMSNorm; tp.PrefillExchange)."""
 
     def __init__(self, weights: Qwen3Weights, *, shard: bool = False, tp: bool = False, group=None):
         cfg = weights.config
@@ -172,6 +174,7 @@ class Engine:
         self.gather = None
         self.tp = bool(tp)
         self.tpx = None
+        self.tpp = None          # tensor-parallel prefill exchange, made by the first prefill
         if shard or tp:
             import torch.distributed as dist
             from .nvlink_gather import NVLinkGather
@@ -212,6 +215,9 @@ class Engine:
         if self.tpx is not None:
             self.tpx.close()
             self.tpx = None
+        if self.tpp is not None:
+            self.tpp.close()
+            self.tpp = None
 
     def _attend_one(self, q, cache_layer, n: int, out=None):
         """Decode attention of one query row over n keys: [1, nq_local, 128] in,
@@ -229,11 +235,21 @@ class Engine:
         return self.gather.decode_into(q.reshape(1, self.nq_local, HEAD_DIM).contiguous(), ptrs, lens, n,
                                        cache_layer.shape[2], self.scale, ws, self.epoch_dev, out)
 
-    def _all_reduce_bf16(self, part):
-        """Sum of the ranks' FP32 partials [n, hidden] (NCCL), rounded once to BF16."""
-        import torch.distributed as dist
-        dist.all_reduce(part, group=self.group)
-        return part.to(torch.bfloat16)
+    def _prefill_exchange(self, rows: int):
+        """The tensor-parallel prefill exchange, holding at least `rows` rows
+        (collective: every rank prefills the same chunk lengths)."""
+        if self.tpp is None or self.tpp.rows_cap < rows:
+            from .tp import PrefillExchange
+            if self.tpp is not None:
+                self.tpp.close()
+            self.tpp = PrefillExchange(self.cfg.hidden_size, max(rows, 4096), self.device, self.group)
+        return self.tpp
+
+    def _tp_add_rms(self, x, W, h, norm_w):
+        """Under tensor parallelism: h <- bf16(h + bf16(sum over ranks of x W^T))
+        in place over NVLink (tp.PrefillExchange); returns (h, RMSNorm(h) * norm_w),
+        the second None when norm_w is None."""
+        return self._prefill_exchange(x.shape[0]).project_add_rms(x.contiguous(), W, h, norm_w)
 
     def _gather_vocab(self, local):
         """[..., V/N] FP32 logit slices of every rank -> [..., V] (NCCL all-gather)."""
@@ -241,13 +257,6 @@ class Engine:
         parts = [torch.empty_like(local) for _ in range(self.world)]
         dist.all_gather(parts, local.contiguous(), group=self.group)
         return torch.cat(parts, dim=-1)
-
-    def _proj_out(self, x, W):
-        """Row-parallel projection: the full output under tensor parallelism
-        (FP32 partials summed over ranks), else a plain BF16 GEMM."""
-        if self.tp:
-            return self._all_reduce_bf16(_linear(x, W, "f32"))
-        return _linear(x, W)
 
     def _gather_rows(self, o_local):
         """[n, nq_local * 128] per rank -> [n, n_heads * 128] (NCCL all-gather)."""
@@ -291,12 +300,17 @@ class Engine:
                 kvl = cache.kv[i]
                 o = attention(q, kvl[0], kvl[1], n, off + n, self.scale)       # [n, nq_local*128]
                 o = o if self.tp else self._gather_rows(o)                     # [n, H*128]
-            h, x = add_rms(h, self._proj_out(o, w["o"]), w["post_norm"])
-            r = self._proj_out(_linear(x, w["gu"], "swiglu"), w["down"])
+            nxt = None if final else self.layers[i + 1]["in_norm"]
+            if self.tp:  # row-parallel O and down: partial sums exchanged over NVLink
+                h, x = self._tp_add_rms(o, w["o"], h.contiguous(), w["post_norm"])
+                h, x = self._tp_add_rms(_linear(x, w["gu"], "swiglu"), w["down"], h, nxt)
+                continue
+            h, x = add_rms(h, _linear(o, w["o"]), w["post_norm"])
+            r = _linear(_linear(x, w["gu"], "swiglu"), w["down"])
             if final:
                 h = h + r
             else:
-                h, x = add_rms(h, r, self.layers[i + 1]["in_norm"])
+                h, x = add_rms(h, r, nxt)
         cache.offset += n
         if not last:
             return None

@@ -42,6 +42,12 @@ class _TpExchangeStruct(ctypes.Structure):
                 ("done", ctypes.c_uint64), ("slot", ctypes.c_int)]
 
 
+class _PrefillExchangeStruct(ctypes.Structure):
+    """rib_tp_prefill_exchange (include/rib_attention.h)."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("buf", ctypes.c_uint64 * MAX_RANKS), ("rows_cap", ctypes.c_int), ("hidden", ctypes.c_int)]
+
+
 def _bind(L: ctypes.CDLL) -> None:
     vp, i, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
     L.rib_tp_buffer_bytes.argtypes = [i, i]
@@ -50,6 +56,13 @@ def _bind(L: ctypes.CDLL) -> None:
     L.rib_gemv_tp.restype = i
     L.rib_argmax_f32_tp.argtypes = [vp, i, i, vp, vp, ctypes.POINTER(_TpExchangeStruct), vp]
     L.rib_argmax_f32_tp.restype = i
+    L.rib_tp_prefill_buffer_bytes.argtypes = [i, i, i]
+    L.rib_tp_prefill_buffer_bytes.restype = sz
+    L.rib_gemm_tp_partial.argtypes = [vp, i, i, vp, ctypes.POINTER(_PrefillExchangeStruct), vp]
+    L.rib_gemm_tp_partial.restype = i
+    L.rib_tp_reduce_add_rms.argtypes = [ctypes.POINTER(_PrefillExchangeStruct), i, ctypes.c_ulonglong, vp, vp, vp,
+                                        vp]
+    L.rib_tp_reduce_add_rms.restype = i
 
 
 def split_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -127,6 +140,75 @@ class TPExchange:
                                             workspace.data_ptr(), ctypes.byref(self.struct),
                                             stream_handle(self.device)), "argmax_f32_tp")
         return out
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        if self.closed:
+            return
+        self.peers.close()
+        self.closed = True
+
+
+class PrefillExchange:
+    """The exchange after the row-parallel O and down projections of a
+    tensor-parallel prefill (the add_rms after each projection of
+    Engine.prefill, agent-test/v2/engine.py:111-116), fused over NVLink in
+    place of an NCCL all-reduce.  rib_gemm_tp_partial stores each row's FP32
+    partial into the owner rank's receive slot (rows split over the ranks in
+    contiguous runs); rib_tp_reduce_add_rms sums each owned row in rank
+    order, rounds it to BF16, stores it into every rank's gather buffer and
+    then applies residual add + RMSNorm to all rows on every rank.
+
+    rows_cap: the most rows one call may carry.  Setup and close() are
+    collective, and every rank makes the same calls in the same order."""
+
+    def __init__(self, hidden: int, rows_cap: int, device, group=None):
+        self.L = L = _lib.load()
+        _bind(L)
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > MAX_RANKS:
+            raise ValueError(f"at most {MAX_RANKS} ranks")
+        self.device = torch.device(device)
+        self.hidden, self.rows_cap = int(hidden), int(rows_cap)
+        nbytes = int(L.rib_tp_prefill_buffer_bytes(self.world, self.rows_cap, self.hidden))
+        if nbytes == 0:
+            raise ValueError(f"unsupported prefill exchange geometry (hidden {hidden}, rows {rows_cap})")
+        self.peers = PeerBuffers(nbytes, self.device, group)
+        s = _PrefillExchangeStruct()
+        s.world, s.rank, s.rows_cap, s.hidden = self.world, self.rank, self.rows_cap, self.hidden
+        for r in range(self.world):
+            s.buf[r] = self.peers.base[r]
+        self.struct = s
+        self.epoch = 0
+        self.closed = False
+
+    def project_add_rms(self, x, W, residual, norm_w=None, out=None):
+        """residual <- bf16(residual + bf16(sum over ranks of x W^T)), in place;
+        with norm_w, out <- its RMSNorm (allocated when None).  x [M, K] BF16
+        (this rank's columns of the projection's input), W [hidden, K] BF16,
+        residual [M, hidden] BF16.  Returns (residual, out)."""
+        from ._tensors import stream_handle
+        if self.closed:
+            raise RuntimeError("PrefillExchange is closed")
+        M, K = x.shape
+        if W.shape != (self.hidden, K) or residual.shape != (M, self.hidden) or M > self.rows_cap:
+            raise ValueError(f"shapes x {tuple(x.shape)}, W {tuple(W.shape)}, residual "
+                             f"{tuple(residual.shape)} do not fit the exchange (hidden {self.hidden}, "
+                             f"rows {self.rows_cap})")
+        for t in (x, W, residual):
+            if not (t.is_contiguous() and t.dtype == torch.bfloat16 and t.device == self.device):
+                raise ValueError("x, W and residual must be contiguous BF16 tensors on the exchange's device")
+        if norm_w is not None and out is None:
+            out = torch.empty_like(residual)
+        st = stream_handle(self.device)
+        self.epoch += 1
+        _lib.check(self.L.rib_gemm_tp_partial(x.data_ptr(), M, K, W.data_ptr(), ctypes.byref(self.struct), st),
+                   "gemm_tp_partial")
+        _lib.check(self.L.rib_tp_reduce_add_rms(
+            ctypes.byref(self.struct), M, self.epoch, residual.data_ptr(),
+            None if norm_w is None else norm_w.data_ptr(), None if out is None else out.data_ptr(), st),
+            "tp_reduce_add_rms")
+        return residual, out
 
     def close(self) -> None:
         """Collective: unmap the peers' buffers and free this rank's."""

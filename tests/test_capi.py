@@ -165,3 +165,45 @@ def test_wait_limit_range_checked_on_host(rib):
     assert L.rib_set_wait_limit_ns(10) == 1
     assert L.rib_set_wait_limit_ns(61_000_000_000) == 1
     assert L.rib_get_wait_limit_ns(None) == 1
+
+
+def test_tp_prefill_exchange_rejects_bad_arguments(rib):
+    """rib_tp_prefill_buffer_bytes / rib_gemm_tp_partial /
+    rib_tp_reduce_add_rms: the buffer layout (flags, receive slots of
+    ceil(rows / world) rows per source, BF16 gather rows) and the host-side
+    checks, before any launch."""
+    import importlib
+    T = importlib.import_module("roofline-inference_b200.tp")
+    L = rib.load_library()
+    T._bind(L)
+    H, rows, world = 1024, 4096, 2
+    nbytes = int(L.rib_tp_prefill_buffer_bytes(world, rows, H))
+    recv = world * ((rows + world - 1) // world) * H * 4
+    assert nbytes == (256 + recv + 255) // 256 * 256 + rows * H * 2
+    assert L.rib_tp_prefill_buffer_bytes(3, 37, 256) == (256 + 3 * 13 * 256 * 4 + 255) // 256 * 256 + 37 * 256 * 2
+    for bad in [(0, rows, H), (9, rows, H), (world, 0, H), (world, rows, 768), (world, rows, 128),
+                (world, rows, 4096)]:
+        assert L.rib_tp_prefill_buffer_bytes(*bad) == 0, bad
+
+    def ex(world=2, rank=0, rows_cap=rows, hidden=H, bufs=(FAKE * 16, FAKE * 32)):
+        s = T._PrefillExchangeStruct()
+        s.world, s.rank, s.rows_cap, s.hidden = world, rank, rows_cap, hidden
+        for r, b in enumerate(bufs):
+            s.buf[r] = b
+        return ctypes.byref(s)
+
+    assert L.rib_gemm_tp_partial(FAKE, rows + 1, 1024, FAKE, ex(), None) == 1       # more rows than the buffers
+    assert L.rib_gemm_tp_partial(FAKE, 0, 1024, FAKE, ex(), None) == 1
+    assert L.rib_gemm_tp_partial(FAKE, 64, 1024, FAKE, ex(rank=2), None) == 1
+    assert L.rib_gemm_tp_partial(FAKE, 64, 1024, FAKE, ex(bufs=(FAKE * 16, 0)), None) == 1
+    assert L.rib_gemm_tp_partial(FAKE, 64, 1024, FAKE, ex(bufs=(FAKE * 16, FAKE * 16 + 128)), None) == 3
+    assert L.rib_gemm_tp_partial(FAKE, 64, 1024, FAKE, ex(hidden=768), None) == 1
+    assert L.rib_gemm_tp_partial(FAKE, 64, 96, FAKE, ex(), None) == 1              # K not a multiple of 64
+    assert L.rib_gemm_tp_partial(MISALIGNED, 64, 1024, FAKE, ex(), None) == 3
+    assert L.rib_gemm_tp_partial(FAKE, 64, 1024, FAKE, None, None) == 1
+    assert L.rib_tp_reduce_add_rms(ex(), 64, 0, FAKE, FAKE, FAKE, None) == 1          # epoch 0 is never valid
+    assert L.rib_tp_reduce_add_rms(ex(), 64, 1, None, FAKE, FAKE, None) == 1
+    assert L.rib_tp_reduce_add_rms(ex(), 64, 1, FAKE, FAKE, None, None) == 1          # a norm needs an output
+    assert L.rib_tp_reduce_add_rms(ex(), rows + 1, 1, FAKE, None, None, None) == 1
+    assert L.rib_tp_reduce_add_rms(ex(), 64, 1, MISALIGNED, None, None, None) == 3
+    assert L.rib_tp_reduce_add_rms(ex(), 64, 1, FAKE, FAKE, MISALIGNED, None) == 3

@@ -130,3 +130,50 @@ def test_tensor_parallel_partial_wait_times_out(lib, rib, wl):
     want = model_np.gemv(u16(W), u16(x))
     assert np.abs(bf16f(got) - bf16f(want)).max() <= np.abs(bf16f(want)).max() * 2.0 ** -7
     assert lib.take_device_status() == 0
+
+
+def test_tp_prefill_exchange_wait_times_out(lib, rib, wl):
+    """The tensor-parallel prefill exchange with world = 2, where "rank 1" is
+    a second buffer in this GPU's memory that no kernel signals: the owner-slot
+    GEMM stores its partials, the reduce kernel publishes this rank's signal
+    to both buffers and its wait for rank 1's runs out; the residual is left
+    untouched, and the next exchange on fresh buffers is correct."""
+    tp = importlib.import_module("roofline-inference_b200.tp")
+    from oracle import model_np
+    L = lib.load()
+    tp._bind(L)
+    M, K, H = 64, 256, 256
+    nb = int(L.rib_tp_prefill_buffer_bytes(2, M, H))
+    bufs = [torch.zeros(nb, dtype=torch.uint8, device="cuda") for _ in range(2)]
+    ex = tp._PrefillExchangeStruct()
+    ex.world, ex.rank, ex.rows_cap, ex.hidden = 2, 0, M, H
+    ex.buf[0], ex.buf[1] = bufs[0].data_ptr(), bufs[1].data_ptr()
+    A = wl.randn_bf16((M, K), seed=21, device="cuda")
+    W = wl.randn_bf16((H, K), seed=22, device="cuda", scale=K ** -0.5)
+    h = wl.randn_bf16((M, H), seed=23, device="cuda")
+    h_before = h.clone()
+    st = torch.cuda.current_stream().cuda_stream
+    lib.set_wait_limit_ns(LIMIT_NS)
+    t0 = time.perf_counter()
+    assert L.rib_gemm_tp_partial(A.data_ptr(), M, K, W.data_ptr(), ctypes.byref(ex), st) == 0
+    assert L.rib_tp_reduce_add_rms(ctypes.byref(ex), M, 1, h.data_ptr(), None, None, st) == 0
+    status = lib.take_device_status()
+    elapsed = time.perf_counter() - t0
+    assert status == lib.RIB_ETIMEOUT, status
+    assert elapsed < 1.5, elapsed
+    assert torch.equal(h, h_before)
+    f0, f1 = bufs[0][:128].view(torch.int64).cpu(), bufs[1][:128].view(torch.int64).cpu()
+    assert int(f0[0]) == 1 and int(f1[0]) == 1       # rank 0's "partials in place" reached both
+    assert int(f0[1]) == 0 and int(f0[8]) == 0       # nothing from rank 1; no "rows in place"
+    lib.set_wait_limit_ns(lib.DEFAULT_WAIT_LIMIT_NS)
+    one = torch.zeros(int(L.rib_tp_prefill_buffer_bytes(1, M, H)), dtype=torch.uint8, device="cuda")
+    ex1 = tp._PrefillExchangeStruct()
+    ex1.world, ex1.rank, ex1.rows_cap, ex1.hidden = 1, 0, M, H
+    ex1.buf[0] = one.data_ptr()
+    assert L.rib_gemm_tp_partial(A.data_ptr(), M, K, W.data_ptr(), ctypes.byref(ex1), st) == 0
+    assert L.rib_tp_reduce_add_rms(ctypes.byref(ex1), M, 1, h.data_ptr(), None, None, st) == 0
+    torch.cuda.synchronize()
+    r = model_np.matmul(u16(A), u16(W))
+    want = model_np.add_rms(u16(h_before), r, np.full(H, 0x3F80, np.uint16))[0]  # the residual bf16(h + r)
+    assert np.abs(bf16f(h) - bf16f(want)).max() <= np.abs(bf16f(want)).max() * 2.0 ** -7
+    assert lib.take_device_status() == 0

@@ -224,3 +224,67 @@ def test_tp_engine_two_gpus():
         assert graph == eager, (r, graph, eager)
         assert margin <= 1e-2, (r, margin)
     assert res[0][0] == res[1][0]
+
+
+# ------------------------------------------------------------------ tensor-parallel prefill exchange
+def _tpp_worker(rank, world, port, q_out):
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        torch.distributed.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                             timeout=datetime.timedelta(seconds=60))
+        sys.path.insert(0, str(ROOT / "tests"))
+        from test_gpu_tp_prefill import close_bf16, expected
+        wl = importlib.import_module("roofline-inference_b200.workloads")
+        T = importlib.import_module("roofline-inference_b200.tp")
+        u16 = lambda t: t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        H, K = 1024, 1024                      # K: this rank's columns of a 2048-wide input
+        ex = T.PrefillExchange(H, 4096, dev)
+        results = []
+        # ragged and full row counts, with and without the norm, on the same buffers (epochs 1-4)
+        for call, (M, norm) in enumerate([(4096, True), (37, True), (1, False), (1000, True)]):
+            As = [wl.randn_bf16((M, K), seed=1000 * call + r) for r in range(world)]
+            Ws = [wl.randn_bf16((H, K), seed=1000 * call + 100 + r, scale=(K * world) ** -0.5) for r in range(world)]
+            h = wl.randn_bf16((M, H), seed=1000 * call + 500)
+            nw = (wl.randn_bf16((H,), seed=1000 * call + 600, scale=0.1) + 1.0).to(torch.bfloat16) if norm else None
+            hd = h.to(dev)
+            _, x = ex.project_add_rms(As[rank].to(dev), Ws[rank].to(dev), hd, None if nw is None else nw.to(dev))
+            torch.cuda.synchronize(dev)
+            res, xr = expected([(u16(a), u16(w)) for a, w in zip(As, Ws)], u16(h), None if nw is None else u16(nw))
+            close_bf16(hd, res, f"call {call} residual")
+            if norm:
+                close_bf16(x, xr, f"call {call} normalised")
+            results.append((u16(hd), None if x is None else u16(x)))
+        status = importlib.import_module("roofline-inference_b200._lib").take_device_status()
+        ex.close()
+        torch.distributed.destroy_process_group()
+        q_out.put((rank, (results, status)))
+    except Exception as e:  # report to the parent
+        q_out.put((rank, repr(e)))
+
+
+def test_tp_prefill_exchange_two_gpus():
+    """The tensor-parallel prefill exchange on 2 GPUs: each rank's owner-slot
+    GEMM partials and the reduce kernel's NVLink row stores give, on both
+    ranks, the oracle's residual add + RMSNorm of the rank-order sum, and the
+    two ranks' results are bit-identical."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_tpp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, v in res.items():
+        assert not isinstance(v, str), f"rank {r}: {v}"
+        assert v[1] == 0, f"rank {r}: device status {v[1]}"
+    for (h0, x0), (h1, x1) in zip(res[0][0], res[1][0]):
+        assert np.array_equal(h0, h1)
+        assert (x0 is None and x1 is None) or np.array_equal(x0, x1)
