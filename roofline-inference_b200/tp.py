@@ -19,7 +19,15 @@ The single-GPU reference runs every GEMV of a decode step on one device
     every rank gets the same token.
 
 Per layer each rank reads 1/N of the projection weights, at the price of two
-cross-GPU exchanges (a few KB each).  Setup and close() are collective.
+cross-GPU exchanges (a few KB each).
+
+A prefill's O and down projections are GEMMs over M prompt rows; their
+exchange (PrefillExchange) splits the rows over the ranks: the tcgen05 GEMM's
+epilogue stores each row's FP32 partial into its owner rank's receive slot
+over NVLink, and one kernel then sums each owned row in rank order, stores the
+BF16 row into every rank's gather buffer and applies the residual add and
+RMSNorm to all rows -- a reduce-scatter and an all-gather fused into the
+GEMM and the add_rms, with no NCCL call.  Setup and close() are collective.
 """
 from __future__ import annotations
 
