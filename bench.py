@@ -1288,7 +1288,11 @@ def run_case(case: str):
     model-prefill is three 4096-token prefills of Qwen3-0.6B (last row's
     logits), the TTFT path of the request benchmark; gemm is one launch of
     each Qwen3 prefill projection at 4096 tokens (O, gate/up + SwiGLU, down,
-    QKV + norm + RoPE + append)."""
+    QKV + norm + RoPE + append); tp-exchange is the tensor-parallel prefill
+    exchange of one rank (M = 32768 rows, K = 1024, hidden 1024: 128 MB of
+    FP32 partials, above L2): three pairs of the owner-slot GEMM and the
+    reduce + gather + add_rms kernel, each followed by the plain FP32 GEMM of
+    the same shape."""
     rib = load_rib()
     wl = importlib.import_module("roofline-inference_b200.workloads")
     device = torch.device("cuda", 0)
@@ -1331,6 +1335,20 @@ def run_case(case: str):
         qw, kw = wl.norm_weights(1, device), wl.norm_weights(2, device)
         cache = torch.zeros((2, 8, M, 128), dtype=torch.bfloat16, device=device)
         G.gemm_qkv_rope(x, W, qw, kw, G.rope_table(0, M, 1e6, device), 0, 16, 8, cache, M)
+    elif case == "tp-exchange":
+        G = importlib.import_module("roofline-inference_b200.gemm")
+        T = importlib.import_module("roofline-inference_b200.tp")
+        M, K, H = 32768, 1024, 1024
+        ex = T.PrefillExchange(H, M, device, local=True)
+        A = wl.randn_bf16((M, K), seed=91, device=device)
+        W = wl.randn_bf16((H, K), seed=92, device=device, scale=K ** -0.5)
+        h = wl.randn_bf16((M, H), seed=93, device=device)
+        nw = (1.0 + 0.1 * wl.randn_bf16((H,), seed=94, device=device).float()).to(torch.bfloat16)
+        out = torch.empty_like(h)
+        for _ in range(3):
+            ex.project_add_rms(A, W, h, nw, out)
+            G.gemm(A, W, epi="f32", small=False)
+        ex.close()
     elif case == "model-batch":
         eng = rib.Engine(rib.random_weights(rib.QWEN3_0_6B, seed=11, device=device))
         _, dec = batch_workload(eng, device, 8)
@@ -1359,7 +1377,7 @@ def main():
     ap.add_argument("--no-model", action="store_true", help="skip the full Qwen3-0.6B forward")
     ap.add_argument("--case", choices=["decode-small", "decode-4k", "decode-28", "prefill-small", "prefill-32k",
                                        "model-decode",
-                                       "model-prefill", "gemm",
+                                       "model-prefill", "gemm", "tp-exchange",
                              "model-batch"], default=None,
                     help="run a bounded case for profiling (ncu) and exit")
     args = ap.parse_args()

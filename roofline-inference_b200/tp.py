@@ -168,12 +168,18 @@ class PrefillExchange:
     then applies residual add + RMSNorm to all rows on every rank.
 
     rows_cap: the most rows one call may carry.  Setup and close() are
-    collective, and every rank makes the same calls in the same order."""
+    collective, and every rank makes the same calls in the same order.
+    local=True makes a one-rank exchange over a plain device buffer, with no
+    process group: every row is this rank's own and every signal its own
+    (the two kernels alone, for tests and profiling)."""
 
-    def __init__(self, hidden: int, rows_cap: int, device, group=None):
+    def __init__(self, hidden: int, rows_cap: int, device, group=None, *, local: bool = False):
         self.L = L = _lib.load()
         _bind(L)
-        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if local:
+            self.world, self.rank = 1, 0
+        else:
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         if self.world > MAX_RANKS:
             raise ValueError(f"at most {MAX_RANKS} ranks")
         self.device = torch.device(device)
@@ -181,11 +187,17 @@ class PrefillExchange:
         nbytes = int(L.rib_tp_prefill_buffer_bytes(self.world, self.rows_cap, self.hidden))
         if nbytes == 0:
             raise ValueError(f"unsupported prefill exchange geometry (hidden {hidden}, rows {rows_cap})")
-        self.peers = PeerBuffers(nbytes, self.device, group)
+        self.peers, self._local = None, None
+        if local:
+            self._local = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            base = [self._local.data_ptr()]
+        else:
+            self.peers = PeerBuffers(nbytes, self.device, group)
+            base = self.peers.base
         s = _PrefillExchangeStruct()
         s.world, s.rank, s.rows_cap, s.hidden = self.world, self.rank, self.rows_cap, self.hidden
         for r in range(self.world):
-            s.buf[r] = self.peers.base[r]
+            s.buf[r] = base[r]
         self.struct = s
         self.epoch = 0
         self.closed = False
@@ -222,5 +234,7 @@ class PrefillExchange:
         """Collective: unmap the peers' buffers and free this rank's."""
         if self.closed:
             return
-        self.peers.close()
+        if self.peers is not None:
+            self.peers.close()
+        self._local = None
         self.closed = True

@@ -252,3 +252,14 @@ def test_fused_decode_wrapper_checks_shapes(rib):
     with pytest.raises(ValueError):
         rib.decode_attention_qkv(qkv, w, w, 1e6, torch.zeros((1, 2, 8, 256, 128), dtype=torch.bfloat16), [5],
                                  0.09)
+
+
+def test_local_prefill_exchange_checks_its_geometry():
+    """tp.PrefillExchange(local=True) needs no process group, and a geometry
+    the kernels do not take (hidden not 256/512/1024/2048, no rows) is refused
+    on the host before any buffer is made."""
+    import importlib
+    T = importlib.import_module("roofline-inference_b200.tp")
+    for hidden, rows in [(768, 4096), (4096, 4096), (1024, 0)]:
+        with pytest.raises(ValueError, match="unsupported prefill exchange geometry"):
+            T.PrefillExchange(hidden, rows, "cpu", local=True)
