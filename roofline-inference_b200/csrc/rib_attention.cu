@@ -1024,6 +1024,18 @@ int rib_gemm_tp_partial(const void *A, int M, int K, const void *W, const rib_tp
   return gemm_run(A, M, K, W, H, kF32Owner, 256, p, stream);
 }
 
+// At most one CTA per SM, so every CTA of the grid is resident while they
+// wait for one another.
+extern "C++" {
+template <int C>
+static int tpp_reduce_launch(const rib::tpp::ReduceParams &p, cudaStream_t s) {
+  constexpr int nt = rib::tpp::threads_for<C>();
+  const dim3 grid(std::max(1, std::min(ceil_div(p.M, nt / 32), sm_count())));
+  return launch_pdl("tp_reduce_add_rms_kernel launch", rib::tpp::tp_reduce_add_rms_kernel<C>, grid, dim3(nt), 0, s,
+                    p);
+}
+}
+
 int rib_tp_reduce_add_rms(const rib_tp_prefill_exchange *ex, int M, unsigned long long epoch, void *residual,
                           const void *norm_w, void *out, void *stream) {
   using namespace rib::tpp;
@@ -1052,14 +1064,12 @@ int rib_tp_reduce_add_rms(const rib_tp_prefill_exchange *ex, int M, unsigned lon
   p.residual = static_cast<uint16_t *>(residual);
   p.w = static_cast<const uint16_t *>(norm_w);
   p.out = static_cast<uint16_t *>(out);
-  // at most one CTA per SM, so every CTA of the grid is resident while they wait for one another
-  const dim3 grid(std::max(1, std::min(ceil_div(M, kThreads / 32), sm_count()))), block(kThreads);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (H) {
-    case 256: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<1>, grid, block, 0, s, p);
-    case 512: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<2>, grid, block, 0, s, p);
-    case 1024: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<4>, grid, block, 0, s, p);
-    default: return launch_pdl("tp_reduce_add_rms_kernel launch", tp_reduce_add_rms_kernel<8>, grid, block, 0, s, p);
+    case 256: return tpp_reduce_launch<1>(p, s);
+    case 512: return tpp_reduce_launch<2>(p, s);
+    case 1024: return tpp_reduce_launch<4>(p, s);
+    default: return tpp_reduce_launch<8>(p, s);
   }
 }
 

@@ -40,7 +40,10 @@ namespace rib {
 namespace tpp {
 
 constexpr int kMaxRanks = 8;
-constexpr int kThreads = 256;  // 8 warps, one row per warp at a time
+// Threads per CTA for H = 256 C: 16 warps (one row per warp at a time) up to
+// H = 1024, 8 at H = 2048, whose rows take twice the registers.
+template <int C>
+__host__ __device__ constexpr int threads_for() { return C <= 4 ? 512 : 256; }
 
 // Layout of one rank's exchange buffer (bytes from its base):
 //   [0, 128)          flags: u64 [2][8], [0][s] = source s's partials are in
@@ -100,12 +103,13 @@ __device__ __forceinline__ bool wait_all(const ReduceParams &p, int which, int *
 }
 
 template <int C>  // H = 256 C: lane l holds the 16-byte chunks l, l + 32, ... of a row
-__global__ void __launch_bounds__(kThreads) tp_reduce_add_rms_kernel(const __grid_constant__ ReduceParams p) {
+__global__ void __launch_bounds__(threads_for<C>()) tp_reduce_add_rms_kernel(const __grid_constant__ ReduceParams p) {
+  constexpr int kWarps = threads_for<C>() / 32;
   __shared__ int s_ok, s_last;
   pdl_launch_dependents();
   pdl_wait();  // this rank's GEMM (and its fences) are complete
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gw = blockIdx.x * (kThreads / 32) + warp, nw = gridDim.x * (kThreads / 32);
+  const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
 
   // ---- 1. partials in place everywhere
   if (blockIdx.x == 0 && threadIdx.x < p.world) {
