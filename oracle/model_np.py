@@ -73,6 +73,24 @@ def gemv(W, x, nw=None, res=None, swiglu_epi=False, out_float=False):
     return f32_to_bf16(acc)
 
 
+def row_parallel_add_rms(parts, h, w=None):
+    """A row-parallel projection over ranks followed by add_rms, as the
+    tensor-parallel prefill computes it: parts = [(x_r u16 [m, K_r],
+    W_r u16 [N, K_r])] in rank order; each rank's FP32 partial x_r W_r^T, the
+    partials added in rank order in FP32, rounded once to BF16 (r), then
+    residual = bf16(h + r) and, with the norm weight w, its RMSNorm -- the
+    add_rms after each projection of Engine.prefill (engine.py:129-134,
+    kernels.py:227-268).  Returns (residual, normalised or None) as u16."""
+    acc = None
+    for x, W in parts:
+        p = (_f(x) @ _f(W).T).astype(np.float32)
+        acc = p if acc is None else (acc + p).astype(np.float32)
+    r = f32_to_bf16(acc)
+    if w is None:
+        return f32_to_bf16(bf16_to_f32(np.asarray(h, np.uint16)) + bf16_to_f32(r)), None
+    return add_rms(h, r, w)
+
+
 def matmul(x, W) -> np.ndarray:
     """x u16 [m, K] @ W u16 [N, K]^T -> u16 [m, N] (a BF16 GEMM, FP32 accumulate)."""
     return f32_to_bf16((_f(x) @ _f(W).T).astype(np.float32))

@@ -25,18 +25,9 @@ pytestmark = pytest.mark.gpu
 
 
 def expected(parts_in, h, nw):
-    """Oracle: parts_in = [(A_r, W_r)] per rank (u16); h, nw u16.  Returns
-    (residual, normalised or None) as u16."""
-    from oracle import model_np as M
-    from oracle.reference_np import bf16_to_f32, f32_to_bf16
-    acc = None
-    for A, W in parts_in:
-        p = (M._f(A) @ M._f(W).T).astype(np.float32)
-        acc = p if acc is None else (acc + p).astype(np.float32)
-    r = f32_to_bf16(acc)
-    if nw is None:
-        return f32_to_bf16(bf16_to_f32(h) + bf16_to_f32(r)), None
-    return M.add_rms(h, r, nw)
+    """The oracle's row-parallel projection + add_rms (u16 in and out)."""
+    from oracle import model_np
+    return model_np.row_parallel_add_rms(parts_in, h, nw)
 
 
 def close_bf16(got, want, what):

@@ -263,3 +263,30 @@ def test_local_prefill_exchange_checks_its_geometry():
     for hidden, rows in [(768, 4096), (4096, 4096), (1024, 0)]:
         with pytest.raises(ValueError, match="unsupported prefill exchange geometry"):
             T.PrefillExchange(hidden, rows, "cpu", local=True)
+
+
+def test_row_parallel_oracle_matches_the_unsplit_projection():
+    """The oracle of the tensor-parallel prefill exchange: splitting K over 1,
+    2 or 4 ranks and adding the FP32 partials in rank order gives the unsplit
+    projection's BF16 residual add and RMSNorm up to one BF16 step (the FP32
+    sums differ only in order)."""
+    from oracle import model_np
+    from oracle.reference_np import bf16_to_f32, f32_to_bf16
+    rng = np.random.default_rng(3)
+    m, K, N = 7, 512, 256
+    x = f32_to_bf16(rng.standard_normal((m, K)).astype(np.float32))
+    W = f32_to_bf16((rng.standard_normal((N, K)) * K ** -0.5).astype(np.float32))
+    h = f32_to_bf16(rng.standard_normal((m, N)).astype(np.float32))
+    w = f32_to_bf16((1.0 + 0.1 * rng.standard_normal(N)).astype(np.float32))
+    full_res, full_x = model_np.add_rms(h, model_np.matmul(x, W), w)
+    for world in (1, 2, 4):
+        k = K // world
+        parts = [(x[:, r * k:(r + 1) * k], W[:, r * k:(r + 1) * k]) for r in range(world)]
+        res, xn = model_np.row_parallel_add_rms(parts, h, w)
+        for got, want in ((res, full_res), (xn, full_x)):
+            g, f = bf16_to_f32(got).astype(np.float64), bf16_to_f32(want).astype(np.float64)
+            assert np.all(np.abs(g - f) <= 2.0 ** -6 * np.abs(f) + 2.0 ** -7 * np.abs(f).max(-1, keepdims=True))
+        if world == 1:
+            assert np.array_equal(res, full_res) and np.array_equal(xn, full_x)
+        res_only, none = model_np.row_parallel_add_rms(parts, h)
+        assert none is None and np.array_equal(res_only, res)
