@@ -1074,7 +1074,8 @@ def run_full_model(rib, rank, world, device, args, tp: bool = False):
     heads, the decode kernel gathers every head's output over NVLink, the
     rest of the layer runs on every rank); times are the max over ranks.
     With tp the projections are split too (Engine(tp=True): O / down partial
-    sums and the argmax keys exchanged over NVLink inside the GEMV kernels).
+    sums and the argmax keys exchanged over NVLink inside the GEMV kernels;
+    in prefill inside the tcgen05 GEMM's epilogue and the add_rms kernel).
     Each figure is reported against the full-model Level-A line (cold start)."""
     rl = importlib.import_module("roofline-inference_b200.roofline_line")
     cfg = rib.QWEN3_0_6B
@@ -1169,6 +1170,11 @@ def run_full_model(rib, rank, world, device, args, tp: bool = False):
         "total_ms": t_tot * 1e3,
         "reference_line": {"ttft_ms": rline["ttft_s"] * 1e3, "total_ms": rline["total_s"] * 1e3},
         "fraction_ttft": rline["ttft_s"] / t_ttft, "fraction_total": rline["total_s"] / t_tot}
+    if world > 1:
+        out["request"]["prefill_exchange"] = (
+            "O / down row partials stored by the tcgen05 GEMM's epilogue into their owner rank's buffer over "
+            "NVLink; one kernel reduces, stores the BF16 rows into every rank and applies add_rms (no NCCL)"
+            if tp else "attention outputs all-gathered with NCCL (all_gather_into_tensor)")
     if world == 1 and not tp:
         out["batched_decode"] = run_model_batch(rib, eng, device, args)
         out["serving"] = run_serving(rib, eng, device)
